@@ -1,0 +1,341 @@
+#!/usr/bin/env python
+"""Benchmark: wavefront decode attention, BASELINE config 2, on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wfd|reference]
+
+One step = one wavefront decode tick of the isolated attention op: B=8
+sequences x R=8 loop-depth slots, Hq=16 / Hkv=4 (GQA 4:1), Dh=128, bf16; slot r
+holds L_r = 4096 - r positions and gets one query (the new row is appended and
+attended in the same launch).  Q, K, V ~ N(0,1) from torch CPU seed 1 (draw
+order q, K, V), synthetic.  The KV working set (537 MB) is larger than L2
+(126 MB), so no L2 flush is needed between steps.
+
+value : algorithmic KV-read GB/s with every input resident in HBM (one CUDA
+        graph per step: planner + decode kernel), max time over ranks.
+e2e   : the same metric through the public Python/C-ABI call with host buffers:
+        every step copies q, the new K/V rows and the item table from pinned
+        host memory and reads the output back.
+Multi-GPU (torchrun): every rank runs its own independent batch (weak scaling);
+the only collectives are the timing max and a final counter gather.
+--impl reference: the reference's CPU path (write_tokens + gather_pack + SDPA
+varlen loop, restated in oracle/cpu_path.py) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "WFD decode tokens/s/GPU; wavefront-attn KV read GB/s vs HBM peak"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+CFG2 = dict(B=8, R=8, H=16, Hkv=4, Dh=128, S=4096, seed=1)
+
+# DRAM traffic of the decode kernel per launch, from the ncu capture summarised
+# in profiles/wave_decode_cfg2.md (dram__bytes_read.sum + dram__bytes_write.sum).
+NCU_TRAFFIC_BYTES = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def cfg2_cpu_inputs(seed: int):
+    import torch
+    c = CFG2
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn((c["B"], c["R"], c["H"], c["Dh"]), generator=g).to(torch.bfloat16)
+    K = torch.randn((c["R"], c["B"], c["S"], c["Hkv"], c["Dh"]), generator=g).to(torch.bfloat16)
+    V = torch.randn((c["R"], c["B"], c["S"], c["Hkv"], c["Dh"]), generator=g).to(torch.bfloat16)
+    items = [[r, b, c["S"] - r - 1, 1, b * c["R"] + r] for b in range(c["B"]) for r in range(c["R"])]
+    q = q.reshape(c["B"] * c["R"], c["H"], c["Dh"])
+    kn = torch.stack([K[r, b, p] for r, b, p, _, _ in items])
+    vn = torch.stack([V[r, b, p] for r, b, p, _, _ in items])
+    return q, K, V, kn, vn, items
+
+
+def algorithmic_bytes(items, H, Hkv, Dh, elem=2):
+    kv = sum((p0 + ql) for _, _, p0, ql, _ in items) * Hkv * Dh * elem * 2   # every key row read once per kv head
+    rows = sum(it[3] for it in items)
+    qo = 2 * rows * H * Dh * elem                                             # q in, out
+    app = rows * Hkv * Dh * elem * 2                                          # appended K/V rows written
+    return kv + qo + app, rows
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in (out or "").splitlines() if ln.strip()]
+
+    def summary(self):
+        rows = []
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(f[1]), max=float(f[2]), power=float(f[3]), hw=f[5], hwt=f[6], swt=f[7],
+                                 pcap=f[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        reasons = set()
+        for r in rows:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                              ("pcap", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in rows), "sm_max_mhz": max(r["max"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": max(r["power"] for r in rows)}
+
+
+def cpu_baseline(q, K, V, kn, vn, items, budget_s: float, warmup: int = 1, steps: int | None = None):
+    """Time the reference's CPU path (oracle/cpu_path.py) on a bounded sample."""
+    import torch
+    from oracle import cpu_path
+    H, Dh = q.shape[1], q.shape[2]
+    Hkv = K.shape[3]
+    t0 = time.perf_counter()
+    cpu_path.wave_step(K, V, q, kn, vn, items)
+    first = time.perf_counter() - t0
+    sample = items
+    if first > 2.0:  # slow host: time a proportional subset of the rows
+        keep = max(1, int(len(items) * 2.0 / first))
+        sample = items[:keep]
+    for _ in range(max(0, warmup - 1)):
+        cpu_path.wave_step(K, V, q, kn, vn, sample)
+    n = steps if steps is not None else max(1, int(budget_s / max(first * len(sample) / len(items), 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        cpu_path.wave_step(K, V, q, kn, vn, sample)
+    dt = (time.perf_counter() - t0) / n
+    nbytes, rows = algorithmic_bytes(sample, H, Hkv, Dh)
+    return {"value": nbytes / dt / 1e9, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(sample)} of {len(items)} cfg2 decode rows per step (write_tokens + gather_pack + "
+                      f"SDPA varlen loop, bf16, torch CPU), {n} steps, {dt * 1e3:.1f} ms/step",
+            "ms_per_step": dt * 1e3, "host_cpu_count": os.cpu_count()}, n, dt
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    q, K, V, kn, vn, items = cfg2_cpu_inputs(CFG2["seed"])
+    base, n, dt = cpu_baseline(q, K, V, kn, vn, items, 0.0, warmup=max(1, args.warmup), steps=max(1, args.steps))
+    c = CFG2
+    line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
+            "steps": n, "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg2_wavefront_decode_attention", "batch": c["B"], "slots": c["R"],
+                       "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "4096-r",
+                       "l2": "KV working set 537 MB > 126 MB L2, no flush"},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_wfd(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from wavefront_decoding_b200 import attention as wa
+    from wavefront_decoding_b200 import runtime as rt
+
+    c = CFG2
+    q, K, V, kn, vn, items = cfg2_cpu_inputs(c["seed"] + rank)
+    nbytes, rows = algorithmic_bytes(items, c["H"], c["Hkv"], c["Dh"])
+    qd, Kd, Vd, knd, vnd = q.to(dev), K.to(dev), V.to(dev), kn.to(dev), vn.to(dev)
+    items_t = torch.tensor(items, dtype=torch.int32)
+    itd = items_t.to(dev)
+    lens = torch.zeros((c["R"], c["B"]), dtype=torch.int32, device=dev)
+    out = torch.empty_like(qd)
+    rt.reserve_workspace(dev, len(items), c["Dh"])
+    rt.error_word(dev)
+
+    def step():
+        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, 1, lens=lens, out=out)
+
+    # warm up eagerly, then capture one step
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    rt.read_device_error(dev)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            g.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    rt.read_device_error(dev)
+
+    # ---- e2e: public API call with host buffers every step ----
+    q_h, kn_h, vn_h = q.pin_memory(), kn.pin_memory(), vn.pin_memory()
+    it_h = items_t.pin_memory()
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = q_h.numel() * 2 + kn_h.numel() * 2 + vn_h.numel() * 2 + it_h.numel() * 4
+    d2h = out_h.numel() * 2
+
+    def e2e_step():
+        qd.copy_(q_h, non_blocking=True)
+        knd.copy_(kn_h, non_blocking=True)
+        vnd.copy_(vn_h, non_blocking=True)
+        itd.copy_(it_h, non_blocking=True)
+        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, 1, lens=lens, out=out)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    ev0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms_e2e = ev0.elapsed_time(ev1) / args.steps
+    rt.read_device_error(dev)
+
+    if world > 1:
+        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = t.tolist()
+        counters = torch.tensor([nbytes, rows], dtype=torch.float64, device=dev)
+        gathered = [torch.zeros_like(counters) for _ in range(world)]
+        dist.all_gather(gathered, counters)
+        total_bytes = sum(float(x[0]) for x in gathered)
+        total_rows = sum(float(x[1]) for x in gathered)
+    else:
+        total_bytes, total_rows = float(nbytes), float(rows)
+
+    value = total_bytes / (ms * 1e-3) / 1e9
+    value_e2e = total_bytes / (ms_e2e * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    achieved = nbytes / (ms * 1e-3) / 1e9    # per GPU, per launch of the step
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg2_wavefront_decode_attention", "batch_per_gpu": c["B"], "slots": c["R"],
+                       "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "4096-r",
+                       "rows_per_step_per_gpu": rows, "parallelism": f"sequences sharded, {world} rank(s)",
+                       "l2": "KV working set 537 MB > 126 MB L2, no flush", "timing": "CUDA graph replay"},
+            "wave_rows_per_s": total_rows / (ms * 1e-3),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC_BYTES,
+                         "algorithmic_bytes_per_launch": nbytes,
+                         "kernel": "wave_decode_kernel (+ plan_kernel, timed together)"},
+            "e2e": {"value": value_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        del g
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            base, _, _ = cpu_baseline(q, K, V, kn, vn, items, args.cpu_seconds)
+            line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        else:
+            line["cpu_baseline"] = None
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_wfd(args)
+
+
+if __name__ == "__main__":
+    main()

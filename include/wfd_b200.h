@@ -1,0 +1,194 @@
+/*
+ * wfd_b200.h — C ABI of the B200 wavefront-decoding attention / KV-slot library.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t (passed
+ * as void*), launches asynchronously on that stream and returns an int status
+ * (WFD_OK = 0).  Argument checks that need no device data are done on the host
+ * and reported as a status before anything launches.  Checks that need device
+ * data (slot ids, positions, cu_seqlens) are done inside the kernels, which skip
+ * the offending work item and OR an error bit into the caller's device error
+ * word `d_err` (int32, may be NULL); read it with wfd_read_error().  No kernel
+ * traps, asserts or waits without a bound.
+ *
+ * Layouts (row-major, contiguous, the reference's own layouts):
+ *   q, out            (n_rows, Hq, Dh)
+ *   k_new, v_new      (n_rows, Hkv, Dh)               new K/V rows, row i <-> q row i
+ *   k_cache, v_cache  (n_slots, n_seqs, max_seq, Hkv, Dh)
+ *                     == BatchStaticKVCache.K / .V, buffer index == absolute position
+ *                     (reference src/decoding/batch_kv_cache.py:28-44)
+ *   lens              (n_slots, n_seqs) int32, logical slot lengths
+ *                     == BatchStaticKVCache.seqlen (batch_kv_cache.py:44)
+ *   packed k, v       (total_k, Hkv, Dh) with cu_k (n_seg+1) int32,
+ *                     q (total_q, Hq, Dh) with cu_q (n_seg+1) int32
+ *                     (reference fa4_attention.py:294-317)
+ * dtype: WFD_DTYPE_BF16 or WFD_DTYPE_F32 (all tensors of one call share it).
+ * GQA: query head hq reads kv head hq / (Hq / Hkv), as SDPA enable_gqa does.
+ * Softmax statistics are accumulated in fp32 in every variant.
+ */
+#ifndef WFD_B200_H
+#define WFD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WFD_ABI_VERSION 1
+
+enum wfd_status {
+  WFD_OK = 0,
+  WFD_ERR_INVALID_ARG = 1,     /* host-side argument check failed            */
+  WFD_ERR_UNSUPPORTED = 2,     /* dtype / head_dim / GQA shape not built     */
+  WFD_ERR_WORKSPACE = 3,       /* workspace missing or too small             */
+  WFD_ERR_CUDA = 4,            /* a CUDA runtime call failed                 */
+  WFD_ERR_ALIGNMENT = 5,       /* a pointer is not 16-byte aligned           */
+  WFD_ERR_DEVICE_TIMEOUT = 16, /* device error word: bounded wait gave up    */
+  WFD_ERR_DEVICE_BOUNDS = 17   /* device error word: index/length out of range */
+};
+
+enum wfd_dtype { WFD_DTYPE_BF16 = 0, WFD_DTYPE_F32 = 1 };
+
+/* One wavefront work item: q_len query rows of sequence `seq` that sit at
+ * absolute positions pos0 .. pos0+q_len-1 of KV slot `slot`.  Row j of the item
+ * (q / k_new row q_row0 + j) writes its K/V at position pos0 + j and attends
+ * keys [0, pos0 + j] of that slot (bottom-right causal inside the window).
+ * q_len == 1 is the wavefront decode row; q_len > 1 is a verify window or a
+ * group of rows sharing one slot.  Mirrors the (slots, seq_ids, positions)
+ * triples of BatchStaticKVCache.write_tokens / gather_pack
+ * (batch_kv_cache.py:61-96) and the grouped segments of
+ * OuroBlocksBatch.advance_union (ouro_blocks_batch.py:180-231). */
+typedef struct wfd_item {
+  int32_t slot;
+  int32_t seq;
+  int32_t pos0;
+  int32_t q_len;
+  int32_t q_row0;
+} wfd_item;
+
+/* Library identity. */
+int wfd_abi_version(void);
+const char* wfd_status_string(int status);
+
+/* Copy the device error word to *h_err and reset it to 0 (synchronises
+ * `stream`).  Returns WFD_OK, or WFD_ERR_DEVICE_TIMEOUT / _BOUNDS when the word
+ * was non-zero. */
+int wfd_read_error(int32_t* d_err, int32_t* h_err, void* stream);
+
+/* Bytes of device workspace the attention entry points need for up to
+ * `max_items` work items / segments.  The workspace must be zero-filled once
+ * after allocation (wfd_workspace_init); the kernels leave it zeroed again. */
+size_t wfd_workspace_bytes(int32_t max_items, int32_t head_dim, int32_t dtype);
+int wfd_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/* Wavefront decode / verify attention over KV slots, with the K/V append fused.
+ *
+ * Replaces, per reference call site, the sequence
+ *   BatchStaticKVCache.write_tokens   (batch_kv_cache.py:61-73)
+ *   BatchStaticKVCache.gather_pack    (batch_kv_cache.py:75-96)
+ *   fa4_attention.attn_varlen / attn_varlen_q1_padded (fa4_attention.py:301-342)
+ * made by OuroBlocksBatch.advance_union (ouro_blocks_batch.py:207-231) and
+ * HuginnBlocksBatch._union_attn (huginn_blocks_batch.py:254-285), and the
+ * per-row graph-engine loop of `_fa_varlen` + index_copy_
+ * (graph_blocks.py:171-194, 306-328).
+ *
+ * For every item: writes k_new/v_new rows into the cache at (slot+slot_offset,
+ * seq, pos0+j), raises lens[slot+slot_offset][seq] to at least pos0+q_len (if
+ * lens != NULL), and writes out rows q_row0.. with the attention of each row
+ * over its slot prefix.  Keys in [0, pos0) are read in place from the cache;
+ * the window keys come from k_new/v_new.  `slot_offset` lets one item table
+ * serve every layer of a tick (slot = depth * n_layers + layer in the
+ * reference, ouro_blocks_batch.py:77-78).  `items` is a DEVICE array so the
+ * table can be updated between CUDA-graph replays.  scale <= 0 selects
+ * 1/sqrt(head_dim).  Chooses the CUDA-core decode kernel or the tcgen05 verify
+ * kernel from max_q (largest q_len in the table; an upper bound is fine). */
+int wfd_wave_attn(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                  void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
+                  int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
+                  int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
+                  void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream);
+
+/* Same as wfd_wave_attn but forces the kernel: 0 = CUDA-core decode kernel,
+ * 1 = tcgen05 verify kernel.  For tests and benchmarks. */
+int wfd_wave_attn_kernel(int32_t which, const void* q, const void* k_new, const void* v_new, void* k_cache,
+                         void* v_cache, void* out, int32_t* lens, const wfd_item* items, int32_t n_items,
+                         int32_t max_q, int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs,
+                         int32_t max_seq, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
+                         float scale, void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream);
+
+/* Packed varlen attention, drop-in for fa4_attention.attn_varlen
+ * (fa4_attention.py:301-317) and for the graph engine's direct
+ * aten._flash_attention_forward call (graph_blocks.py:37-43).  Segment i: query
+ * rows [cu_q[i], cu_q[i+1]), key rows [cu_k[i], cu_k[i+1]) of k / v.
+ * causal != 0: bottom-right causal per segment (row r sees keys
+ * <= k_len - q_len + r); causal == 0: every row sees the whole segment.
+ * cu_q / cu_k are DEVICE int32 arrays (lengths as data, graph_blocks.py:5-11).
+ * total_k bounds the key rows any cu_k entry may address. */
+int wfd_attn_varlen(const void* q, const void* k, const void* v, void* out, const int32_t* cu_q,
+                    const int32_t* cu_k, int32_t n_seg, int32_t max_q, int32_t total_q, int32_t total_k,
+                    int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t causal,
+                    float scale, void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream);
+
+/* Explicit-segment attention: segment i has query rows [q_row0[i], +q_len[i])
+ * and key rows [k_row0[i], +k_len[i]), bottom-right causal when causal != 0.
+ * Segments may share key rows.  Serves attn_dense (fa4_attention.py:191-232)
+ * and attn_cutoff_multi (fa4_attention.py:240-291) where each query has its
+ * own key cutoff.  All arrays are DEVICE int32. */
+int wfd_attn_segments(const void* q, const void* k, const void* v, void* out, const int32_t* q_row0,
+                      const int32_t* q_len, const int32_t* k_row0, const int32_t* k_len, int32_t n_seg,
+                      int32_t max_q, int32_t total_q, int32_t total_k, int32_t n_heads, int32_t n_kv_heads,
+                      int32_t head_dim, int32_t dtype, int32_t causal, float scale, void* workspace,
+                      size_t workspace_bytes, int32_t* d_err, void* stream);
+
+/* KV append: BatchStaticKVCache.write_tokens (batch_kv_cache.py:61-73).  Row i
+ * of k_new / v_new goes to (slots[i]+slot_offset, seqs[i], positions[i]);
+ * lens[slot][seq] = max(lens, positions[i] + 1) when lens != NULL.  Device int32
+ * index arrays.  Out-of-range rows are skipped and flagged (the reference
+ * raises IndexError, batch_kv_cache.py:70-71). */
+int wfd_append(const void* k_new, const void* v_new, void* k_cache, void* v_cache, int32_t* lens,
+               const int32_t* slots, const int32_t* seqs, const int32_t* positions, int32_t n, int32_t slot_offset,
+               int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_kv_heads, int32_t head_dim,
+               int32_t dtype, int32_t* d_err, void* stream);
+
+/* Prefill write: BatchStaticKVCache.write_prefill (batch_kv_cache.py:51-59).
+ * k, v (n_seqs, L, Hkv, Dh) go to positions [0, L) of `slot` for every
+ * sequence; lens[slot][*] = max(lens, L). */
+int wfd_write_prefill(const void* k, const void* v, void* k_cache, void* v_cache, int32_t* lens, int32_t slot,
+                      int32_t L, int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_kv_heads,
+                      int32_t head_dim, int32_t dtype, void* stream);
+
+/* Rollback commit: BatchStaticKVCache.drop_positions_at_and_after
+ * (batch_kv_cache.py:99-105) for many sequences at once.  For every sequence b
+ * with drop_pos[b] >= 0: lens[s][b] = min(lens[s][b], drop_pos[b]) for all
+ * slots s.  K/V buffers are untouched (stale tails are never read). */
+int wfd_commit_drop(int32_t* lens, const int32_t* drop_pos, int32_t n_slots, int32_t n_seqs, void* stream);
+
+/* Accept commit for verify windows.  For item i (slot, seq, pos0, q_len,
+ * q_row0) the accepted rows are either rows [0, accept_len[i]) (accept_len !=
+ * NULL, the greedy accept-prefix of the DtV cascade, scheduler_batch.py:472-499)
+ * or the rows whose accept_mask byte (indexed by q row) is non-zero.  Accepted
+ * rows are compacted in place to positions pos0, pos0+1, ... of the slot (a
+ * no-op when they already form a prefix), lens[slot+slot_offset][seq] is set to
+ * pos0 + n_accepted, acc_rows[q_row0 + k] receives the q row of the k-th
+ * accepted row and acc_count[i] the count (either output may be NULL). */
+int wfd_commit_window(void* k_cache, void* v_cache, int32_t* lens, const wfd_item* items, int32_t n_items,
+                      const int32_t* accept_len, const uint8_t* accept_mask, int32_t* acc_rows,
+                      int32_t* acc_count, int32_t slot_offset, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
+                      int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t* d_err, void* stream);
+
+/* Gather packed prefixes, BatchStaticKVCache.gather_pack (batch_kv_cache.py:75-96):
+ * segment i copies positions [0, uptos[i]] of (slots[i], seqs[i]) into rows
+ * cu_k[i] .. of k_pack / v_pack.  cu_k (n+1) is a DEVICE int32 array the caller
+ * computed (cu_k[i+1] - cu_k[i] == uptos[i] + 1).  Kept for API parity; the
+ * wavefront kernels read slots in place and never need it. */
+int wfd_gather_pack(const void* k_cache, const void* v_cache, void* k_pack, void* v_pack, const int32_t* slots,
+                    const int32_t* seqs, const int32_t* cu_k, int32_t n, int32_t n_slots, int32_t n_seqs,
+                    int32_t max_seq, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t* d_err,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WFD_B200_H */

@@ -1,0 +1,59 @@
+"""The C-ABI library loads and exports every symbol include/wfd_b200.h declares
+(no compute calls: these run without a GPU)."""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "wfd_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(wfd_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import __graft_entry__
+    __graft_entry__.build()
+    from wavefront_decoding_b200 import _abi
+    return _abi.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "wfd_wave_attn" in names and "wfd_commit_window" in names and "wfd_append" in names
+
+
+def test_every_declared_symbol_exported(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in wfd_b200.h but not exported"
+
+
+def test_python_binding_covers_header(lib):
+    from wavefront_decoding_b200 import _abi
+    assert set(_abi.EXPORTED) == set(declared_functions())
+
+
+def test_abi_version_and_status_strings(lib):
+    assert lib.wfd_abi_version() == 1
+    assert lib.wfd_status_string(0) == b"ok"
+    assert b"workspace" in lib.wfd_status_string(3)
+
+
+def test_item_struct_layout():
+    from wavefront_decoding_b200 import _abi
+    assert ctypes.sizeof(_abi.wfd_item) == 20
+
+
+def test_product_does_not_import_oracle():
+    pkg = ROOT / "wavefront-decoding_b200"
+    for p in pkg.rglob("*.py"):
+        src = p.read_text()
+        assert "oracle" not in re.findall(r"^\s*(?:from|import)\s+(\w+)", src, flags=re.M), p

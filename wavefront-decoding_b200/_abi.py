@@ -1,0 +1,102 @@
+"""ctypes binding of libwfd_b200.so (include/wfd_b200.h).
+
+The library is the product: every attention / KV-slot operation of this
+package goes through these entry points.  Loading fails loudly when the built
+library is missing — there is no Python or CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+_PKG_DIR = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _PKG_DIR / "_lib" / "libwfd_b200.so"
+
+WFD_OK = 0
+WFD_DTYPE_BF16 = 0
+WFD_DTYPE_F32 = 1
+
+# every symbol include/wfd_b200.h declares
+EXPORTED = (
+    "wfd_abi_version", "wfd_status_string", "wfd_read_error", "wfd_workspace_bytes", "wfd_workspace_init",
+    "wfd_wave_attn", "wfd_wave_attn_kernel", "wfd_attn_varlen", "wfd_attn_segments", "wfd_append",
+    "wfd_write_prefill", "wfd_commit_drop", "wfd_commit_window", "wfd_gather_pack",
+)
+
+
+class WfdError(RuntimeError):
+    """A libwfd_b200 entry point returned a non-zero status."""
+
+    def __init__(self, what: str, status: int, detail: str):
+        super().__init__(f"{what}: status {status} ({detail})")
+        self.status = status
+
+
+class wfd_item(ctypes.Structure):
+    _fields_ = [("slot", ctypes.c_int32), ("seq", ctypes.c_int32), ("pos0", ctypes.c_int32),
+                ("q_len", ctypes.c_int32), ("q_row0", ctypes.c_int32)]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int32
+_F = ctypes.c_float
+_S = ctypes.c_size_t
+
+_SIGS = {
+    "wfd_abi_version": ([], _I),
+    "wfd_status_string": ([_I], ctypes.c_char_p),
+    "wfd_read_error": ([_P, _P, _P], _I),
+    "wfd_workspace_bytes": ([_I, _I, _I], _S),
+    "wfd_workspace_init": ([_P, _S, _P], _I),
+    # q k_new v_new kc vc out lens items n max_q slot_off n_rows n_slots n_seqs max_seq Hq Hkv Dh dtype scale ws ws_bytes err stream
+    "wfd_wave_attn": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P, _P], _I),
+    "wfd_wave_attn_kernel": ([_I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S,
+                              _P, _P], _I),
+    # q k v out cu_q cu_k n max_q total_q total_k Hq Hkv Dh dtype causal scale ws ws_bytes err stream
+    "wfd_attn_varlen": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P, _P], _I),
+    # q k v out q_row0 q_len k_row0 k_len n max_q total_q total_k Hq Hkv Dh dtype causal scale ws ws_bytes err stream
+    "wfd_attn_segments": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P, _P], _I),
+    # k_new v_new kc vc lens slots seqs positions n slot_off n_slots n_seqs max_seq Hkv Dh dtype err stream
+    "wfd_append": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
+    # k v kc vc lens slot L n_slots n_seqs max_seq Hkv Dh dtype stream
+    "wfd_write_prefill": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P], _I),
+    "wfd_commit_drop": ([_P, _P, _I, _I, _P], _I),
+    # kc vc lens items n accept_len accept_mask acc_rows acc_count slot_off n_slots n_seqs max_seq Hkv Dh dtype err stream
+    "wfd_commit_window": ([_P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
+    # kc vc kp vp slots seqs cu_k n n_slots n_seqs max_seq Hkv Dh dtype err stream
+    "wfd_gather_pack": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load libwfd_b200.so once and attach the C signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"libwfd_b200.so not found at {LIB_PATH}; build it with "
+                "`python wavefront-decoding_b200/build.py` (nvcc, sm_100a)")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return load().wfd_status_string(status).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != WFD_OK:
+        raise WfdError(what, status, status_string(status))

@@ -1,0 +1,534 @@
+// extern "C" entry points of libwfd_b200.so (declared in include/wfd_b200.h).
+//
+// Host side only: argument checks, workspace carving, kernel-variant selection
+// and launches.  Every launch goes to the caller's stream; nothing here
+// allocates device memory or synchronises (except wfd_read_error, whose job is
+// to read the device error word).
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "wfd_cache.cuh"
+#include "wfd_common.cuh"
+#include "wfd_decode.cuh"
+#include "wfd_plan.cuh"
+#include "wfd_verify.cuh"
+
+using namespace wfd;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kGridPerSm = 4;  // upper bound on resident decode CTAs per SM used for sizing
+
+struct DevInfo {
+  int sms = 0;
+  bool init = false;
+};
+DevInfo g_dev[kMaxDevices];
+std::mutex g_mu;
+
+int current_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_dev[dev].init) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    g_dev[dev].sms = sms;
+    g_dev[dev].init = true;
+  }
+  return g_dev[dev].sms;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int elem_bytes(int dtype) { return dtype == WFD_DTYPE_BF16 ? 2 : 4; }
+inline int pow2ceil(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Largest NQ the CUDA-core kernel is built for: query vectors per unit are
+// register-resident (q and the output accumulator), so 16-byte-vector bf16 rows
+// stop at 8 vectors and fp32 rows at 16.
+inline int nq_cap(int dtype, int dh) { return dtype == WFD_DTYPE_BF16 ? 8 : 16; }
+
+// Workspace layout, all regions 256-byte aligned.
+struct WsLayout {
+  size_t segs, prefix, cnt, part, total;
+};
+
+WsLayout ws_layout(int max_items, int head_dim, int sms) {
+  WsLayout w;
+  const size_t n_ctas = (size_t)sms * kGridPerSm;
+  w.segs = 0;
+  w.prefix = align256(w.segs + (size_t)max_items * sizeof(Seg));
+  w.cnt = align256(w.prefix + (size_t)(max_items + 1) * sizeof(long long));
+  w.part = align256(w.cnt + n_ctas * sizeof(int));
+  // decode: NQ <= 16 query vectors per partial slot, kGridPerSm CTAs per SM;
+  // verify: kVerifyMaxRows vectors per slot, one CTA per SM.
+  const size_t dec = 2 * n_ctas * (size_t)16 * (head_dim + 2);
+  const size_t ver = 2 * (size_t)sms * kVerifyMaxRows * (head_dim + 2);
+  w.total = align256(w.part + (dec > ver ? dec : ver) * sizeof(float));
+  return w;
+}
+
+template <typename T, int DH, int NQ>
+int launch_decode_t(const DecodeParams& p, int sms, cudaStream_t st) {
+  using C = DecodeCfg<T, DH, NQ>;
+  static bool attr_set[kMaxDevices] = {};
+  static int occ_cache[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(wave_decode_kernel<T, DH, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
+      return WFD_ERR_CUDA;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, wave_decode_kernel<T, DH, NQ>, C::THREADS, C::SMEM) !=
+        cudaSuccess)
+      return WFD_ERR_CUDA;
+    occ_cache[dev] = occ < 1 ? 1 : (occ > kGridPerSm ? kGridPerSm : occ);
+    attr_set[dev] = true;
+  }
+  const int grid = sms * occ_cache[dev];
+  wave_decode_kernel<T, DH, NQ><<<grid, C::THREADS, C::SMEM, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+template <typename T, int DH>
+int launch_decode_dh(int nq, const DecodeParams& p, int sms, cudaStream_t st) {
+  switch (nq) {
+    case 1: return launch_decode_t<T, DH, 1>(p, sms, st);
+    case 2: return launch_decode_t<T, DH, 2>(p, sms, st);
+    case 4: return launch_decode_t<T, DH, 4>(p, sms, st);
+    case 8: return launch_decode_t<T, DH, 8>(p, sms, st);
+    default: break;
+  }
+  if constexpr (Elem<T>::kVec == 4) {
+    if (nq == 16) return launch_decode_t<T, DH, 16>(p, sms, st);
+  }
+  return WFD_ERR_UNSUPPORTED;
+}
+
+int launch_decode(int dtype, int dh, int nq, const DecodeParams& p, int sms, cudaStream_t st) {
+  if (dtype == WFD_DTYPE_BF16) {
+    if (dh == 128) return launch_decode_dh<__nv_bfloat16, 128>(nq, p, sms, st);
+    if (dh == 64) return launch_decode_dh<__nv_bfloat16, 64>(nq, p, sms, st);
+  } else {
+    if (dh == 128) return launch_decode_dh<float, 128>(nq, p, sms, st);
+    if (dh == 64) return launch_decode_dh<float, 64>(nq, p, sms, st);
+  }
+  return WFD_ERR_UNSUPPORTED;
+}
+
+// Common core of every attention entry point: plan, then attend.
+struct AttnArgs {
+  int mode;
+  // plan inputs
+  const wfd_item* items;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  const int32_t *s_q_row0, *s_q_len, *s_k_row0, *s_k_len;
+  int n, max_q;
+  int n_slots, n_seqs, max_seq, n_rows, total_q, total_k;
+  int slot_offset;
+  // tensors
+  const void *q, *k, *v, *k_new, *v_new;
+  void *k_app, *v_app, *out;
+  int32_t* lens;
+  int Hq, Hkv, Dh, dtype, causal;
+  float scale;
+  void* ws;
+  size_t ws_bytes;
+  int* err;
+  int which;  // -1 auto, 0 decode kernel, 1 verify kernel
+};
+
+int run_attention(const AttnArgs& A, cudaStream_t st) {
+  if (A.n < 0 || A.Hq <= 0 || A.Hkv <= 0 || A.Hq % A.Hkv != 0) return WFD_ERR_INVALID_ARG;
+  if (A.dtype != WFD_DTYPE_BF16 && A.dtype != WFD_DTYPE_F32) return WFD_ERR_UNSUPPORTED;
+  if (A.Dh != 64 && A.Dh != 128) return WFD_ERR_UNSUPPORTED;
+  if (!A.q || !A.k || !A.v || !A.out || !A.ws) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(A.q) || !aligned16(A.k) || !aligned16(A.v) || !aligned16(A.out)) return WFD_ERR_ALIGNMENT;
+  if ((A.k_new && !aligned16(A.k_new)) || (A.v_new && !aligned16(A.v_new))) return WFD_ERR_ALIGNMENT;
+  const int G = A.Hq / A.Hkv;
+  const int sms = current_sms();
+  if (sms <= 0) return WFD_ERR_CUDA;
+  if (A.n == 0) return WFD_OK;
+  const WsLayout L = ws_layout(A.n, A.Dh, sms);
+  if (A.ws_bytes < L.total || !aligned16(A.ws)) return WFD_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(A.ws);
+
+  const int max_q = A.max_q < 1 ? 1 : A.max_q;
+  int which = A.which;
+  if (which < 0) which = (max_q >= kVerifyMinRows && verify_supported(A.dtype, A.Dh, G, max_q)) ? 1 : 0;
+  if (which == 1 && !verify_supported(A.dtype, A.Dh, G, max_q)) return WFD_ERR_UNSUPPORTED;
+
+  int NQ;
+  if (which == 0) {
+    NQ = pow2ceil(max_q * G);
+    const int cap = nq_cap(A.dtype, A.Dh);
+    if (NQ > cap) NQ = cap;
+  } else {
+    NQ = verify_rows(G, max_q);
+  }
+
+  PlanParams pp;
+  memset(&pp, 0, sizeof(pp));
+  pp.mode = A.mode;
+  pp.n = A.n;
+  pp.items = A.items;
+  pp.n_slots = A.n_slots;
+  pp.n_seqs = A.n_seqs;
+  pp.max_seq = A.max_seq;
+  pp.n_rows = A.n_rows;
+  pp.cu_q = A.cu_q;
+  pp.cu_k = A.cu_k;
+  pp.total_q = A.total_q;
+  pp.total_k = A.total_k;
+  pp.s_q_row0 = A.s_q_row0;
+  pp.s_q_len = A.s_q_len;
+  pp.s_k_row0 = A.s_k_row0;
+  pp.s_k_len = A.s_k_len;
+  pp.G = G;
+  pp.NQ = NQ;
+  pp.qg_split = which == 0 ? 1 : 0;
+  pp.segs = reinterpret_cast<Seg*>(ws + L.segs);
+  pp.prefix = reinterpret_cast<long long*>(ws + L.prefix);
+  pp.out = A.out;
+  pp.Hq = A.Hq;
+  pp.Dh = A.Dh;
+  pp.elem_bytes = elem_bytes(A.dtype);
+  pp.err = A.err;
+  plan_kernel<<<1, kPlanThreads, 0, st>>>(pp);
+  if (cudaGetLastError() != cudaSuccess) return WFD_ERR_CUDA;
+
+  const float scale = A.scale > 0.f ? A.scale : 1.0f / std::sqrt((float)A.Dh);
+  const float log2e = 1.4426950408889634f;
+
+  if (which == 1) {
+    VerifyParams vp;
+    memset(&vp, 0, sizeof(vp));
+    vp.q = A.q;
+    vp.k = A.k;
+    vp.v = A.v;
+    vp.k_new = A.k_new;
+    vp.v_new = A.v_new;
+    vp.k_app = A.k_app;
+    vp.v_app = A.v_app;
+    vp.out = A.out;
+    vp.lens = A.lens;
+    vp.segs = pp.segs;
+    vp.prefix = pp.prefix;
+    vp.n_segs = A.n;
+    vp.Hq = A.Hq;
+    vp.Hkv = A.Hkv;
+    vp.G = G;
+    vp.scale_log2 = scale * log2e;
+    vp.causal = A.causal;
+    vp.k_row_offset = (long long)A.slot_offset * A.n_seqs * (long long)A.max_seq;
+    vp.lens_offset = A.slot_offset * A.n_seqs;
+    vp.ws_part = reinterpret_cast<float*>(ws + L.part);
+    vp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
+    vp.err = A.err;
+    return launch_verify(A.dtype, A.Dh, NQ, vp, sms, st);
+  }
+
+  DecodeParams dp;
+  memset(&dp, 0, sizeof(dp));
+  dp.q = A.q;
+  dp.k = A.k;
+  dp.v = A.v;
+  dp.k_new = A.k_new;
+  dp.v_new = A.v_new;
+  dp.k_app = A.k_app;
+  dp.v_app = A.v_app;
+  dp.out = A.out;
+  dp.lens = A.lens;
+  dp.segs = pp.segs;
+  dp.prefix = pp.prefix;
+  dp.n_segs = A.n;
+  dp.Hq = A.Hq;
+  dp.Hkv = A.Hkv;
+  dp.G = G;
+  dp.scale_log2 = scale * log2e;
+  dp.causal = A.causal;
+  dp.k_row_offset = (long long)A.slot_offset * A.n_seqs * (long long)A.max_seq;
+  dp.lens_offset = A.slot_offset * A.n_seqs;
+  dp.ws_part = reinterpret_cast<float*>(ws + L.part);
+  dp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
+  dp.err = A.err;
+  return launch_decode(A.dtype, A.Dh, NQ, dp, sms, st);
+}
+
+int wave_common(int which, const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
+                int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
+                int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
+                void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream) {
+  if (!items || !k_new || !v_new || !k_cache || !v_cache) return WFD_ERR_INVALID_ARG;
+  if (n_slots <= 0 || n_seqs <= 0 || max_seq <= 0 || n_rows < 0) return WFD_ERR_INVALID_ARG;
+  if (slot_offset < 0 || slot_offset >= n_slots) return WFD_ERR_INVALID_ARG;
+  AttnArgs A;
+  memset(&A, 0, sizeof(A));
+  A.mode = kPlanSlots;
+  A.items = items;
+  A.n = n_items;
+  A.max_q = max_q;
+  // items are checked against the slots the table can address at this offset
+  A.n_slots = n_slots - slot_offset;
+  A.n_seqs = n_seqs;
+  A.max_seq = max_seq;
+  A.n_rows = n_rows;
+  A.slot_offset = slot_offset;
+  A.q = q;
+  A.k = k_cache;
+  A.v = v_cache;
+  A.k_new = k_new;
+  A.v_new = v_new;
+  A.k_app = k_cache;
+  A.v_app = v_cache;
+  A.out = out;
+  A.lens = lens;
+  A.Hq = n_heads;
+  A.Hkv = n_kv_heads;
+  A.Dh = head_dim;
+  A.dtype = dtype;
+  A.causal = 1;
+  A.scale = scale;
+  A.ws = workspace;
+  A.ws_bytes = workspace_bytes;
+  A.err = d_err;
+  A.which = which;
+  return run_attention(A, static_cast<cudaStream_t>(stream));
+}
+
+CacheGeom geom(int n_slots, int n_seqs, int max_seq, int Hkv, int Dh, int dtype) {
+  CacheGeom g;
+  g.n_slots = n_slots;
+  g.n_seqs = n_seqs;
+  g.max_seq = max_seq;
+  g.Hkv = Hkv;
+  g.Dh = Dh;
+  g.elem_bytes = elem_bytes(dtype);
+  return g;
+}
+
+bool geom_ok(int n_slots, int n_seqs, int max_seq, int Hkv, int Dh, int dtype) {
+  if (n_slots <= 0 || n_seqs <= 0 || max_seq <= 0 || Hkv <= 0 || Dh <= 0) return false;
+  if (dtype != WFD_DTYPE_BF16 && dtype != WFD_DTYPE_F32) return false;
+  return ((long long)Hkv * Dh * elem_bytes(dtype)) % 16 == 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wfd_abi_version(void) { return WFD_ABI_VERSION; }
+
+const char* wfd_status_string(int status) {
+  switch (status) {
+    case WFD_OK: return "ok";
+    case WFD_ERR_INVALID_ARG: return "invalid argument";
+    case WFD_ERR_UNSUPPORTED: return "unsupported dtype / head_dim / shape";
+    case WFD_ERR_WORKSPACE: return "workspace missing or too small";
+    case WFD_ERR_CUDA: return "CUDA runtime error";
+    case WFD_ERR_ALIGNMENT: return "pointer not 16-byte aligned";
+    case WFD_ERR_DEVICE_TIMEOUT: return "device: bounded wait gave up";
+    case WFD_ERR_DEVICE_BOUNDS: return "device: index or length out of range";
+    default: return "unknown status";
+  }
+}
+
+int wfd_read_error(int32_t* d_err, int32_t* h_err, void* stream) {
+  if (!d_err || !h_err) return WFD_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess) return WFD_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return WFD_ERR_CUDA;
+  *h_err = v;
+  if (v == 0) return WFD_OK;
+  if (cudaMemsetAsync(d_err, 0, sizeof(int32_t), st) != cudaSuccess) return WFD_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return WFD_ERR_CUDA;
+  return (v & kErrTimeout) ? WFD_ERR_DEVICE_TIMEOUT : WFD_ERR_DEVICE_BOUNDS;
+}
+
+size_t wfd_workspace_bytes(int32_t max_items, int32_t head_dim, int32_t dtype) {
+  (void)dtype;
+  const int sms = current_sms();
+  if (sms <= 0 || max_items < 0) return 0;
+  return ws_layout(max_items, head_dim, sms).total;
+}
+
+int wfd_workspace_init(void* workspace, size_t bytes, void* stream) {
+  if (!workspace) return WFD_ERR_INVALID_ARG;
+  return cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream)) == cudaSuccess ? WFD_OK
+                                                                                                  : WFD_ERR_CUDA;
+}
+
+int wfd_wave_attn(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache, void* out,
+                  int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q, int32_t slot_offset,
+                  int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_heads,
+                  int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale, void* workspace,
+                  size_t workspace_bytes, int32_t* d_err, void* stream) {
+  return wave_common(-1, q, k_new, v_new, k_cache, v_cache, out, lens, items, n_items, max_q, slot_offset, n_rows,
+                     n_slots, n_seqs, max_seq, n_heads, n_kv_heads, head_dim, dtype, scale, workspace,
+                     workspace_bytes, d_err, stream);
+}
+
+int wfd_wave_attn_kernel(int32_t which, const void* q, const void* k_new, const void* v_new, void* k_cache,
+                         void* v_cache, void* out, int32_t* lens, const wfd_item* items, int32_t n_items,
+                         int32_t max_q, int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs,
+                         int32_t max_seq, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
+                         float scale, void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream) {
+  if (which != 0 && which != 1) return WFD_ERR_INVALID_ARG;
+  return wave_common(which, q, k_new, v_new, k_cache, v_cache, out, lens, items, n_items, max_q, slot_offset,
+                     n_rows, n_slots, n_seqs, max_seq, n_heads, n_kv_heads, head_dim, dtype, scale, workspace,
+                     workspace_bytes, d_err, stream);
+}
+
+int wfd_attn_varlen(const void* q, const void* k, const void* v, void* out, const int32_t* cu_q, const int32_t* cu_k,
+                    int32_t n_seg, int32_t max_q, int32_t total_q, int32_t total_k, int32_t n_heads,
+                    int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t causal, float scale,
+                    void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream) {
+  if (!cu_q || !cu_k || total_q < 0 || total_k < 0) return WFD_ERR_INVALID_ARG;
+  AttnArgs A;
+  memset(&A, 0, sizeof(A));
+  A.mode = kPlanCu;
+  A.cu_q = cu_q;
+  A.cu_k = cu_k;
+  A.n = n_seg;
+  A.max_q = max_q;
+  A.total_q = total_q;
+  A.total_k = total_k;
+  A.q = q;
+  A.k = k;
+  A.v = v;
+  A.out = out;
+  A.Hq = n_heads;
+  A.Hkv = n_kv_heads;
+  A.Dh = head_dim;
+  A.dtype = dtype;
+  A.causal = causal ? 1 : 0;
+  A.scale = scale;
+  A.ws = workspace;
+  A.ws_bytes = workspace_bytes;
+  A.err = d_err;
+  A.which = -1;
+  return run_attention(A, static_cast<cudaStream_t>(stream));
+}
+
+int wfd_attn_segments(const void* q, const void* k, const void* v, void* out, const int32_t* q_row0,
+                      const int32_t* q_len, const int32_t* k_row0, const int32_t* k_len, int32_t n_seg,
+                      int32_t max_q, int32_t total_q, int32_t total_k, int32_t n_heads, int32_t n_kv_heads,
+                      int32_t head_dim, int32_t dtype, int32_t causal, float scale, void* workspace,
+                      size_t workspace_bytes, int32_t* d_err, void* stream) {
+  if (!q_row0 || !q_len || !k_row0 || !k_len || total_q < 0 || total_k < 0) return WFD_ERR_INVALID_ARG;
+  AttnArgs A;
+  memset(&A, 0, sizeof(A));
+  A.mode = kPlanSegs;
+  A.s_q_row0 = q_row0;
+  A.s_q_len = q_len;
+  A.s_k_row0 = k_row0;
+  A.s_k_len = k_len;
+  A.n = n_seg;
+  A.max_q = max_q;
+  A.total_q = total_q;
+  A.total_k = total_k;
+  A.q = q;
+  A.k = k;
+  A.v = v;
+  A.out = out;
+  A.Hq = n_heads;
+  A.Hkv = n_kv_heads;
+  A.Dh = head_dim;
+  A.dtype = dtype;
+  A.causal = causal ? 1 : 0;
+  A.scale = scale;
+  A.ws = workspace;
+  A.ws_bytes = workspace_bytes;
+  A.err = d_err;
+  A.which = -1;
+  return run_attention(A, static_cast<cudaStream_t>(stream));
+}
+
+int wfd_append(const void* k_new, const void* v_new, void* k_cache, void* v_cache, int32_t* lens,
+               const int32_t* slots, const int32_t* seqs, const int32_t* positions, int32_t n, int32_t slot_offset,
+               int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_kv_heads, int32_t head_dim,
+               int32_t dtype, int32_t* d_err, void* stream) {
+  if (!geom_ok(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype)) return WFD_ERR_INVALID_ARG;
+  if (n < 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!k_new || !v_new || !k_cache || !v_cache || !slots || !seqs || !positions) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(k_new) || !aligned16(v_new) || !aligned16(k_cache) || !aligned16(v_cache)) return WFD_ERR_ALIGNMENT;
+  const int threads = 256;
+  const int blocks = (int)(((long long)n * 32 + threads - 1) / threads);
+  append_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const char*>(k_new), static_cast<const char*>(v_new), static_cast<char*>(k_cache),
+      static_cast<char*>(v_cache), lens, slots, seqs, positions, n, slot_offset,
+      geom(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype), d_err);
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+int wfd_write_prefill(const void* k, const void* v, void* k_cache, void* v_cache, int32_t* lens, int32_t slot,
+                      int32_t L, int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_kv_heads,
+                      int32_t head_dim, int32_t dtype, void* stream) {
+  if (!geom_ok(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype)) return WFD_ERR_INVALID_ARG;
+  if (slot < 0 || slot >= n_slots || L < 0 || L > max_seq) return WFD_ERR_INVALID_ARG;
+  if (L == 0) return WFD_OK;
+  if (!k || !v || !k_cache || !v_cache) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(k) || !aligned16(v) || !aligned16(k_cache) || !aligned16(v_cache)) return WFD_ERR_ALIGNMENT;
+  const int sms = current_sms();
+  prefill_kernel<<<sms > 0 ? sms * 4 : 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const char*>(k), static_cast<const char*>(v), static_cast<char*>(k_cache),
+      static_cast<char*>(v_cache), lens, slot, L, geom(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype));
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+int wfd_commit_drop(int32_t* lens, const int32_t* drop_pos, int32_t n_slots, int32_t n_seqs, void* stream) {
+  if (!lens || !drop_pos || n_slots <= 0 || n_seqs <= 0) return WFD_ERR_INVALID_ARG;
+  const long long n = (long long)n_slots * n_seqs;
+  const int threads = 256;
+  commit_drop_kernel<<<(int)((n + threads - 1) / threads), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      lens, drop_pos, n_slots, n_seqs);
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+int wfd_commit_window(void* k_cache, void* v_cache, int32_t* lens, const wfd_item* items, int32_t n_items,
+                      const int32_t* accept_len, const uint8_t* accept_mask, int32_t* acc_rows, int32_t* acc_count,
+                      int32_t slot_offset, int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_kv_heads,
+                      int32_t head_dim, int32_t dtype, int32_t* d_err, void* stream) {
+  if (!geom_ok(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype)) return WFD_ERR_INVALID_ARG;
+  if (n_items < 0 || !lens || !items || !k_cache || !v_cache) return WFD_ERR_INVALID_ARG;
+  if ((accept_len == nullptr) == (accept_mask == nullptr)) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(k_cache) || !aligned16(v_cache)) return WFD_ERR_ALIGNMENT;
+  if (n_items == 0) return WFD_OK;
+  commit_window_kernel<<<n_items, kCommitThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<char*>(k_cache), static_cast<char*>(v_cache), lens, items, n_items, accept_len, accept_mask,
+      acc_rows, acc_count, slot_offset, geom(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype), d_err);
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+int wfd_gather_pack(const void* k_cache, const void* v_cache, void* k_pack, void* v_pack, const int32_t* slots,
+                    const int32_t* seqs, const int32_t* cu_k, int32_t n, int32_t n_slots, int32_t n_seqs,
+                    int32_t max_seq, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t* d_err,
+                    void* stream) {
+  if (!geom_ok(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype)) return WFD_ERR_INVALID_ARG;
+  if (n < 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!k_cache || !v_cache || !k_pack || !v_pack || !slots || !seqs || !cu_k) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(k_pack) || !aligned16(v_pack))
+    return WFD_ERR_ALIGNMENT;
+  dim3 grid(8, n);
+  gather_pack_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const char*>(k_cache), static_cast<const char*>(v_cache), static_cast<char*>(k_pack),
+      static_cast<char*>(v_pack), slots, seqs, cu_k, n, geom(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype),
+      d_err);
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+}  // extern "C"

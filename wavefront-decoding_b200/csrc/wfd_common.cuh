@@ -1,0 +1,174 @@
+// Shared device helpers for the wavefront attention / KV-slot kernels (sm_100a).
+//
+// Everything here is plain CUDA + inline PTX for Blackwell: mbarrier-tracked bulk
+// copies (the TMA engine's non-tensor path), bounded waits that report through an
+// error word instead of trapping, and the segment table the planner produces.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/wfd_b200.h"
+
+namespace wfd {
+
+// One attention segment after planning.  A segment is a run of q_len query rows
+// that all read the same key rows [k_row0, k_row0 + k_len) of one key buffer; the
+// last q_len keys are the rows those queries appended (bottom-right causal window,
+// exactly the FA2/SDPA varlen convention used by the reference's attn_varlen).
+struct Seg {
+  long long k_row0;   // first key row, in rows of (Hkv * Dh) elements
+  int k_len;          // number of keys the last query row sees
+  int q_row0;         // first query row in q / out
+  int q_len;          // query rows in the segment
+  int new_row0;       // >= 0: keys [k_len - q_len, k_len) come from k_new rows new_row0.. and
+                      //       are appended to the key buffer; < 0: all keys already in place
+  int n_qg;           // query groups (ceil(q_len * G / NQ)) the decode kernel splits the rows into
+  int lens_idx;       // slot * n_seqs + seq of the slot length to raise (slot mode), else -1
+};
+static_assert(sizeof(Seg) == 32, "Seg must stay 32 bytes");
+
+// Error bits written into the caller's device error word (atomicOr).  The host
+// turns them into WFD_ERR_* status codes; no kernel ever traps.
+enum : int {
+  kErrTimeout = 1 << 0,      // a bounded mbarrier / flag wait gave up
+  kErrBadSlot = 1 << 1,      // slot / sequence index out of range
+  kErrBadPos = 1 << 2,       // position or length outside the slot capacity
+  kErrBadRows = 1 << 3,      // query / new-row index outside the given tensors
+  kErrBadSegs = 1 << 4,      // cu_seqlens not monotone / out of range
+};
+
+__device__ __forceinline__ void set_error(int* err, int bits) {
+  if (err) atomicOr(err, bits);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk copy (PTX ISA 8.x, sm_90+; used here on sm_100a)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: try_wait already suspends for a hardware time slice, so the spin
+// limit below is a multi-second ceiling, never reached by a healthy pipeline.
+constexpr uint32_t kSpinLimit = 1u << 20;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completion tracked as tx bytes
+// on `bar`.  Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// element helpers
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr int kVec = 8;  // elements per 16-byte vector
+  // unpack 8 bf16 (one uint4) into 8 floats: a bf16 is the high half of an fp32.
+  __device__ __forceinline__ static void unpack(const uint4& u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+template <>
+struct Elem<float> {
+  static constexpr int kVec = 4;
+  __device__ __forceinline__ static void unpack(const uint4& u, float (&f)[4]) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float (&f)[4]) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+};
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float ld_cg_f32(const float* p) {
+  float r;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(r) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  // exp2 of a log2-domain score; -inf -> 0.
+  return exp2f(x);
+}
+
+}  // namespace wfd

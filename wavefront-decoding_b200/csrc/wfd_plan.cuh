@@ -1,0 +1,161 @@
+// K0 — segment planner.
+//
+// Turns one of the three caller-facing work descriptions into the normalised
+// segment table (wfd::Seg) plus an exclusive prefix over per-segment work, which
+// the attention kernels use to split the flattened (segment, query-group,
+// kv-head, key) space evenly over a persistent grid.  One CTA; runs before every
+// attention launch so that lengths can live in device memory (CUDA-graph replay
+// with changing positions, as the reference's graph engine requires,
+// graph_blocks.py:5-11).
+#pragma once
+
+#include "wfd_common.cuh"
+
+namespace wfd {
+
+enum PlanMode : int { kPlanSlots = 0, kPlanCu = 1, kPlanSegs = 2 };
+
+struct PlanParams {
+  int mode;
+  int n;  // items / segments
+  // kPlanSlots
+  const wfd_item* items;
+  int n_slots, n_seqs, max_seq, n_rows;
+  // kPlanCu
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int total_q, total_k;
+  // kPlanSegs
+  const int32_t* s_q_row0;
+  const int32_t* s_q_len;
+  const int32_t* s_k_row0;
+  const int32_t* s_k_len;
+  // common
+  int G, NQ;         // GQA group size, query vectors per decode unit
+  int qg_split;      // 1: split rows into ceil(q_len*G/NQ) query groups; 0: one group
+  // outputs
+  Seg* segs;
+  long long* prefix;  // n + 1 entries, per-kv-head work units
+  // zero-fill of query rows that see no keys (k_len == 0)
+  void* out;
+  int Hq, Dh, elem_bytes;
+  int* err;
+};
+
+constexpr int kPlanThreads = 1024;
+
+__device__ __forceinline__ long long block_excl_scan(long long x, long long* warp_tot, long long* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  long long incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    long long y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    long long w = (lane < (blockDim.x >> 5)) ? warp_tot[lane] : 0;
+    long long wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      long long y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    warp_tot[lane] = wi - w;  // exclusive prefix of warp totals
+    if (lane == 31) *total = wi;
+  }
+  __syncthreads();
+  long long r = warp_tot[warp] + incl - x;
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) {
+  __shared__ long long warp_tot[32];
+  __shared__ long long s_total;
+  long long carry = 0;
+  for (int base = 0; base < p.n; base += kPlanThreads) {
+    const int i = base + threadIdx.x;
+    long long work = 0;
+    if (i < p.n) {
+      Seg s;
+      s.k_row0 = 0;
+      s.k_len = 0;
+      s.q_row0 = 0;
+      s.q_len = 0;
+      s.new_row0 = -1;
+      s.lens_idx = -1;
+      bool ok = true;
+      if (p.mode == kPlanSlots) {
+        const wfd_item it = p.items[i];
+        if (it.slot < 0 || it.slot >= p.n_slots || it.seq < 0 || it.seq >= p.n_seqs) {
+          set_error(p.err, kErrBadSlot);
+          ok = false;
+        } else if (it.pos0 < 0 || it.q_len < 0 || (long long)it.pos0 + it.q_len > p.max_seq) {
+          set_error(p.err, kErrBadPos);
+          ok = false;
+        } else if (it.q_row0 < 0 || (long long)it.q_row0 + it.q_len > p.n_rows) {
+          set_error(p.err, kErrBadRows);
+          ok = false;
+        }
+        if (ok) {
+          s.k_row0 = ((long long)it.slot * p.n_seqs + it.seq) * (long long)p.max_seq;
+          s.k_len = it.pos0 + it.q_len;
+          s.q_row0 = it.q_row0;
+          s.q_len = it.q_len;
+          s.new_row0 = it.q_row0;
+          s.lens_idx = it.slot * p.n_seqs + it.seq;
+        }
+      } else if (p.mode == kPlanCu) {
+        const int q0 = p.cu_q[i], q1 = p.cu_q[i + 1];
+        const int k0 = p.cu_k[i], k1 = p.cu_k[i + 1];
+        if (q0 < 0 || q1 < q0 || q1 > p.total_q || k0 < 0 || k1 < k0 || k1 > p.total_k) {
+          set_error(p.err, kErrBadSegs);
+          ok = false;
+        } else {
+          s.k_row0 = k0;
+          s.k_len = k1 - k0;
+          s.q_row0 = q0;
+          s.q_len = q1 - q0;
+        }
+      } else {
+        const int q0 = p.s_q_row0[i], ql = p.s_q_len[i];
+        const int k0 = p.s_k_row0[i], kl = p.s_k_len[i];
+        if (q0 < 0 || ql < 0 || (long long)q0 + ql > p.total_q || k0 < 0 || kl < 0 ||
+            (long long)k0 + kl > p.total_k) {
+          set_error(p.err, kErrBadSegs);
+          ok = false;
+        } else {
+          s.k_row0 = k0;
+          s.k_len = kl;
+          s.q_row0 = q0;
+          s.q_len = ql;
+        }
+      }
+      if (!ok) {
+        s.k_len = 0;
+        s.q_len = 0;
+      }
+      const long long qv = (long long)s.q_len * p.G;
+      s.n_qg = (qv == 0) ? 0 : (p.qg_split ? (int)((qv + p.NQ - 1) / p.NQ) : 1);
+      work = (long long)s.n_qg * s.k_len;
+      p.segs[i] = s;
+      // Query rows with no key to attend produce zeros (written here; no
+      // attention CTA visits a zero-work segment).
+      if (ok && s.q_len > 0 && s.k_len == 0 && p.out != nullptr) {
+        const long long row_bytes = (long long)p.Hq * p.Dh * p.elem_bytes;
+        uint4* o = reinterpret_cast<uint4*>(static_cast<char*>(p.out) + (long long)s.q_row0 * row_bytes);
+        const long long nvec = (long long)s.q_len * row_bytes / 16;
+        for (long long v = 0; v < nvec; ++v) o[v] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    const long long excl = block_excl_scan(work, warp_tot, &s_total);
+    if (i < p.n) p.prefix[i] = carry + excl;
+    carry += s_total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) p.prefix[p.n] = carry;
+}
+
+}  // namespace wfd
