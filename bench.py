@@ -44,14 +44,14 @@ CFG2 = dict(B=8, R=8, H=16, Hkv=4, Dh=128, S=4096, seed=1)
 
 # DRAM traffic of the decode kernel per launch, from the ncu capture summarised
 # in profiles/wave_decode_cfg2.md (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_TRAFFIC_BYTES = None
+NCU_TRAFFIC_BYTES = 537_539_072 + 5_969_920
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -102,7 +102,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -153,12 +153,19 @@ def cpu_baseline(q, K, V, kn, vn, items, budget_s: float, warmup: int = 1, steps
     cpu_path.wave_step(K, V, q, kn, vn, items)
     first = time.perf_counter() - t0
     sample = items
-    if first > 2.0:  # slow host: time a proportional subset of the rows
-        keep = max(1, int(len(items) * 2.0 / first))
-        sample = items[:keep]
+    if steps is None:
+        if first > 2.0:  # slow host: time a proportional subset of the rows
+            sample = items[:max(1, int(len(items) * 2.0 / first))]
+        n = max(1, int(budget_s / max(first * len(sample) / len(items), 1e-3)))
+    else:
+        # fixed step count (reference arm): shrink the rows per step so that
+        # warm-up + timed steps stay within the budget
+        per_step = budget_s / max(1, steps + warmup)
+        if first > per_step:
+            sample = items[:max(1, int(len(items) * per_step / first))]
+        n = steps
     for _ in range(max(0, warmup - 1)):
         cpu_path.wave_step(K, V, q, kn, vn, sample)
-    n = steps if steps is not None else max(1, int(budget_s / max(first * len(sample) / len(items), 1e-3)))
     t0 = time.perf_counter()
     for _ in range(n):
         cpu_path.wave_step(K, V, q, kn, vn, sample)
@@ -176,7 +183,7 @@ def run_reference(args):
     if rank != 0:
         return
     q, K, V, kn, vn, items = cfg2_cpu_inputs(CFG2["seed"])
-    base, n, dt = cpu_baseline(q, K, V, kn, vn, items, 0.0, warmup=max(1, args.warmup), steps=max(1, args.steps))
+    base, n, dt = cpu_baseline(q, K, V, kn, vn, items, 90.0, warmup=max(1, args.warmup), steps=max(1, args.steps))
     c = CFG2
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
             "steps": n, "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True,

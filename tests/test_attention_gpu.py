@@ -234,10 +234,17 @@ def test_wave_attn_many_items_balanced_split(cuda_dev):
         for b in range(B):
             items.append([r, b, int(rng.integers(0, S - 1)), 1, len(items)])
     K, V, q, kn, vn = _wave_case(21, n_slots, B, S, 8, 2, 128, items, torch.bfloat16)
-    for rep in range(2):  # second launch checks the counters were left zeroed
+    ref, _ = _oracle_wave(K, V, q, kn, vn, items)
+    small = [[0, 0, 700, 1, 0], [1, 3, 5, 1, 1], [5, 15, 1000, 1, 2]]
+    Ks, Vs, qs, kns, vns = _wave_case(22, n_slots, B, S, 8, 2, 128, small, torch.float32)
+    ref_s, _ = _oracle_wave(Ks, Vs, qs, kns, vns, small)
+    for rep in range(3):
+        # launches with other item counts / dtypes in between must not disturb
+        # the split-K arrival counters the next launch relies on
         out, _, _, _ = _run_wave(cuda_dev, K, V, q, kn, vn, items, 1)
-        ref, _ = _oracle_wave(K, V, q, kn, vn, items)
         assert maxdiff(out, ref) < TOL_BF16
+        out_s, _, _, _ = _run_wave(cuda_dev, Ks, Vs, qs, kns, vns, small, 1)
+        assert maxdiff(out_s, ref_s) < TOL_F32
     no_device_error(cuda_dev)
 
 

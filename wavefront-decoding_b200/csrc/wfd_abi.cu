@@ -56,23 +56,26 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // stop at 8 vectors and fp32 rows at 16.
 inline int nq_cap(int dtype, int dh) { return dtype == WFD_DTYPE_BF16 ? 8 : 16; }
 
-// Workspace layout, all regions 256-byte aligned.
+// Workspace layout, all regions 256-byte aligned.  The arrival counters come
+// first, at an offset that depends on nothing but the device: they must stay
+// zero between launches, so every call has to find them at the same place
+// whatever its item count or head_dim.
 struct WsLayout {
-  size_t segs, prefix, cnt, part, total;
+  size_t cnt, part, segs, prefix, total;
 };
 
 WsLayout ws_layout(int max_items, int head_dim, int sms) {
   WsLayout w;
   const size_t n_ctas = (size_t)sms * kGridPerSm;
-  w.segs = 0;
-  w.prefix = align256(w.segs + (size_t)max_items * sizeof(Seg));
-  w.cnt = align256(w.prefix + (size_t)(max_items + 1) * sizeof(long long));
+  w.cnt = 0;
   w.part = align256(w.cnt + n_ctas * sizeof(int));
   // decode: NQ <= 16 query vectors per partial slot, kGridPerSm CTAs per SM;
   // verify: kVerifyMaxRows vectors per slot, one CTA per SM.
   const size_t dec = 2 * n_ctas * (size_t)16 * (head_dim + 2);
   const size_t ver = 2 * (size_t)sms * kVerifyMaxRows * (head_dim + 2);
-  w.total = align256(w.part + (dec > ver ? dec : ver) * sizeof(float));
+  w.segs = align256(w.part + (dec > ver ? dec : ver) * sizeof(float));
+  w.prefix = align256(w.segs + (size_t)max_items * sizeof(Seg));
+  w.total = align256(w.prefix + (size_t)(max_items + 1) * sizeof(long long));
   return w;
 }
 
@@ -150,6 +153,7 @@ struct AttnArgs {
 
 int run_attention(const AttnArgs& A, cudaStream_t st) {
   if (A.n < 0 || A.Hq <= 0 || A.Hkv <= 0 || A.Hq % A.Hkv != 0) return WFD_ERR_INVALID_ARG;
+  if (A.n == 0) return WFD_OK;
   if (A.dtype != WFD_DTYPE_BF16 && A.dtype != WFD_DTYPE_F32) return WFD_ERR_UNSUPPORTED;
   if (A.Dh != 64 && A.Dh != 128) return WFD_ERR_UNSUPPORTED;
   if (!A.q || !A.k || !A.v || !A.out || !A.ws) return WFD_ERR_INVALID_ARG;
@@ -270,7 +274,8 @@ int wave_common(int which, const void* q, const void* k_new, const void* v_new, 
                 int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
                 int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
                 void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream) {
-  if (!items || !k_new || !v_new || !k_cache || !v_cache) return WFD_ERR_INVALID_ARG;
+  if (n_items == 0) return WFD_OK;  // empty tick: nothing to append or attend
+  if (!items || !k_new || !v_new || !k_cache || !v_cache || n_items < 0) return WFD_ERR_INVALID_ARG;
   if (n_slots <= 0 || n_seqs <= 0 || max_seq <= 0 || n_rows < 0) return WFD_ERR_INVALID_ARG;
   if (slot_offset < 0 || slot_offset >= n_slots) return WFD_ERR_INVALID_ARG;
   AttnArgs A;

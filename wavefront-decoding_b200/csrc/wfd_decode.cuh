@@ -8,9 +8,10 @@
 // that straddles CTAs is finished by the last CTA to reach it (atomic arrival
 // counter, no spinning), which merges the partial softmax states.
 //
-// Per CTA: 4 warps.  K/V rows of the current unit are staged into shared memory
-// by the TMA bulk-copy engine (cp.async.bulk, one row per copy, mbarrier
-// completion, STAGES-deep ring).  Each key row is read by LANES = Dh/VEC lanes
+// Per CTA: 4 warps, each with a private STAGES-deep ring in shared memory: the
+// warp's lanes stage its K/V rows with the TMA bulk-copy engine (cp.async.bulk,
+// one row per copy, mbarrier completion) and consume them without any CTA-wide
+// barrier inside the key loop.  Each key row is read by LANES = Dh/VEC lanes
 // holding 16 contiguous bytes each; the NQ query vectors of one kv head (GQA
 // group x window rows) live in registers, so every K/V byte is read from HBM
 // once for all query heads that share it.  Scores of TK keys x NQ queries are
@@ -62,13 +63,17 @@ struct DecodeCfg {
   static constexpr int NWARPS = 4;
   static constexpr int THREADS = NWARPS * 32;
   static constexpr int KPW = GROUPS * TK;        // keys per warp per stage
-  static constexpr int KPS = NWARPS * KPW;       // keys per stage
+  static constexpr int KPS = NWARPS * KPW;       // keys per CTA-wide stage (warps interleave)
   static constexpr int ROWB = DH * (int)sizeof(T);
-  static constexpr int STAGE_BYTES = KPS * ROWB * 2;
-  static constexpr int STAGES = cmax(2, cmin(8, 65536 / STAGE_BYTES));
+  // every warp owns a private ring of STAGES buffers (KPW K rows, then KPW V
+  // rows) with its own mbarriers, so no CTA barrier sits inside the key loop
+  static constexpr int WSTAGE_BYTES = KPW * ROWB * 2;
+  static constexpr int STAGES = cmax(2, cmin(8, 16384 / WSTAGE_BYTES));
+  static constexpr int WARP_BYTES = STAGES * WSTAGE_BYTES;
   static constexpr int NG = NWARPS * GROUPS;     // independent softmax states per CTA
   static constexpr int MERGE_BYTES = NG * NQ * (DH + 2) * 4;
-  static constexpr int SMEM = cmax(STAGES * STAGE_BYTES, MERGE_BYTES);
+  static constexpr int SMEM = cmax(NWARPS * WARP_BYTES, MERGE_BYTES);
+  static_assert(KPW <= 32, "one lane issues one row copy pair");
   static constexpr int PART_FLOATS = NQ * (DH + 2);  // one partial slot
   static_assert(LANES >= 8 && LANES <= 32 && (LANES & (LANES - 1)) == 0, "lanes per row");
   static_assert(NQ >= 1 && NQ <= LANES && (NQ & (NQ - 1)) == 0, "NQ must be a power of two <= LANES");
@@ -130,7 +135,8 @@ __device__ __forceinline__ void issue_stage(const DecodeParams& p, const Seg& S,
   if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(cnt * C::ROWB * 2));
   __syncwarp();
   const int win0 = S.k_len - S.q_len;  // first window key (appended rows)
-  for (int k = lane; k < cnt; k += 32) {
+  if (lane < cnt) {
+    const int k = lane;
     const int r = r_base + k;
     const T* ksrc;
     const T* vsrc;
@@ -144,7 +150,7 @@ __device__ __forceinline__ void issue_stage(const DecodeParams& p, const Seg& S,
       vsrc = static_cast<const T*>(p.v) + (row * p.Hkv + h) * DH;
     }
     bulk_g2s(stage + k * C::ROWB, ksrc, C::ROWB, bar);
-    bulk_g2s(stage + C::KPS * C::ROWB + k * C::ROWB, vsrc, C::ROWB, bar);
+    bulk_g2s(stage + C::KPW * C::ROWB + k * C::ROWB, vsrc, C::ROWB, bar);
   }
 }
 
@@ -158,7 +164,7 @@ __global__ void __launch_bounds__(128) wave_decode_kernel(const DecodeParams p) 
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t full_bar[C::STAGES];
+  __shared__ uint64_t full_bar[C::NWARPS][C::STAGES];
   __shared__ int s_flag;
   __shared__ int s_abort;
 
@@ -167,12 +173,14 @@ __global__ void __launch_bounds__(128) wave_decode_kernel(const DecodeParams p) 
   const int gbase = grp * LANES;
 
   if (tid == 0) {
-#pragma unroll
-    for (int s = 0; s < C::STAGES; ++s) mbar_init(&full_bar[s], 1);
+    for (int w = 0; w < C::NWARPS; ++w)
+      for (int s = 0; s < C::STAGES; ++s) mbar_init(&full_bar[w][s], 1);
     fence_mbar_init();
     s_abort = 0;
   }
   __syncthreads();
+  unsigned char* const wbase = smem + warp * C::WARP_BYTES;  // this warp's stage ring
+  uint64_t* const wbar = full_bar[warp];
 
   const long long total = (long long)p.Hkv * p.prefix[p.n_segs];
   if (total <= 0) return;
@@ -198,7 +206,7 @@ __global__ void __launch_bounds__(128) wave_decode_kernel(const DecodeParams p) 
     seg = lo;
   }
 
-  uint32_t gs = 0;  // stages consumed so far (mbarrier phase bookkeeping)
+  uint32_t gs = 0;  // this warp's stages consumed so far (mbarrier phase bookkeeping)
   long long pos = a;
   while (pos < b) {
     while (seg + 1 <= p.n_segs - 1 && (long long)p.Hkv * p.prefix[seg + 1] <= pos) ++seg;
@@ -269,30 +277,31 @@ __global__ void __launch_bounds__(128) wave_decode_kernel(const DecodeParams p) 
       for (int d = 0; d < VEC / 2; ++d) ov[nq][d] = make_float2(0.f, 0.f);
 
     const int n_keys = r_hi - r_lo;
-    const int n_st = (n_keys + C::KPS - 1) / C::KPS;
+    // warp w takes keys [n*KPS + w*KPW, +KPW) of every CTA-wide stage n
+    const int wk0 = warp * C::KPW;
+    const int n_st = (n_keys > wk0) ? (n_keys - wk0 + C::KPS - 1) / C::KPS : 0;
 
-    // stage ring prologue (previous unit's merge used the same smem: order the
+    // ring prologue (the previous unit's merge used the same smem: order the
     // generic-proxy writes before the bulk copies)
     __syncthreads();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    if (warp == 0) {
-      for (int n = 0; n < n_st && n < C::STAGES; ++n) {
-        const int buf = (int)((gs + n) % C::STAGES);
-        const int cnt = cmin(C::KPS, n_keys - n * C::KPS);
-        issue_stage<T, DH, NQ>(p, S, h, r_lo + n * C::KPS, cnt, smem + buf * C::STAGE_BYTES, &full_bar[buf], lane);
-      }
+    for (int n = 0; n < n_st && n < C::STAGES; ++n) {
+      const int buf = (int)((gs + n) % C::STAGES);
+      const int cnt = cmin(C::KPW, n_keys - (n * C::KPS + wk0));
+      issue_stage<T, DH, NQ>(p, S, h, r_lo + n * C::KPS + wk0, cnt, wbase + buf * C::WSTAGE_BYTES, &wbar[buf], lane);
     }
 
-    const int kb = warp * C::KPW + grp * TK;  // my first key inside a stage
-    int n_stop = n_st;                        // first stage not consumed (abort bookkeeping)
+    const int kb = grp * TK;  // my first key inside this warp's stage
+    int n_stop = n_st;        // first stage not consumed (abort bookkeeping)
+    bool abort_w = false;
     for (int n = 0; n < n_st; ++n) {
       const int buf = (int)((gs + n) % C::STAGES);
       const uint32_t par = ((gs + n) / C::STAGES) & 1u;
-      const int cnt = cmin(C::KPS, n_keys - n * C::KPS);
-      const int rb = r_lo + n * C::KPS;
-      if (!mbar_wait_bounded(&full_bar[buf], par)) s_abort = 1;
-      const unsigned char* kst = smem + buf * C::STAGE_BYTES;
-      const unsigned char* vst = kst + C::KPS * C::ROWB;
+      const int cnt = cmin(C::KPW, n_keys - (n * C::KPS + wk0));
+      const int rb = r_lo + n * C::KPS + wk0;
+      abort_w = __any_sync(0xffffffffu, !mbar_wait_bounded(&wbar[buf], par));
+      const unsigned char* kst = wbase + buf * C::WSTAGE_BYTES;
+      const unsigned char* vst = kst + C::KPW * C::ROWB;
 
       // scores
       float part[P];
@@ -356,33 +365,36 @@ __global__ void __launch_bounds__(128) wave_decode_kernel(const DecodeParams p) 
         }
       }
 
-      __syncthreads();  // every warp is done with this stage buffer
-      if (s_abort) {
+      __syncwarp();  // every lane of this warp is done with the buffer
+      if (abort_w) {
         n_stop = n;
         break;
       }
-      if (warp == 0 && n + C::STAGES < n_st) {
+      if (n + C::STAGES < n_st) {
         const int n2 = n + C::STAGES;
-        const int cnt2 = cmin(C::KPS, n_keys - n2 * C::KPS);
-        issue_stage<T, DH, NQ>(p, S, h, r_lo + n2 * C::KPS, cnt2, smem + buf * C::STAGE_BYTES, &full_bar[buf], lane);
+        const int cnt2 = cmin(C::KPW, n_keys - (n2 * C::KPS + wk0));
+        issue_stage<T, DH, NQ>(p, S, h, r_lo + n2 * C::KPS + wk0, cnt2, wbase + buf * C::WSTAGE_BYTES, &wbar[buf],
+                               lane);
       }
     }
-    if (s_abort) {
-      // drain every copy still in flight into this CTA's smem, then leave
-      // stages n_stop .. n_stop+STAGES-1 are the only ones that can still be in flight
-      if (tid == 0) {
+    if (abort_w) {
+      // a bounded wait gave up: drain this warp's copies that can still be in
+      // flight (stages n_stop .. n_stop+STAGES-1), then leave with the CTA
+      if (lane == 0) {
         set_error(p.err, kErrTimeout);
         for (int n = n_stop; n < n_st && n < n_stop + C::STAGES; ++n)
-          mbar_wait_bounded(&full_bar[(gs + n) % C::STAGES], ((gs + n) / C::STAGES) & 1u);
+          mbar_wait_bounded(&wbar[(gs + n) % C::STAGES], ((gs + n) / C::STAGES) & 1u);
+        s_abort = 1;
       }
-      return;
     }
     gs += (uint32_t)n_st;
-
-    // ---- merge the NG softmax states of this CTA ----
     float l_sum = l_run;
 #pragma unroll
     for (int msk = 1; msk < TK; msk <<= 1) l_sum += __shfl_xor_sync(0xffffffffu, l_sum, msk);
+    __syncthreads();  // all warps done with their rings: smem becomes the merge buffer
+    if (s_abort) return;
+
+    // ---- merge the NG softmax states of this CTA ----
     float* m_s = reinterpret_cast<float*>(smem);
     float* l_s = m_s + C::NG * NQ;
     float* o_s = l_s + C::NG * NQ;
