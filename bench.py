@@ -42,9 +42,10 @@ FALLBACK_HBM_GBS = 6650.0
 
 CFG2 = dict(B=8, R=8, H=16, Hkv=4, Dh=128, S=4096, seed=1)
 
-# DRAM traffic of the decode kernel per launch, from the ncu capture summarised
-# in profiles/wave_decode_cfg2.md (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_TRAFFIC_BYTES = 537_539_072 + 5_969_920
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# timed attention kernel, from the ncu captures summarised under profiles/
+# (wave_decode_cfg2.md for the CUDA-core kernel, wave_tc_cfg2.md for tcgen05).
+NCU_TRAFFIC_BYTES = {"cuda_core": 537_539_072 + 5_969_920, "tc": None}
 
 
 def parse():
@@ -55,6 +56,8 @@ def parse():
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", type=int, default=-1, choices=[-1, 0, 1],
+                    help="-1 library default, 0 CUDA-core decode kernel, 1 tcgen05 kernel")
     return ap.parse_args()
 
 
@@ -225,7 +228,7 @@ def run_wfd(args):
     rt.error_word(dev)
 
     def step():
-        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, 1, lens=lens, out=out)
+        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, 1, lens=lens, out=out, kernel=args.kernel)
 
     # warm up eagerly, then capture one step
     for _ in range(max(3, args.warmup)):
@@ -270,7 +273,7 @@ def run_wfd(args):
         knd.copy_(kn_h, non_blocking=True)
         vnd.copy_(vn_h, non_blocking=True)
         itd.copy_(it_h, non_blocking=True)
-        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, 1, lens=lens, out=out)
+        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, 1, lens=lens, out=out, kernel=args.kernel)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -302,6 +305,12 @@ def run_wfd(args):
     value_e2e = total_bytes / (ms_e2e * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     achieved = nbytes / (ms * 1e-3) / 1e9    # per GPU, per launch of the step
+    # bf16 / Dh=128 defaults to the tensor-core kernel: plan + window append +
+    # wave_tc_kernel per step; the CUDA-core kernel is plan + wave_decode_kernel
+    tc = args.kernel != 0
+    kernel_name = ("wave_tc_kernel<16> (+ plan_kernel, append_segs_kernel, timed together)" if tc else
+                   "wave_decode_kernel<bf16,128,4> (+ plan_kernel, timed together)")
+    launches_per_step = 3 if tc else 2
     line = None
     if rank == 0:
         line = {
@@ -315,12 +324,12 @@ def run_wfd(args):
             "wave_rows_per_s": total_rows / (ms * 1e-3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": NCU_TRAFFIC_BYTES,
+                         "traffic": NCU_TRAFFIC_BYTES.get("tc" if tc else "cuda_core"),
                          "algorithmic_bytes_per_launch": nbytes,
-                         "kernel": "wave_decode_kernel (+ plan_kernel, timed together)"},
+                         "kernel": kernel_name},
             "e2e": {"value": value_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
     if world > 1:

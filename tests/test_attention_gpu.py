@@ -279,3 +279,71 @@ def test_cfg2_full_size_vs_oracle(cuda_dev):
         worst = max(worst, float(np.abs(out[row:row + 1] - ref).max()))
     assert worst < TOL_BF16, worst
     assert torch.equal(Kd.cpu(), K)  # rewriting the same rows leaves the cache unchanged
+
+
+# ---------------------------------------------------------------------------
+# tcgen05 tensor-core kernel (kernel=1): decode rows and verify windows
+# ---------------------------------------------------------------------------
+TC_CASES = [
+    # (name, n_slots, B, S, H, Hkv, items)      Dh = 128, bf16
+    ("tc_decode_gqa4", 4, 3, 300, 16, 4, [[r, b, 250 - 7 * r + b, 1, r * 3 + b] for r in range(4) for b in range(3)]),
+    ("tc_first_and_full", 2, 2, 200, 8, 2, [[0, 0, 0, 1, 0], [1, 1, 199, 1, 1], [0, 1, 127, 1, 2], [1, 0, 128, 1, 3]]),
+    ("tc_window8_gqa4", 3, 2, 400, 16, 4, [[r, b, 300 - 50 * r + 3 * b, 8, (r * 2 + b) * 8]
+                                           for r in range(3) for b in range(2)]),
+    ("tc_window_ragged", 2, 3, 300, 8, 2, [[0, 0, 5, 3, 0], [1, 2, 250, 8, 3], [0, 1, 130, 6, 11], [1, 0, 0, 2, 17]]),
+    ("tc_window16_qgroups", 2, 2, 500, 16, 4, [[0, 0, 400, 16, 0], [1, 1, 37, 12, 16]]),
+    ("tc_mha", 2, 2, 300, 4, 4, [[0, 0, 150, 1, 0], [1, 1, 260, 8, 1]]),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES, ids=[c[0] for c in TC_CASES])
+def test_tc_kernel_vs_oracle(cuda_dev, case):
+    name, n_slots, B, S, H, Hkv, items = case
+    K, V, q, kn, vn = _wave_case(sum(map(ord, name)), n_slots, B, S, H, Hkv, 128, items, torch.bfloat16)
+    max_q = max(it[3] for it in items)
+    out, Kd, Vd, lens = _run_wave(cuda_dev, K, V, q, kn, vn, items, max_q, kernel=1)
+    no_device_error(cuda_dev)
+    ref, o = _oracle_wave(K, V, q, kn, vn, items)
+    assert maxdiff(out, ref) < TOL_BF16
+    assert maxdiff(Kd, o.K) == 0.0 and maxdiff(Vd, o.V) == 0.0
+    for slot, seq, p0, ql, _ in items:
+        assert int(lens[slot, seq]) == p0 + ql
+
+
+def test_tc_kernel_balanced_split(cuda_dev):
+    """Many units of very different lengths over the persistent grid; the
+    second and third launches check the arrival counters were left zeroed."""
+    rng = np.random.default_rng(3)
+    n_slots, B, S = 4, 24, 2048
+    items = []
+    for r in range(n_slots):
+        for b in range(B):
+            ql = int(rng.integers(1, 9))
+            items.append([r, b, int(rng.integers(0, S - ql)), ql, 0])
+    row = 0
+    for it in items:
+        it[4] = row
+        row += it[3]
+    K, V, q, kn, vn = _wave_case(31, n_slots, B, S, 16, 4, 128, items, torch.bfloat16)
+    ref, _ = _oracle_wave(K, V, q, kn, vn, items)
+    for _ in range(3):
+        out, _, _, _ = _run_wave(cuda_dev, K, V, q, kn, vn, items, 8, kernel=1)
+        assert maxdiff(out, ref) < TOL_BF16
+    no_device_error(cuda_dev)
+
+
+def test_tc_varlen_packed_causal(cuda_dev):
+    """Packed varlen (attn_varlen, causal windows) routed to the tensor cores."""
+    from wavefront_decoding_b200 import attention as wa
+    g = gi.gen(77)
+    q_lens, k_lens = [8, 1, 8, 5], [700, 90, 8, 300]
+    q = gi.randn((sum(q_lens), 16, 128), g, torch.bfloat16)
+    k = gi.randn((sum(k_lens), 4, 128), g, torch.bfloat16)
+    v = gi.randn((sum(k_lens), 4, 128), g, torch.bfloat16)
+    cu_q = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]), dtype=torch.int32)
+    cu_k = torch.tensor(np.concatenate([[0], np.cumsum(k_lens)]), dtype=torch.int32)
+    ref = oattn.attn_varlen(q, k, v, cu_q, cu_k, causal=True)
+    out = wa.attn_varlen(q.to(cuda_dev), k.to(cuda_dev), v.to(cuda_dev), cu_q.to(cuda_dev), cu_k.to(cuda_dev), 8,
+                         max(k_lens), causal=True)
+    no_device_error(cuda_dev)
+    assert maxdiff(out, ref) < TOL_BF16

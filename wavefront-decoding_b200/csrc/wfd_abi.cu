@@ -128,6 +128,62 @@ int launch_decode(int dtype, int dh, int nq, const DecodeParams& p, int sms, cud
   return WFD_ERR_UNSUPPORTED;
 }
 
+// ---- tensor maps for the tcgen05 kernel (driver entry point, no -lcuda) ----
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// (Dh=128, Hkv, rows) bf16 key / value buffer; box = 64 dims x 1 head x 128 rows,
+// 128-byte swizzle (the UMMA SWIZZLE_128B layout); rows past the end read as 0.
+bool make_kv_map(CUtensorMap* m, const void* base, long long rows, int Hkv) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {128, (cuuint64_t)Hkv, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {128 * 2, (cuuint64_t)Hkv * 128 * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)kTcTile};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NQP>
+int launch_tc(const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& tv, int sms, cudaStream_t st) {
+  using C = TcCfg<NQP>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(wave_tc_kernel<NQP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
+      return WFD_ERR_CUDA;
+    attr_set[dev] = true;
+  }
+  wave_tc_kernel<NQP><<<sms, kTcThreads, C::SMEM, st>>>(tk, tv, vp);
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+int launch_verify(int nqp, const VerifyParams& vp, const void* k, const void* v, long long rows, int Hkv, int sms,
+                  cudaStream_t st) {
+  if (rows <= 0 || rows >= (1ll << 31)) return WFD_ERR_UNSUPPORTED;  // TMA row coordinates are int32
+  CUtensorMap tk, tv;
+  if (!make_kv_map(&tk, k, rows, Hkv) || !make_kv_map(&tv, v, rows, Hkv)) return WFD_ERR_CUDA;
+  return nqp == 16 ? launch_tc<16>(vp, tk, tv, sms, st) : launch_tc<32>(vp, tk, tv, sms, st);
+}
+
 // Common core of every attention entry point: plan, then attend.
 struct AttnArgs {
   int mode;
@@ -148,7 +204,8 @@ struct AttnArgs {
   void* ws;
   size_t ws_bytes;
   int* err;
-  int which;  // -1 auto, 0 decode kernel, 1 verify kernel
+  int which;           // -1 auto, 0 decode kernel, 1 verify kernel
+  long long key_rows;  // rows of (Hkv * Dh) elements in k / v (tensor-map extent)
 };
 
 int run_attention(const AttnArgs& A, cudaStream_t st) {
@@ -169,8 +226,12 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
 
   const int max_q = A.max_q < 1 ? 1 : A.max_q;
   int which = A.which;
-  if (which < 0) which = (max_q >= kVerifyMinRows && verify_supported(A.dtype, A.Dh, G, max_q)) ? 1 : 0;
-  if (which == 1 && !verify_supported(A.dtype, A.Dh, G, max_q)) return WFD_ERR_UNSUPPORTED;
+  const bool tc_ok = verify_supported(A.dtype, A.Dh, G, max_q) && A.key_rows > 0 && A.key_rows < (1ll << 31);
+  // bf16 / Dh=128 runs on the tensor cores for decode rows too: measured on
+  // B200 (config 2) the CUDA-core kernel is issue-bound at 54 % of HBM peak,
+  // the tcgen05 kernel reaches 68 %.  fp32 and Dh=64 stay on the CUDA cores.
+  if (which < 0) which = tc_ok ? 1 : 0;
+  if (which == 1 && !tc_ok) return WFD_ERR_UNSUPPORTED;
 
   int NQ;
   if (which == 0) {
@@ -200,7 +261,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   pp.s_k_len = A.s_k_len;
   pp.G = G;
   pp.NQ = NQ;
-  pp.qg_split = which == 0 ? 1 : 0;
+  pp.qg_split = 1;
   pp.segs = reinterpret_cast<Seg*>(ws + L.segs);
   pp.prefix = reinterpret_cast<long long*>(ws + L.prefix);
   pp.out = A.out;
@@ -215,17 +276,20 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   const float log2e = 1.4426950408889634f;
 
   if (which == 1) {
+    const long long k_row_offset = (long long)A.slot_offset * A.n_seqs * (long long)A.max_seq;
+    if (A.k_new != nullptr && A.k_app != nullptr) {
+      // the tensor-core kernel reads every key through TMA: append the window
+      // rows to the cache first (same stream, so the attention sees them)
+      append_segs_kernel<<<A.n, 256, 0, st>>>(pp.segs, A.n, static_cast<const char*>(A.k_new),
+                                              static_cast<const char*>(A.v_new), static_cast<char*>(A.k_app),
+                                              static_cast<char*>(A.v_app), (long long)A.Hkv * A.Dh * 2,
+                                              k_row_offset, A.lens, A.slot_offset * A.n_seqs);
+      if (cudaGetLastError() != cudaSuccess) return WFD_ERR_CUDA;
+    }
     VerifyParams vp;
     memset(&vp, 0, sizeof(vp));
     vp.q = A.q;
-    vp.k = A.k;
-    vp.v = A.v;
-    vp.k_new = A.k_new;
-    vp.v_new = A.v_new;
-    vp.k_app = A.k_app;
-    vp.v_app = A.v_app;
     vp.out = A.out;
-    vp.lens = A.lens;
     vp.segs = pp.segs;
     vp.prefix = pp.prefix;
     vp.n_segs = A.n;
@@ -234,12 +298,11 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     vp.G = G;
     vp.scale_log2 = scale * log2e;
     vp.causal = A.causal;
-    vp.k_row_offset = (long long)A.slot_offset * A.n_seqs * (long long)A.max_seq;
-    vp.lens_offset = A.slot_offset * A.n_seqs;
+    vp.k_row_offset = k_row_offset;
     vp.ws_part = reinterpret_cast<float*>(ws + L.part);
     vp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
     vp.err = A.err;
-    return launch_verify(A.dtype, A.Dh, NQ, vp, sms, st);
+    return launch_verify(NQ, vp, A.k, A.v, A.key_rows, A.Hkv, sms, st);
   }
 
   DecodeParams dp;
@@ -309,6 +372,7 @@ int wave_common(int which, const void* q, const void* k_new, const void* v_new, 
   A.ws_bytes = workspace_bytes;
   A.err = d_err;
   A.which = which;
+  A.key_rows = (long long)n_slots * n_seqs * (long long)max_seq;
   return run_attention(A, static_cast<cudaStream_t>(stream));
 }
 
@@ -424,6 +488,7 @@ int wfd_attn_varlen(const void* q, const void* k, const void* v, void* out, cons
   A.ws_bytes = workspace_bytes;
   A.err = d_err;
   A.which = -1;
+  A.key_rows = total_k;
   return run_attention(A, static_cast<cudaStream_t>(stream));
 }
 
@@ -458,6 +523,7 @@ int wfd_attn_segments(const void* q, const void* k, const void* v, void* out, co
   A.ws_bytes = workspace_bytes;
   A.err = d_err;
   A.which = -1;
+  A.key_rows = total_k;
   return run_attention(A, static_cast<cudaStream_t>(stream));
 }
 

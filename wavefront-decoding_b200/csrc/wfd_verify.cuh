@@ -1,24 +1,45 @@
-// K2 — wavefront verify attention on tcgen05 tensor cores (sm_100a).
-// (Interface only in this revision; the kernel body lands with the tcgen05 path.)
+// K2 — wavefront verify / decode attention on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA, sm_100a), bf16 inputs, Dh = 128.
+//
+// Swap-AB formulation: per 128-key tile of one (segment, query group, kv head)
+// unit
+//     S^T[128 keys x N]  = K_tile[128 x 128] . Q^T           (A = K, K-major)
+//     O^T[128 dims x N] += V_tile^T[128 x 128 keys] . P^T     (A = V, MN-major)
+// where N = NQP (16 or 32) >= the unit's query vectors (window rows x GQA
+// group): the tensor core's M = 128 dimension runs over keys (then over head
+// dims), so a handful of query rows still fill the instruction.  Accumulators
+// live in TMEM; each of the four softmax warps owns one 32-lane TMEM quadrant
+// (= 32 keys of S^T, then 32 head dims of O^T).
+//
+// Warp roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: K and V tiles (2 boxes of 64 dims each, 128B
+//               swizzle) into a STAGES-deep ring, mbarrier complete_tx
+//   warp 1      TMEM allocator + tcgen05.mma issuer (one lane issues)
+//   warps 2..5  softmax / correction: S^T from TMEM, column maxima across the
+//               128 keys, exp2, P^T (bf16) to shared memory, O^T accumulated
+//               in registers with the online-softmax rescale
+// The persistent grid splits the flattened (segment, query group, kv head,
+// key) space into equal key shares exactly like the CUDA-core kernel; units
+// that straddle CTAs are merged by the last CTA to arrive.  Every wait is
+// bounded and reports through the error word; no multicast, no cluster launch.
+//
+// Window keys are read from the KV cache: the caller appends the window rows
+// (append_segs_kernel) in a launch before this one.
 #pragma once
+
+#include <cuda.h>
 
 #include "wfd_common.cuh"
 
 namespace wfd {
 
-constexpr int kVerifyMinRows = 8;   // window rows from which the tensor-core kernel is preferred
-constexpr int kVerifyMaxRows = 64;  // query vectors (window rows x GQA group) per unit
+constexpr int kVerifyMaxRows = 32;  // query vectors per unit (larger windows -> query groups)
+constexpr int kTcTile = 128;        // keys per tile == MMA M
+constexpr int kTcThreads = 192;
 
 struct VerifyParams {
   const void* q;
-  const void* k;
-  const void* v;
-  const void* k_new;
-  const void* v_new;
-  void* k_app;
-  void* v_app;
   void* out;
-  int32_t* lens;
   const Seg* segs;
   const long long* prefix;
   int n_segs;
@@ -26,17 +47,592 @@ struct VerifyParams {
   float scale_log2;
   int causal;
   long long k_row_offset;
-  int lens_offset;
   float* ws_part;
   int* ws_cnt;
   int* err;
 };
 
+template <int NQP>
+struct TcCfg {
+  static constexpr int STAGES = 3;
+  static constexpr int BOX_BYTES = kTcTile * 128;          // 128 rows x 64 bf16
+  static constexpr int KV_STAGE = 4 * BOX_BYTES;           // K box0, K box1, V box0, V box1
+  static constexpr int Q_BYTES = NQP * 256;                // 2 boxes of NQP rows x 128 B
+  static constexpr int P_ROWB = NQP * 2;                   // one key row of P^T
+  static constexpr int P_BYTES = kTcTile * P_ROWB;
+  static constexpr int P_SWZ_BITS = NQP == 16 ? 1 : 2;     // Swizzle<1,4,3> (32B) / <2,4,3> (64B)
+  static constexpr uint64_t P_LAYOUT = NQP == 16 ? 6 : 4;  // UMMA layout SWIZZLE_32B / SWIZZLE_64B
+  static constexpr int P_ATOM = 8 * P_ROWB;                // 8 key rows
+  static constexpr int RED_FLOATS = 2 * 4 * NQP;           // double-buffered per-warp column values
+  static constexpr int SMEM = STAGES * KV_STAGE + Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + 1024;
+  static constexpr int TMEM_COLS = NQP == 16 ? 64 : 128;   // S (x2) and O accumulators
+  static constexpr int PART_FLOATS = NQP * (128 + 2);
+  static_assert(NQP == 16 || NQP == 32, "N of the swap-AB MMA");
+};
+
+// Any window size runs on the tensor cores: more than kVerifyMaxRows query
+// vectors per kv head are split into query groups (K/V re-read per group).
 inline bool verify_supported(int dtype, int dh, int G, int max_q) {
-  (void)dtype; (void)dh; (void)G; (void)max_q;
-  return false;
+  (void)G;
+  (void)max_q;
+  return dtype == WFD_DTYPE_BF16 && dh == 128;
 }
-inline int verify_rows(int G, int max_q) { return G * max_q; }
-inline int launch_verify(int, int, int, const VerifyParams&, int, cudaStream_t) { return WFD_ERR_UNSUPPORTED; }
+inline int verify_rows(int G, int max_q) { return (long long)G * max_q <= 16 ? 16 : 32; }
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMA primitives (inline PTX)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (sm_100 UMMA): start, leading / stride byte
+// offsets (16-byte units), descriptor version 1, swizzle layout code.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint64_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= layout << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 x bf16 -> f32, M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc(int n, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// 32 TMEM lanes x 32-bit, N consecutive columns -> N registers per thread
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]);
+
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Bounded mbarrier wait by every lane of a warp, with a warp-uniform result.
+// It gives up at the spin limit (setting the error word and the CTA abort
+// flag) or as soon as another role has aborted.  After an abort the roles keep
+// their control flow (same loop trips, same named barriers) but issue no more
+// TMA or MMA work, so nothing in the CTA can block without a bound.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  bool ok = false;
+  if (!*abort_flag) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+      if (mbar_try_wait(bar, parity)) {
+        ok = true;
+        break;
+      }
+      if ((i & 255u) == 255u && *abort_flag) break;
+    }
+    if (!ok && !*abort_flag) {
+      set_error(err, kErrTimeout);
+      *abort_flag = 1;
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Column reduction (max or sum) of the N values each of the 32 lanes holds:
+// butterfly reduce-scatter; lane l ends with column bitrev(l mod N) reduced
+// over all 32 lanes.  Destroys w.
+template <int N, bool IS_MAX>
+__device__ __forceinline__ float warp_col_reduce(float (&w)[N], int lane) {
+#pragma unroll
+  for (int l = 0; (N >> l) > 1; ++l) {
+    const int H = (N >> l) >> 1;
+    const bool up = (lane >> l) & 1;
+#pragma unroll
+    for (int i = 0; i < (N >> 1); ++i) {
+      if (i < H) {
+        const float send = up ? w[i] : w[i + H];
+        const float keep = up ? w[i + H] : w[i];
+        const float got = __shfl_xor_sync(0xffffffffu, send, 1 << l);
+        w[i] = IS_MAX ? fmaxf(keep, got) : keep + got;
+      }
+    }
+  }
+  float r = w[0];
+  constexpr int LOGN = N == 16 ? 4 : 5;
+#pragma unroll
+  for (int l = LOGN; l < 5; ++l) {
+    const float got = __shfl_xor_sync(0xffffffffu, r, 1 << l);
+    r = IS_MAX ? fmaxf(r, got) : r + got;
+  }
+  return r;
+}
+
+template <int N>
+__device__ __forceinline__ int reduced_col(int lane) {
+  constexpr int LOGN = N == 16 ? 4 : 5;
+  return (int)(__brev((unsigned)(lane & (N - 1))) >> (32 - LOGN));
+}
+
+// The (segment, unit, key range) pieces of one CTA's share, in order; every
+// role walks the same sequence.
+struct UnitIter {
+  long long pos, b;
+  int seg;
+  __device__ __forceinline__ bool next(const VerifyParams& p, Seg& S, int& u, int& r_lo, int& r_hi,
+                                       long long& unit_start) {
+    if (pos >= b) return false;
+    while (seg + 1 <= p.n_segs - 1 && (long long)p.Hkv * p.prefix[seg + 1] <= pos) ++seg;
+    S = p.segs[seg];
+    const long long seg_base = (long long)p.Hkv * p.prefix[seg];
+    const long long o = pos - seg_base;
+    u = (int)(o / S.k_len);
+    r_lo = (int)(o - (long long)u * S.k_len);
+    unit_start = seg_base + (long long)u * S.k_len;
+    const long long unit_end = unit_start + S.k_len;
+    r_hi = (int)(((unit_end < b) ? unit_end : b) - unit_start);
+    pos = unit_start + r_hi;
+    return true;
+  }
+};
+
+template <int NQP>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    wave_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                   const VerifyParams p) {
+  using C = TcCfg<NQP>;
+  constexpr int STAGES = C::STAGES;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* kvs = smem;                               // STAGES x (K0 K1 V0 V1)
+  unsigned char* qs = kvs + STAGES * C::KV_STAGE;          // Q^T operand (K-major, SW128)
+  unsigned char* ps = qs + C::Q_BYTES;                     // P^T operand (MN-major)
+  float* red = reinterpret_cast<float*>(ps + C::P_BYTES);  // [2][4][NQP] column maxima
+  float* lred = red + C::RED_FLOATS;                       // [2][4][NQP] column sums
+
+  __shared__ __align__(8) uint64_t bar_full[STAGES];
+  __shared__ __align__(8) uint64_t bar_empty[STAGES];
+  __shared__ __align__(8) uint64_t bar_sfull[2];
+  __shared__ __align__(8) uint64_t bar_sfree[2];
+  __shared__ __align__(8) uint64_t bar_pfull;
+  __shared__ __align__(8) uint64_t bar_ofull;
+  __shared__ __align__(8) uint64_t bar_ofree;
+  __shared__ __align__(8) uint64_t bar_qready;
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_abort;
+  __shared__ int s_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar_sfull[s], 1);
+      mbar_init(&bar_sfree[s], 4);
+    }
+    mbar_init(&bar_pfull, 1);
+    mbar_init(&bar_ofull, 1);
+    mbar_init(&bar_ofree, 4);
+    mbar_init(&bar_qready, 1);
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  const long long total = (long long)p.Hkv * p.prefix[p.n_segs];
+  long long share = 1, a = 0, b = 0;
+  if (total > 0) {
+    share = (total + gridDim.x - 1) / gridDim.x;
+    a = (long long)blockIdx.x * share;
+    b = (a + share < total) ? a + share : total;
+  }
+  int seg0 = 0;
+  if (a < b) {
+    int lo = 0, hi = p.n_segs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if ((long long)p.Hkv * p.prefix[mid] <= a) lo = mid;
+      else hi = mid - 1;
+    }
+    seg0 = lo;
+  }
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    UnitIter itr{a, b, seg0};
+    Seg S;
+    int u, r_lo, r_hi;
+    long long ustart;
+    uint32_t it = 0;
+    while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
+      const int h = u % p.Hkv;
+      const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
+      const long long row0 = S.k_row0 + p.k_row_offset + r_lo;
+      for (int t = 0; t < n_t; ++t, ++it) {
+        const int stage = (int)(it % STAGES);
+        const bool go = (it >= (uint32_t)STAGES) ? tc_wait(&bar_empty[stage], ((it / STAGES) - 1) & 1u, &s_abort, p.err)
+                                                 : !s_abort;
+        if (go && lane == 0) {
+          unsigned char* dst = kvs + stage * C::KV_STAGE;
+          const int row = (int)(row0 + (long long)t * kTcTile);
+          mbar_arrive_expect_tx(&bar_full[stage], (uint32_t)C::KV_STAGE);
+          tma_load_3d(dst, &tm_k, 0, h, row, &bar_full[stage]);
+          tma_load_3d(dst + C::BOX_BYTES, &tm_k, 64, h, row, &bar_full[stage]);
+          tma_load_3d(dst + 2 * C::BOX_BYTES, &tm_v, 0, h, row, &bar_full[stage]);
+          tma_load_3d(dst + 3 * C::BOX_BYTES, &tm_v, 64, h, row, &bar_full[stage]);
+        }
+        __syncwarp();
+      }
+    }
+    // the MMA warp's last commits arrive on these barriers: see them land
+    // before this CTA may exit
+    const uint32_t n_used = it;
+    for (uint32_t j = (n_used > (uint32_t)STAGES ? n_used - STAGES : 0); j < n_used; ++j)
+      tc_wait(&bar_empty[j % STAGES], (j / STAGES) & 1u, &s_abort, p.err);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    UnitIter itr{a, b, seg0};
+    Seg S;
+    int u, r_lo, r_hi;
+    long long ustart;
+    uint32_t it = 0, pv = 0, units = 0;
+    constexpr uint32_t IDESC_S = umma_idesc(NQP, false, false);
+    constexpr uint32_t IDESC_PV = umma_idesc(NQP, true, true);
+    const uint32_t q_addr = smem_u32(qs);
+    const uint32_t p_addr = smem_u32(ps);
+    while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
+      const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
+      tc_wait(&bar_qready, units & 1u, &s_abort, p.err);
+      tc_fence_after();
+      for (int t = 0; t <= n_t; ++t) {
+        if (t < n_t) {
+          const uint32_t ti = it + t;
+          const int stage = (int)(ti % STAGES);
+          const int sb = (int)(ti & 1u);
+          bool go = tc_wait(&bar_full[stage], (ti / STAGES) & 1u, &s_abort, p.err);
+          if (ti >= 2) go = tc_wait(&bar_sfree[sb], ((ti >> 1) - 1) & 1u, &s_abort, p.err) && go;
+          tc_fence_after();
+          if (go && lane == 0) {
+            const uint32_t k_addr = smem_u32(kvs + stage * C::KV_STAGE);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              // K step j: dims 16j..16j+15 = box j/4, byte 32*(j%4) inside the 128B row
+              const uint32_t koff = (uint32_t)((j >> 2) * C::BOX_BYTES + (j & 3) * 32);
+              const uint32_t qoff = (uint32_t)((j >> 2) * (NQP * 128) + (j & 3) * 32);
+              umma_f16(tmem + (uint32_t)(sb * NQP), umma_desc(k_addr + koff, 16, 1024, 2),
+                       umma_desc(q_addr + qoff, 16, 1024, 2), IDESC_S, j > 0 ? 1u : 0u);
+            }
+            umma_commit(&bar_sfull[sb]);
+          }
+          __syncwarp();
+        }
+        if (t >= 1) {
+          bool go = tc_wait(&bar_pfull, pv & 1u, &s_abort, p.err);
+          if (pv >= 1) go = tc_wait(&bar_ofree, (pv - 1) & 1u, &s_abort, p.err) && go;
+          tc_fence_after();
+          const uint32_t tp = it + t - 1;
+          const int stage = (int)(tp % STAGES);
+          if (go && lane == 0) {
+            const uint32_t v_addr = smem_u32(kvs + stage * C::KV_STAGE + 2 * C::BOX_BYTES);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              // K step j: keys 16j..16j+15 = two 8-row groups of both V boxes / of P^T
+              umma_f16(tmem + (uint32_t)(2 * NQP), umma_desc(v_addr + j * 2048, C::BOX_BYTES, 1024, 2),
+                       umma_desc(p_addr + j * 2 * C::P_ATOM, 16, C::P_ATOM, C::P_LAYOUT), IDESC_PV,
+                       j > 0 ? 1u : 0u);
+            }
+            umma_commit(&bar_ofull);
+            umma_commit(&bar_empty[stage]);
+          }
+          __syncwarp();
+          ++pv;
+        }
+      }
+      it += n_t;
+      ++units;
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int sw = warp - 2;            // 0..3
+    const int qd = warp & 3;            // TMEM lane quadrant this warp may access
+    const int stid = tid - 64;          // 0..127 within the softmax group
+    const int my_row = qd * 32 + lane;  // key row of S^T, then head dim of O^T, this thread owns
+    const uint32_t tq = tmem + ((uint32_t)(qd * 32) << 16);
+    UnitIter itr{a, b, seg0};
+    Seg S;
+    int u, r_lo, r_hi;
+    long long ustart;
+    uint32_t it = 0, pv = 0, units = 0;
+    constexpr int PCH = NQP / 8;  // 16-byte chunks per P^T row
+    while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
+      const int h = u % p.Hkv, qg = u / p.Hkv;
+      const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
+      const int nvec = S.q_len * p.G - qg * NQP;  // query vectors of this group (may exceed NQP)
+      // ---- Q^T operand: row n = query vector qg*NQP + n
+      for (int c = stid; c < NQP * 16; c += 128) {
+        const int n = c >> 4, ch = c & 15;
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (n < nvec) {
+          const int v = qg * NQP + n;
+          const int row = v / p.G, g = v % p.G;
+          val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
+                         ((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * 128 + ch * 8);
+        }
+        const int box = ch >> 3, cc = ch & 7;
+        const uint32_t off = (uint32_t)(box * NQP * 128 + n * 128 + ((cc ^ (n & 7)) << 4));
+        *reinterpret_cast<uint4*>(qs + off) = val;
+      }
+      fence_async_smem();
+      softmax_bar();
+      if (stid == 0) mbar_arrive(&bar_qready);
+
+      float m[NQP], lp[NQP], oacc[NQP];
+#pragma unroll
+      for (int n = 0; n < NQP; ++n) {
+        m[n] = NEG_INF;
+        lp[n] = 0.f;
+        oacc[n] = 0.f;
+      }
+      for (int t = 0; t < n_t; ++t) {
+        const uint32_t ti = it + t;
+        const int sb = (int)(ti & 1u);
+        tc_wait(&bar_sfull[sb], (ti >> 1) & 1u, &s_abort, p.err);
+        tc_fence_after();
+        float s[NQP];
+        tmem_ld<NQP>(tq + (uint32_t)(sb * NQP), s);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_sfree[sb]);
+
+        const int key = r_lo + t * kTcTile + my_row;  // key index inside the unit
+        const bool kvalid = key < r_hi;
+#pragma unroll
+        for (int n = 0; n < NQP; ++n) {
+          const int v = qg * NQP + n;
+          const int lim = (n < nvec) ? (p.causal ? S.k_len - S.q_len + v / p.G : S.k_len - 1) : -1;
+          s[n] = (kvalid && key <= lim) ? s[n] * p.scale_log2 : NEG_INF;
+        }
+        // column maxima over the tile's 128 keys
+        float* rb = red + (ti & 1u) * (4 * NQP);
+        {
+          float w[NQP];
+#pragma unroll
+          for (int n = 0; n < NQP; ++n) w[n] = s[n];
+          const float r = warp_col_reduce<NQP, true>(w, lane);
+          if (lane < NQP) rb[sw * NQP + reduced_col<NQP>(lane)] = r;
+        }
+        softmax_bar();
+        const int stage = (int)(ti % STAGES);
+        if (!kvalid) {
+          // rows past the unit may hold anything (even NaN): zero this key's V row
+          unsigned char* vrow = kvs + stage * C::KV_STAGE + 2 * C::BOX_BYTES + my_row * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(vrow + C::BOX_BYTES + c * 16) = make_uint4(0, 0, 0, 0);
+          }
+        }
+        // the previous tile's P.V: its MMA is done once o_full fires, which also
+        // frees the P^T buffer.  oacc holds O_{t-2} already rescaled to m_{t-1}.
+        if (t >= 1) {
+          tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err);
+          tc_fence_after();
+          float o[NQP];
+          tmem_ld<NQP>(tq + (uint32_t)(2 * NQP), o);
+          tc_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_ofree);
+          ++pv;
+#pragma unroll
+          for (int n = 0; n < NQP; ++n) oacc[n] += o[n];
+        }
+        // online softmax update for this tile; P^T row of this key (bf16, swizzled)
+#pragma unroll
+        for (int c = 0; c < PCH; ++c) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float pr2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int n = c * 8 + 2 * i + e;
+              const float tm = fmaxf(fmaxf(rb[n], rb[NQP + n]), fmaxf(rb[2 * NQP + n], rb[3 * NQP + n]));
+              const float mn = fmaxf(m[n], tm);
+              const float alpha = (mn == NEG_INF) ? 1.f : fast_exp2(m[n] - mn);
+              pr2[e] = (s[n] == NEG_INF) ? 0.f : fast_exp2(s[n] - mn);
+              lp[n] = lp[n] * alpha + pr2[e];
+              oacc[n] *= alpha;
+              m[n] = mn;
+            }
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(pr2[0], pr2[1]);
+            w4[i] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          uint32_t off = (uint32_t)(my_row * C::P_ROWB + c * 16);
+          off ^= ((off >> 7) & ((1u << C::P_SWZ_BITS) - 1u)) << 4;
+          *reinterpret_cast<uint4*>(ps + off) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+        fence_async_smem();
+        softmax_bar();
+        if (stid == 0) mbar_arrive(&bar_pfull);
+      }
+      {
+        tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err);
+        tc_fence_after();
+        float o[NQP];
+        tmem_ld<NQP>(tq + (uint32_t)(2 * NQP), o);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_ofree);
+        ++pv;
+#pragma unroll
+        for (int n = 0; n < NQP; ++n) oacc[n] += o[n];
+      }
+      it += n_t;
+      ++units;
+
+      // ---- column sums of the unnormalised probabilities over the 128 threads
+      float* lb = lred + (units & 1u) * (4 * NQP);
+      {
+        float w[NQP];
+#pragma unroll
+        for (int n = 0; n < NQP; ++n) w[n] = lp[n];
+        const float r = warp_col_reduce<NQP, false>(w, lane);
+        if (lane < NQP) lb[sw * NQP + reduced_col<NQP>(lane)] = r;
+      }
+      softmax_bar();
+
+      const int c_first = (int)(ustart / share);
+      const int c_last = (int)((ustart + S.k_len - 1) / share);
+      const int n_contrib = c_last - c_first + 1;
+      const int dim = my_row;  // O^T TMEM lane == head dim
+      if (n_contrib == 1) {
+#pragma unroll
+        for (int n = 0; n < NQP; ++n) {
+          if (n < nvec) {
+            const float L = lb[n] + lb[NQP + n] + lb[2 * NQP + n] + lb[3 * NQP + n];
+            const int v = qg * NQP + n;
+            const int row = v / p.G, g = v % p.G;
+            static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * 128 + dim] =
+                __float2bfloat16_rn(L > 0.f ? oacc[n] / L : 0.f);
+          }
+        }
+      } else {
+        const int slot = (ustart < a) ? 2 * (int)blockIdx.x : 2 * (int)blockIdx.x + 1;
+        float* pb = p.ws_part + (size_t)slot * C::PART_FLOATS;
+        // every thread holds the same m[]; thread n publishes column n's (m, l)
+#pragma unroll
+        for (int n = 0; n < NQP; ++n) {
+          if (stid == n) {
+            pb[n] = m[n];
+            pb[NQP + n] = lb[n] + lb[NQP + n] + lb[2 * NQP + n] + lb[3 * NQP + n];
+          }
+          pb[2 * NQP + n * 128 + dim] = oacc[n];
+        }
+        __threadfence();
+        softmax_bar();
+        if (stid == 0) {
+          const int prev = atomicAdd(p.ws_cnt + c_first, 1);
+          s_flag = (prev == n_contrib - 1) ? 1 : 0;
+        }
+        softmax_bar();
+        if (s_flag) {
+          __threadfence();
+          for (int n = 0; n < nvec && n < NQP; ++n) {
+            float M = NEG_INF;
+            for (int k = 0; k < n_contrib; ++k) {
+              const int cc = c_first + k;
+              const int sl = (k == 0) ? 2 * cc + 1 : 2 * cc;
+              M = fmaxf(M, ld_cg_f32(p.ws_part + (size_t)sl * C::PART_FLOATS + n));
+            }
+            float Ls = 0.f, acc = 0.f;
+            for (int k = 0; k < n_contrib; ++k) {
+              const int cc = c_first + k;
+              const int sl = (k == 0) ? 2 * cc + 1 : 2 * cc;
+              const float* base = p.ws_part + (size_t)sl * C::PART_FLOATS;
+              const float mk = ld_cg_f32(base + n);
+              const float wgt = (mk == NEG_INF) ? 0.f : fast_exp2(mk - M);
+              Ls += wgt * ld_cg_f32(base + NQP + n);
+              acc += wgt * ld_cg_f32(base + 2 * NQP + n * 128 + dim);
+            }
+            const int v = qg * NQP + n;
+            const int row = v / p.G, g = v % p.G;
+            static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * 128 + dim] =
+                __float2bfloat16_rn(Ls > 0.f ? acc / Ls : 0.f);
+          }
+          if (stid == 0) p.ws_cnt[c_first] = 0;
+        }
+        softmax_bar();  // s_flag is re-written by the next unit
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
+  }
+}
 
 }  // namespace wfd
