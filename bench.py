@@ -1,20 +1,27 @@
 #!/usr/bin/env python
-"""Benchmark: wavefront decode attention, BASELINE config 2, on B200.
+"""Benchmark: wavefront decode / verify attention on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wfd|reference]
+                    [--workload cfg2|cfg3] [--kernel -1|0|1]
 
-One step = one wavefront decode tick of the isolated attention op: B=8
-sequences x R=8 loop-depth slots, Hq=16 / Hkv=4 (GQA 4:1), Dh=128, bf16; slot r
-holds L_r = 4096 - r positions and gets one query (the new row is appended and
-attended in the same launch).  Q, K, V ~ N(0,1) from torch CPU seed 1 (draw
-order q, K, V), synthetic.  The KV working set (537 MB) is larger than L2
-(126 MB), so no L2 flush is needed between steps.
+Default workload: one step = one wavefront decode tick of
+the isolated attention op: B=8 sequences x R=8 loop-depth slots, Hq=16 / Hkv=4
+(GQA 4:1), Dh=128, bf16; slot r holds L_r = 4096 - r positions and gets one
+query (the new row is appended and attended in the same step).  Q, K, V ~
+N(0,1) from torch CPU seed 1 (draw order q, K, V), synthetic.  The KV working
+set (537 MB) is larger than L2 (126 MB), so no L2 flush is needed.
+
+--workload cfg3: verify + commit.  B=32 (or --batch),
+R=8, Hq=32 / Hkv=8, Dh=128, bf16; slot r holds 8192 - r positions and gets an
+8-row causal draft window; a step is the fused append + verify attention and
+the accept commit (per-sequence accepted lengths U{0..8}, seed 3).  Q, K, V
+~ N(0,1) drawn on the device from seed 2 (8.6 GB of KV does not fit a CPU draw).
 
 value : algorithmic KV-read GB/s with every input resident in HBM (one CUDA
-        graph per step: planner + decode kernel), max time over ranks.
-e2e   : the same metric through the public Python/C-ABI call with host buffers:
-        every step copies q, the new K/V rows and the item table from pinned
-        host memory and reads the output back.
+        graph per step), max time over ranks.
+e2e   : the same metric through the public Python / C-ABI call with host
+        buffers: every step copies q, the new K/V rows and the item table from
+        pinned host memory and reads the output back.
 Multi-GPU (torchrun): every rank runs its own independent batch (weak scaling);
 the only collectives are the timing max and a final counter gather.
 --impl reference: the reference's CPU path (write_tokens + gather_pack + SDPA
@@ -25,7 +32,6 @@ from __future__ import annotations
 import argparse
 import datetime
 import json
-import math
 import os
 import pathlib
 import statistics
@@ -41,11 +47,12 @@ UNIT = "GB/s"
 FALLBACK_HBM_GBS = 6650.0
 
 CFG2 = dict(B=8, R=8, H=16, Hkv=4, Dh=128, S=4096, seed=1)
+CFG3 = dict(B=32, R=8, H=32, Hkv=8, Dh=128, L0=8192, W=8, seed=2, accept_seed=3)
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # timed attention kernel, from the ncu captures summarised under profiles/
 # (wave_decode_cfg2.md for the CUDA-core kernel, wave_tc_cfg2.md for tcgen05).
-NCU_TRAFFIC_BYTES = {"cuda_core": 537_539_072 + 5_969_920, "tc": None}
+NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920}
 
 
 def parse():
@@ -54,6 +61,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=4000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (default: the config's)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", type=int, default=-1, choices=[-1, 0, 1],
@@ -70,9 +79,22 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def cfg2_cpu_inputs(seed: int):
+def algorithmic_bytes(items, H, Hkv, Dh, elem=2):
+    kv = sum((p0 + ql) for _, _, p0, ql, _ in items) * Hkv * Dh * elem * 2   # every key row read once per kv head
+    rows = sum(it[3] for it in items)
+    qo = 2 * rows * H * Dh * elem                                             # q in, out
+    app = rows * Hkv * Dh * elem * 2                                          # appended K/V rows written
+    return kv + qo + app, rows
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def cfg2_cpu_inputs(seed: int, batch: int | None = None):
     import torch
-    c = CFG2
+    c = dict(CFG2)
+    if batch:
+        c["B"] = batch
     g = torch.Generator().manual_seed(seed)
     q = torch.randn((c["B"], c["R"], c["H"], c["Dh"]), generator=g).to(torch.bfloat16)
     K = torch.randn((c["R"], c["B"], c["S"], c["Hkv"], c["Dh"]), generator=g).to(torch.bfloat16)
@@ -81,15 +103,31 @@ def cfg2_cpu_inputs(seed: int):
     q = q.reshape(c["B"] * c["R"], c["H"], c["Dh"])
     kn = torch.stack([K[r, b, p] for r, b, p, _, _ in items])
     vn = torch.stack([V[r, b, p] for r, b, p, _, _ in items])
-    return q, K, V, kn, vn, items
+    return c, q, K, V, kn, vn, items
 
 
-def algorithmic_bytes(items, H, Hkv, Dh, elem=2):
-    kv = sum((p0 + ql) for _, _, p0, ql, _ in items) * Hkv * Dh * elem * 2   # every key row read once per kv head
-    rows = sum(it[3] for it in items)
-    qo = 2 * rows * H * Dh * elem                                             # q in, out
-    app = rows * Hkv * Dh * elem * 2                                          # appended K/V rows written
-    return kv + qo + app, rows
+def cfg3_device_inputs(dev, seed: int, batch: int | None = None):
+    import torch
+    c = dict(CFG3)
+    if batch:
+        c["B"] = batch
+    B, R, H, Hkv, Dh, L0, W = c["B"], c["R"], c["H"], c["Hkv"], c["Dh"], c["L0"], c["W"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn((B, R, W, H, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    K = torch.randn((R, B, L0 + W, Hkv, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    V = torch.randn((R, B, L0 + W, Hkv, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    items = [[r, b, L0 - r, W, (b * R + r) * W] for b in range(B) for r in range(R)]
+    q = q.reshape(B * R * W, H, Dh)
+    # the window rows are the rows already drawn at those positions, so every
+    # repetition of the step appends identical data
+    idx_r = torch.tensor([r for r, b, p, w, _ in items for j in range(w)], device=dev)
+    idx_b = torch.tensor([b for r, b, p, w, _ in items for j in range(w)], device=dev)
+    idx_p = torch.tensor([p + j for r, b, p, w, _ in items for j in range(w)], device=dev)
+    kn = K[idx_r, idx_b, idx_p].contiguous()
+    vn = V[idx_r, idx_b, idx_p].contiguous()
+    accept = torch.randint(0, 9, (32,), generator=torch.Generator().manual_seed(c["accept_seed"]))
+    acc_items = torch.tensor([int(accept[b % 32]) for r, b, p, w, _ in items], dtype=torch.int32, device=dev)
+    return c, q, K, V, kn, vn, items, acc_items
 
 
 class ClockSampler:
@@ -146,7 +184,8 @@ class ClockSampler:
                 "power_w_max": max(r["power"] for r in rows)}
 
 
-def cpu_baseline(q, K, V, kn, vn, items, budget_s: float, warmup: int = 1, steps: int | None = None):
+def cpu_baseline(q, K, V, kn, vn, items, budget_s: float, warmup: int = 1, steps: int | None = None,
+                 label: str = "cfg2 decode"):
     """Time the reference's CPU path (oracle/cpu_path.py) on a bounded sample."""
     import torch
     from oracle import cpu_path
@@ -175,9 +214,30 @@ def cpu_baseline(q, K, V, kn, vn, items, budget_s: float, warmup: int = 1, steps
     dt = (time.perf_counter() - t0) / n
     nbytes, rows = algorithmic_bytes(sample, H, Hkv, Dh)
     return {"value": nbytes / dt / 1e9, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{len(sample)} of {len(items)} cfg2 decode rows per step (write_tokens + gather_pack + "
+            "sample": f"{len(sample)} of {len(items)} {label} items per step (write_tokens + gather_pack + "
                       f"SDPA varlen loop, bf16, torch CPU), {n} steps, {dt * 1e3:.1f} ms/step",
             "ms_per_step": dt * 1e3, "host_cpu_count": os.cpu_count()}, n, dt
+
+
+def cfg3_cpu_sample(K, V, q, kn, vn, items, n_items: int = 4):
+    """A few cfg3 items copied to host memory for the CPU baseline."""
+    import torch
+    sel = items[:n_items]
+    Hkv, Dh = K.shape[3], K.shape[4]
+    S = K.shape[2]
+    Kc = torch.empty((1, len(sel), S, Hkv, Dh), dtype=K.dtype)
+    Vc = torch.empty_like(Kc)
+    qs, ks, vs, its = [], [], [], []
+    row = 0
+    for i, (r, b, p0, ql, r0) in enumerate(sel):
+        Kc[0, i] = K[r, b].cpu()
+        Vc[0, i] = V[r, b].cpu()
+        qs.append(q[r0:r0 + ql].cpu())
+        ks.append(kn[r0:r0 + ql].cpu())
+        vs.append(vn[r0:r0 + ql].cpu())
+        its.append([0, i, p0, ql, row])
+        row += ql
+    return Kc, Vc, torch.cat(qs), torch.cat(ks), torch.cat(vs), its
 
 
 def run_reference(args):
@@ -185,18 +245,43 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    q, K, V, kn, vn, items = cfg2_cpu_inputs(CFG2["seed"])
-    base, n, dt = cpu_baseline(q, K, V, kn, vn, items, 90.0, warmup=max(1, args.warmup), steps=max(1, args.steps))
-    c = CFG2
+    if args.workload == "cfg2":
+        c, q, K, V, kn, vn, items = cfg2_cpu_inputs(CFG2["seed"], args.batch)
+        label = "cfg2 decode"
+    else:
+        import torch
+        dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+        if dev is None:
+            print(json.dumps({"impl": "reference", "unavailable": "cfg3 inputs are drawn on the GPU"}))
+            return
+        c, q, K, V, kn, vn, items, _ = cfg3_device_inputs(dev, CFG3["seed"], args.batch)
+        K, V, q, kn, vn, items = cfg3_cpu_sample(K, V, q, kn, vn, items)
+        label = "cfg3 verify"
+    base, n, dt = cpu_baseline(q, K, V, kn, vn, items, 90.0, warmup=max(1, args.warmup), steps=max(1, args.steps),
+                               label=label)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
             "steps": n, "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2_wavefront_decode_attention", "batch": c["B"], "slots": c["R"],
-                       "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "4096-r",
-                       "l2": "KV working set 537 MB > 126 MB L2, no flush"},
+            "config": workload_config(args.workload, c, 1),
             "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def workload_config(name, c, world, rows=None):
+    if name == "cfg2":
+        d = {"workload": "cfg2_wavefront_decode_attention", "batch_per_gpu": c["B"], "slots": c["R"],
+             "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "4096-r",
+             "l2": "KV working set 537 MB > 126 MB L2, no flush"}
+    else:
+        d = {"workload": "cfg3_wavefront_verify_attention_plus_commit", "batch_per_gpu": c["B"], "slots": c["R"],
+             "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "8192-r + 8-row window",
+             "window": c["W"], "l2": "KV working set > 126 MB L2, no flush"}
+    d["parallelism"] = f"sequences sharded, {world} rank(s)"
+    d["timing"] = "CUDA graph replay"
+    if rows is not None:
+        d["rows_per_step_per_gpu"] = rows
+    return d
 
 
 def run_wfd(args):
@@ -215,20 +300,33 @@ def run_wfd(args):
     __graft_entry__.load_package()
     from wavefront_decoding_b200 import attention as wa
     from wavefront_decoding_b200 import runtime as rt
+    from wavefront_decoding_b200.kv_cache import SlotKVCache
 
-    c = CFG2
-    q, K, V, kn, vn, items = cfg2_cpu_inputs(c["seed"] + rank)
-    nbytes, rows = algorithmic_bytes(items, c["H"], c["Hkv"], c["Dh"])
-    qd, Kd, Vd, knd, vnd = q.to(dev), K.to(dev), V.to(dev), kn.to(dev), vn.to(dev)
+    if args.workload == "cfg2":
+        c, q, K, V, kn, vn, items = cfg2_cpu_inputs(CFG2["seed"] + rank, args.batch)
+        qd, Kd, Vd, knd, vnd = q.to(dev), K.to(dev), V.to(dev), kn.to(dev), vn.to(dev)
+        acc = None
+        max_q = 1
+    else:
+        c, qd, Kd, Vd, knd, vnd, items, acc = cfg3_device_inputs(dev, CFG3["seed"] + rank, args.batch)
+        max_q = c["W"]
+        q = kn = vn = K = V = None
+    H, Hkv, Dh = c["H"], c["Hkv"], c["Dh"]
+    nbytes, rows = algorithmic_bytes(items, H, Hkv, Dh)
     items_t = torch.tensor(items, dtype=torch.int32)
     itd = items_t.to(dev)
-    lens = torch.zeros((c["R"], c["B"]), dtype=torch.int32, device=dev)
+    # the cache object owns the slot lengths; its K / V are the workload's tensors
+    cache = SlotKVCache.wrap(Kd, Vd)
     out = torch.empty_like(qd)
-    rt.reserve_workspace(dev, len(items), c["Dh"])
+    rt.reserve_workspace(dev, len(items), Dh)
     rt.error_word(dev)
+    acc_rows = torch.empty((qd.shape[0],), dtype=torch.int32, device=dev)
+    acc_cnt = torch.empty((len(items),), dtype=torch.int32, device=dev)
 
     def step():
-        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, 1, lens=lens, out=out, kernel=args.kernel)
+        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, max_q, lens=cache.lens, out=out, kernel=args.kernel)
+        if acc is not None:
+            cache.commit_window(itd, accept_len=acc, n_rows=qd.shape[0], out=(acc_rows, acc_cnt))
 
     # warm up eagerly, then capture one step
     for _ in range(max(3, args.warmup)):
@@ -262,10 +360,10 @@ def run_wfd(args):
     rt.read_device_error(dev)
 
     # ---- e2e: public API call with host buffers every step ----
-    q_h, kn_h, vn_h = q.pin_memory(), kn.pin_memory(), vn.pin_memory()
+    q_h, kn_h, vn_h = qd.cpu().pin_memory(), knd.cpu().pin_memory(), vnd.cpu().pin_memory()
     it_h = items_t.pin_memory()
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    h2d = q_h.numel() * 2 + kn_h.numel() * 2 + vn_h.numel() * 2 + it_h.numel() * 4
+    h2d = (q_h.numel() + kn_h.numel() + vn_h.numel()) * 2 + it_h.numel() * 4
     d2h = out_h.numel() * 2
 
     def e2e_step():
@@ -273,20 +371,21 @@ def run_wfd(args):
         knd.copy_(kn_h, non_blocking=True)
         vnd.copy_(vn_h, non_blocking=True)
         itd.copy_(it_h, non_blocking=True)
-        wa.wave_attn(qd, knd, vnd, Kd, Vd, itd, 1, lens=lens, out=out, kernel=args.kernel)
+        step()
         out_h.copy_(out, non_blocking=True)
 
+    e2e_steps = args.steps if args.workload == "cfg2" else max(1, args.steps // 4)
     for _ in range(args.warmup):
         e2e_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier(device_ids=[local])
     ev0.record()
-    for _ in range(args.steps):
+    for _ in range(e2e_steps):
         e2e_step()
     ev1.record()
     torch.cuda.synchronize()
-    ms_e2e = ev0.elapsed_time(ev1) / args.steps
+    ms_e2e = ev0.elapsed_time(ev1) / e2e_steps
     rt.read_device_error(dev)
 
     if world > 1:
@@ -308,23 +407,22 @@ def run_wfd(args):
     # bf16 / Dh=128 defaults to the tensor-core kernel: plan + window append +
     # wave_tc_kernel per step; the CUDA-core kernel is plan + wave_decode_kernel
     tc = args.kernel != 0
-    kernel_name = ("wave_tc_kernel<16> (+ plan_kernel, append_segs_kernel, timed together)" if tc else
-                   "wave_decode_kernel<bf16,128,4> (+ plan_kernel, timed together)")
-    launches_per_step = 3 if tc else 2
+    nqp = 16 if c["H"] // c["Hkv"] * max_q <= 16 else 32
+    kernel_name = (f"wave_tc_kernel<{nqp}> (+ plan_kernel, append_segs_kernel" if tc else
+                   "wave_decode_kernel<bf16,128,4> (+ plan_kernel")
+    kernel_name += (", commit_window_kernel" if acc is not None else "") + ", timed together)"
+    launches_per_step = (3 if tc else 2) + (1 if acc is not None else 0)
     line = None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2_wavefront_decode_attention", "batch_per_gpu": c["B"], "slots": c["R"],
-                       "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "4096-r",
-                       "rows_per_step_per_gpu": rows, "parallelism": f"sequences sharded, {world} rank(s)",
-                       "l2": "KV working set 537 MB > 126 MB L2, no flush", "timing": "CUDA graph replay"},
+            "config": workload_config(args.workload, c, world, rows),
             "wave_rows_per_s": total_rows / (ms * 1e-3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": NCU_TRAFFIC_BYTES.get("tc" if tc else "cuda_core"),
+                         "traffic": NCU_TRAFFIC_BYTES.get((args.workload, "tc" if tc else "cuda_core")),
                          "algorithmic_bytes_per_launch": nbytes,
                          "kernel": kernel_name},
             "e2e": {"value": value_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -332,13 +430,20 @@ def run_wfd(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
+        if args.workload == "cfg3":
+            flops = sum((p0 + ql) for _, _, p0, ql, _ in items) * Hkv * (H // Hkv) * max_q * Dh * 4
+            line["tensor_tflops"] = flops / (ms * 1e-3) / 1e12
     if world > 1:
         dist.barrier(device_ids=[local])
         del g
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            base, _, _ = cpu_baseline(q, K, V, kn, vn, items, args.cpu_seconds)
+            if args.workload == "cfg2":
+                base, _, _ = cpu_baseline(q, K, V, kn, vn, items, args.cpu_seconds)
+            else:
+                Kc, Vc, qc, knc, vnc, itc = cfg3_cpu_sample(Kd, Vd, qd, knd, vnd, items)
+                base, _, _ = cpu_baseline(qc, Kc, Vc, knc, vnc, itc, args.cpu_seconds, label="cfg3 verify")
             line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
         else:
             line["cpu_baseline"] = None

@@ -64,7 +64,7 @@ struct TcCfg {
   static constexpr uint64_t P_LAYOUT = NQP == 16 ? 6 : 4;  // UMMA layout SWIZZLE_32B / SWIZZLE_64B
   static constexpr int P_ATOM = 8 * P_ROWB;                // 8 key rows
   static constexpr int RED_FLOATS = 2 * 4 * NQP;           // double-buffered per-warp column values
-  static constexpr int SMEM = STAGES * KV_STAGE + Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + 1024;
+  static constexpr int SMEM = STAGES * KV_STAGE + Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + (2 * NQP + 4) * 4 + 1024;
   static constexpr int TMEM_COLS = NQP == 16 ? 64 : 128;   // S (x2) and O accumulators
   static constexpr int PART_FLOATS = NQP * (128 + 2);
   static_assert(NQP == 16 || NQP == 32, "N of the swap-AB MMA");
@@ -255,6 +255,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   unsigned char* ps = qs + C::Q_BYTES;                     // P^T operand (MN-major)
   float* red = reinterpret_cast<float*>(ps + C::P_BYTES);  // [2][4][NQP] column maxima
   float* lred = red + C::RED_FLOATS;                       // [2][4][NQP] column sums
+  float* mst = lred + C::RED_FLOATS;                       // [NQP] running column max (log2-scaled)
+  float* ast = mst + NQP;                                  // [NQP] this tile's rescale factors
+  int* rflag = reinterpret_cast<int*>(ast + NQP);          // any factor != 1 this tile
 
   __shared__ __align__(8) uint64_t bar_full[STAGES];
   __shared__ __align__(8) uint64_t bar_empty[STAGES];
@@ -444,13 +447,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       softmax_bar();
       if (stid == 0) mbar_arrive(&bar_qready);
 
-      float m[NQP], lp[NQP], oacc[NQP];
+      // running column maxima live in shared memory (mst, log2-scaled), owned
+      // by lanes 0..NQP-1 of the first softmax warp
+      if (sw == 0 && lane < NQP) mst[lane] = NEG_INF;
+      float lp[NQP], oacc[NQP];
 #pragma unroll
       for (int n = 0; n < NQP; ++n) {
-        m[n] = NEG_INF;
         lp[n] = 0.f;
         oacc[n] = 0.f;
       }
+      const float c2 = p.scale_log2;
       for (int t = 0; t < n_t; ++t) {
         const uint32_t ti = it + t;
         const int sb = (int)(ti & 1u);
@@ -463,14 +469,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_sfree[sb]);
 
-        const int key = r_lo + t * kTcTile + my_row;  // key index inside the unit
+        // key `key` (unit index) is visible to query vector v = qg*NQP + n iff
+        // key <= k_len - q_len + v / G, i.e. n >= (key - (k_len - q_len)) * G - qg*NQP
+        const int key = r_lo + t * kTcTile + my_row;
         const bool kvalid = key < r_hi;
+        const int thr = p.causal ? (key - (S.k_len - S.q_len)) * p.G - qg * NQP : -(1 << 30);
+        const int nlim = kvalid ? nvec : 0;
 #pragma unroll
-        for (int n = 0; n < NQP; ++n) {
-          const int v = qg * NQP + n;
-          const int lim = (n < nvec) ? (p.causal ? S.k_len - S.q_len + v / p.G : S.k_len - 1) : -1;
-          s[n] = (kvalid && key <= lim) ? s[n] * p.scale_log2 : NEG_INF;
-        }
+        for (int n = 0; n < NQP; ++n) s[n] = (n < nlim && n >= thr) ? s[n] : NEG_INF;  // raw (unscaled) scores
         // column maxima over the tile's 128 keys
         float* rb = red + (ti & 1u) * (4 * NQP);
         {
@@ -479,6 +485,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int n = 0; n < NQP; ++n) w[n] = s[n];
           const float r = warp_col_reduce<NQP, true>(w, lane);
           if (lane < NQP) rb[sw * NQP + reduced_col<NQP>(lane)] = r;
+        }
+        softmax_bar();
+        // column owner: new running max (moved only when the tile exceeds it by
+        // more than 8 in log2 units; O and l share the stale max, so the result
+        // is exact) and the rescale factor alpha
+        if (sw == 0) {
+          float alpha = 1.f;
+          if (lane < NQP) {
+            const float tmax = fmaxf(fmaxf(rb[lane], rb[NQP + lane]), fmaxf(rb[2 * NQP + lane], rb[3 * NQP + lane]));
+            const float mo = mst[lane];
+            if (tmax != NEG_INF) {
+              const float ts = tmax * c2;
+              if (mo == NEG_INF) {
+                mst[lane] = ts;
+              } else if (ts > mo + 8.f) {
+                alpha = fast_exp2(mo - ts);
+                mst[lane] = ts;
+              }
+            }
+            ast[lane] = alpha;
+          }
+          const bool any = __any_sync(0xffffffffu, alpha != 1.f);
+          if (lane == 0) *rflag = any ? 1 : 0;
         }
         softmax_bar();
         const int stage = (int)(ti % STAGES);
@@ -506,9 +535,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int n = 0; n < NQP; ++n) oacc[n] += o[n];
         }
-        // online softmax update for this tile; P^T row of this key (bf16, swizzled)
+        // rescale the running sums when some column's max moved
+        if (*rflag) {
+#pragma unroll
+          for (int n4 = 0; n4 < NQP / 4; ++n4) {
+            const float4 a4 = reinterpret_cast<const float4*>(ast)[n4];
+            const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              lp[n4 * 4 + e] *= av[e];
+              oacc[n4 * 4 + e] *= av[e];
+            }
+          }
+        }
+        // probabilities of this key; P^T row (bf16, swizzled MN-major)
 #pragma unroll
         for (int c = 0; c < PCH; ++c) {
+          const float4 m0 = reinterpret_cast<const float4*>(mst)[2 * c];
+          const float4 m1 = reinterpret_cast<const float4*>(mst)[2 * c + 1];
+          const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
           uint32_t w4[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -516,13 +561,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int n = c * 8 + 2 * i + e;
-              const float tm = fmaxf(fmaxf(rb[n], rb[NQP + n]), fmaxf(rb[2 * NQP + n], rb[3 * NQP + n]));
-              const float mn = fmaxf(m[n], tm);
-              const float alpha = (mn == NEG_INF) ? 1.f : fast_exp2(m[n] - mn);
-              pr2[e] = (s[n] == NEG_INF) ? 0.f : fast_exp2(s[n] - mn);
-              lp[n] = lp[n] * alpha + pr2[e];
-              oacc[n] *= alpha;
-              m[n] = mn;
+              pr2[e] = (s[n] == NEG_INF) ? 0.f : fast_exp2(fmaf(s[n], c2, -mv[2 * i + e]));
+              lp[n] += pr2[e];
             }
             __nv_bfloat162 h2 = __floats2bfloat162_rn(pr2[0], pr2[1]);
             w4[i] = *reinterpret_cast<uint32_t*>(&h2);
@@ -584,7 +624,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int n = 0; n < NQP; ++n) {
           if (stid == n) {
-            pb[n] = m[n];
+            pb[n] = mst[n];
             pb[NQP + n] = lb[n] + lb[NQP + n] + lb[2 * NQP + n] + lb[3 * NQP + n];
           }
           pb[2 * NQP + n * 128 + dim] = oacc[n];

@@ -37,6 +37,23 @@ class SlotKVCache:
         self.V = torch.zeros(shape, dtype=dtype, device=self.device)
         self.lens = torch.zeros((n_slots, batch_size), dtype=torch.int32, device=self.device)
 
+    @classmethod
+    def wrap(cls, K: torch.Tensor, V: torch.Tensor, lens: torch.Tensor | None = None) -> "SlotKVCache":
+        """Adopt existing (n_slots, B, S, Hkv, Dh) K / V tensors (e.g. a reference
+        BatchStaticKVCache's .K / .V) without copying."""
+        if K.dim() != 5 or V.shape != K.shape or not (K.is_contiguous() and V.is_contiguous()):
+            raise ValueError("K, V must be contiguous (n_slots, B, max_seq_len, Hkv, Dh) tensors")
+        rt.dtype_code(K.dtype)
+        self = cls.__new__(cls)
+        self.n_slots, self.B, self.S, self.n_kv_head, self.head_dim = K.shape
+        self.dtype, self.device, self.K, self.V = K.dtype, K.device, K, V
+        if lens is None:
+            lens = torch.zeros((self.n_slots, self.B), dtype=torch.int32, device=K.device)
+        if lens.dtype != torch.int32 or tuple(lens.shape) != (self.n_slots, self.B):
+            raise ValueError("lens must be int32 (n_slots, B)")
+        self.lens = lens
+        return self
+
     # ------------------------------------------------------------------
     @property
     def nbytes(self) -> int:
@@ -121,19 +138,28 @@ class SlotKVCache:
         _abi.check(st, "wfd_commit_drop")
 
     def commit_window(self, items: torch.Tensor, *, accept_len: torch.Tensor | None = None,
-                      accept_mask: torch.Tensor | None = None, slot_offset: int = 0, n_rows: int | None = None):
+                      accept_mask: torch.Tensor | None = None, slot_offset: int = 0, n_rows: int | None = None,
+                      out: tuple[torch.Tensor, torch.Tensor] | None = None):
         """Accept commit of verify windows.  Returns (acc_rows, acc_count):
         acc_rows[q_row0 + k] = q row of the k-th accepted row of an item (rows
-        past the count are left -1), acc_count[i] = accepted rows of item i.
-        Accepted K/V rows are compacted in place to pos0, pos0+1, ..."""
+        past the count are left untouched: -1 when allocated here),
+        acc_count[i] = accepted rows of item i.  Accepted K/V rows are compacted
+        in place to pos0, pos0+1, ...  `out` supplies preallocated (acc_rows,
+        acc_count) int32 tensors (nothing is allocated then, e.g. under graph
+        capture)."""
         if (accept_len is None) == (accept_mask is None):
             raise ValueError("give exactly one of accept_len / accept_mask")
         items = _attn._i32(items, self.device).reshape(-1, 5)
         n = items.shape[0]
-        if n_rows is None:
-            n_rows = int((items[:, 4] + items[:, 3]).max().item()) if n else 0
-        acc_rows = torch.full((max(n_rows, 1),), -1, dtype=torch.int32, device=self.device)
-        acc_count = torch.zeros((max(n, 1),), dtype=torch.int32, device=self.device)
+        if out is not None:
+            acc_rows, acc_count = out
+            if n_rows is None:
+                n_rows = acc_rows.numel()
+        else:
+            if n_rows is None:
+                n_rows = int((items[:, 4] + items[:, 3]).max().item()) if n else 0
+            acc_rows = torch.full((max(n_rows, 1),), -1, dtype=torch.int32, device=self.device)
+            acc_count = torch.zeros((max(n, 1),), dtype=torch.int32, device=self.device)
         al = None if accept_len is None else _attn._i32(accept_len, self.device)
         am = None
         if accept_mask is not None:
