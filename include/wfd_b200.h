@@ -109,6 +109,31 @@ int wfd_wave_attn(const void* q, const void* k_new, const void* v_new, void* k_c
                   int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
                   void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream);
 
+/* wfd_wave_attn without a caller-supplied workspace, for callers that cannot
+ * allocate device memory when they call: code that runs while a CUDA graph is
+ * being captured without having reserved a buffer first, serving runtimes
+ * that fix their memory plan at start-up and must not allocate (an allocation
+ * can synchronise the device or fail under memory pressure mid-request), and
+ * foreign-language hosts with no device allocator of their own.  Has no
+ * counterpart in the reference.
+ *
+ * The scratch memory is a fixed array inside the library (5.5 MB on every
+ * device that loads the library, held until the process exits).  Limits:
+ * bf16 tensors, head_dim 128 (the tcgen05 kernel), at most 4096 items, at
+ * most 160 SMs; anything else returns WFD_ERR_UNSUPPORTED or
+ * WFD_ERR_WORKSPACE before launching.  The first call on a device looks up the
+ * array's device address (once per device, with that device current), so make
+ * that first call before any stream capture.  Every call shares the one array:
+ * each call clears the part that must start at zero, but calls that overlap on
+ * the GPU (different streams, or different threads racing on one stream)
+ * corrupt each other's results.  Allocates nothing: no cudaMalloc, no
+ * allocating library routine.  Arguments as wfd_wave_attn. */
+int wfd_wave_attn_static(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                         void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
+                         int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
+                         int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
+                         int32_t* d_err, void* stream);
+
 /* Same as wfd_wave_attn but forces the kernel: 0 = CUDA-core decode kernel,
  * 1 = tcgen05 verify kernel.  For tests and benchmarks. */
 int wfd_wave_attn_kernel(int32_t which, const void* q, const void* k_new, const void* v_new, void* k_cache,

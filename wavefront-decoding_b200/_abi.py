@@ -20,7 +20,8 @@ WFD_DTYPE_F32 = 1
 # every symbol include/wfd_b200.h declares
 EXPORTED = (
     "wfd_abi_version", "wfd_status_string", "wfd_read_error", "wfd_workspace_bytes", "wfd_workspace_init",
-    "wfd_wave_attn", "wfd_wave_attn_kernel", "wfd_attn_varlen", "wfd_attn_segments", "wfd_append",
+    "wfd_wave_attn", "wfd_wave_attn_static", "wfd_wave_attn_kernel", "wfd_attn_varlen", "wfd_attn_segments",
+    "wfd_append",
     "wfd_write_prefill", "wfd_commit_drop", "wfd_commit_window", "wfd_gather_pack",
 )
 
@@ -53,6 +54,8 @@ _SIGS = {
     "wfd_wave_attn": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P, _P], _I),
     "wfd_wave_attn_kernel": ([_I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S,
                               _P, _P], _I),
+    # as wfd_wave_attn without (ws, ws_bytes)
+    "wfd_wave_attn_static": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P], _I),
     # q k v out cu_q cu_k n max_q total_q total_k Hq Hkv Dh dtype causal scale ws ws_bytes err stream
     "wfd_attn_varlen": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P, _P], _I),
     # q k v out q_row0 q_len k_row0 k_len n max_q total_q total_k Hq Hkv Dh dtype causal scale ws ws_bytes err stream

@@ -49,7 +49,7 @@ inline int pow2ceil(int x) {
   while (p < x) p <<= 1;
   return p;
 }
-inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Largest NQ the CUDA-core kernel is built for: query vectors per unit are
 // register-resident (q and the output accumulator), so 16-byte-vector bf16 rows
@@ -64,16 +64,21 @@ struct WsLayout {
   size_t cnt, part, segs, prefix, total;
 };
 
-WsLayout ws_layout(int max_items, int head_dim, int sms) {
+constexpr size_t ws_part_floats(bool tc_only, int head_dim, size_t sms) {
+  // decode: NQ <= 16 query vectors per partial slot, kGridPerSm CTAs per SM;
+  // tensor cores: kVerifyMaxRows vectors per slot, one CTA per SM.
+  return tc_only ? 2 * sms * kVerifyMaxRows * (size_t)(head_dim + 2)
+                 : (2 * sms * kGridPerSm * (size_t)16 * (head_dim + 2) > 2 * sms * kVerifyMaxRows * (size_t)(head_dim + 2)
+                        ? 2 * sms * kGridPerSm * (size_t)16 * (head_dim + 2)
+                        : 2 * sms * kVerifyMaxRows * (size_t)(head_dim + 2));
+}
+
+WsLayout ws_layout(int max_items, int head_dim, int sms, bool tc_only = false) {
   WsLayout w;
   const size_t n_ctas = (size_t)sms * kGridPerSm;
   w.cnt = 0;
   w.part = align256(w.cnt + n_ctas * sizeof(int));
-  // decode: NQ <= 16 query vectors per partial slot, kGridPerSm CTAs per SM;
-  // verify: kVerifyMaxRows vectors per slot, one CTA per SM.
-  const size_t dec = 2 * n_ctas * (size_t)16 * (head_dim + 2);
-  const size_t ver = 2 * (size_t)sms * kVerifyMaxRows * (head_dim + 2);
-  w.segs = align256(w.part + (dec > ver ? dec : ver) * sizeof(float));
+  w.segs = align256(w.part + ws_part_floats(tc_only, head_dim, (size_t)sms) * sizeof(float));
   w.prefix = align256(w.segs + (size_t)max_items * sizeof(Seg));
   w.total = align256(w.prefix + (size_t)(max_items + 1) * sizeof(long long));
   return w;
@@ -219,19 +224,19 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   const int G = A.Hq / A.Hkv;
   const int sms = current_sms();
   if (sms <= 0) return WFD_ERR_CUDA;
-  if (A.n == 0) return WFD_OK;
-  const WsLayout L = ws_layout(A.n, A.Dh, sms);
-  if (A.ws_bytes < L.total || !aligned16(A.ws)) return WFD_ERR_WORKSPACE;
-  char* ws = static_cast<char*>(A.ws);
 
   const int max_q = A.max_q < 1 ? 1 : A.max_q;
   int which = A.which;
   const bool tc_ok = verify_supported(A.dtype, A.Dh, G, max_q) && A.key_rows > 0 && A.key_rows < (1ll << 31);
   // bf16 / Dh=128 runs on the tensor cores for decode rows too: measured on
   // B200 (config 2) the CUDA-core kernel is issue-bound at 54 % of HBM peak,
-  // the tcgen05 kernel reaches 68 %.  fp32 and Dh=64 stay on the CUDA cores.
+  // the tcgen05 kernel reaches 71 %.  fp32 and Dh=64 stay on the CUDA cores.
   if (which < 0) which = tc_ok ? 1 : 0;
   if (which == 1 && !tc_ok) return WFD_ERR_UNSUPPORTED;
+
+  const WsLayout L = ws_layout(A.n, A.Dh, sms, which == 1);
+  if (A.ws_bytes < L.total || !aligned16(A.ws)) return WFD_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(A.ws);
 
   int NQ;
   if (which == 0) {
@@ -393,9 +398,71 @@ bool geom_ok(int n_slots, int n_seqs, int max_seq, int Hkv, int Dh, int dtype) {
   return ((long long)Hkv * Dh * elem_bytes(dtype)) % 16 == 0;
 }
 
+// ---- fixed workspace for wfd_wave_attn_static (no device allocation) ----
+// Sized for the tensor-core path (bf16, head_dim 128) with up to
+// kStaticMaxItems work items on a device with up to kStaticMaxSms SMs.
+constexpr int kStaticMaxItems = 4096;
+constexpr int kStaticMaxSms = 160;
+
+constexpr size_t static_ws_bytes() {
+  return align256(align256(align256(align256((size_t)kStaticMaxSms * kGridPerSm * sizeof(int)) +
+                                    ws_part_floats(true, 128, kStaticMaxSms) * sizeof(float)) +
+                           (size_t)kStaticMaxItems * sizeof(Seg)) +
+                  (size_t)(kStaticMaxItems + 1) * sizeof(long long));
+}
+constexpr size_t kStaticWsBytes = static_ws_bytes();
+
+}  // namespace
+
+// One copy per device that loads the library, kept until the process exits.
+// Host code must not use this name as a device address: the device address
+// comes from cudaGetSymbolAddress (static_ws_device_ptr below).
+static __device__ __align__(256) unsigned char g_wfd_static_ws[kStaticWsBytes];
+
+namespace {
+
+void* g_static_ptr[kMaxDevices] = {};
+
+// Resolve the array's device address once per device, with that device current.
+void* static_ws_device_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_wfd_static_ws) != cudaSuccess) return nullptr;
+    g_static_ptr[dev] = p;
+  }
+  return g_static_ptr[dev];
+}
+
 }  // namespace
 
 extern "C" {
+
+int wfd_wave_attn_static(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                         void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
+                         int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
+                         int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
+                         int32_t* d_err, void* stream) {
+  if (dtype != WFD_DTYPE_BF16 || head_dim != 128) return WFD_ERR_UNSUPPORTED;
+  if (n_items < 0 || n_items > kStaticMaxItems) return WFD_ERR_WORKSPACE;
+  const int sms = current_sms();
+  if (sms <= 0) return WFD_ERR_CUDA;
+  if (sms > kStaticMaxSms) return WFD_ERR_WORKSPACE;
+  if (n_items == 0) return WFD_OK;
+  void* ws = static_ws_device_ptr();
+  if (ws == nullptr) return WFD_ERR_CUDA;
+  const WsLayout L = ws_layout(n_items, head_dim, sms, true);
+  if (L.total > kStaticWsBytes) return WFD_ERR_WORKSPACE;
+  // the split-K arrival counters must start at zero; the array keeps whatever
+  // the previous call (possibly an aborted one) left there
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(ws, 0, L.part, st) != cudaSuccess) return WFD_ERR_CUDA;
+  return wave_common(1, q, k_new, v_new, k_cache, v_cache, out, lens, items, n_items, max_q, slot_offset, n_rows,
+                     n_slots, n_seqs, max_seq, n_heads, n_kv_heads, head_dim, dtype, scale, ws, kStaticWsBytes,
+                     d_err, stream);
+}
 
 int wfd_abi_version(void) { return WFD_ABI_VERSION; }
 
