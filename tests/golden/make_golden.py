@@ -137,6 +137,30 @@ def gen_cfg3_commit(BatchStaticKVCache) -> dict:
     return {"cfg3/accept": a.numpy().astype(np.int64), "cfg3/seqlen": seqlen}
 
 
+def gen_scheduler() -> dict:
+    """The reference's own batch schedulers (scheduler_batch.py:185-362) driven
+    by the deterministic FakeBlocks: committed tokens, every per-sequence and
+    batch counter, and the rollback calls, per case."""
+    from src.decoding import scheduler_batch as sb
+    from src.decoding.emu import EmulatedAcceptance
+    from src.decoding.policy import SsdPolicy
+    out = {}
+    for case in gi.SCHED_CASES:
+        blocks = gi.FakeBlocks(case["T_total"])
+        prompts = gi.sched_prompts(case)
+        emus = None
+        if case["alpha"] is not None:
+            emus = [EmulatedAcceptance(case["alpha"], seed=100 + b) for b in range(case["B"])]
+        bt = sb.generate_wavefront_batch(blocks, prompts, case["new"],
+                                         SsdPolicy(T_total=case["T_total"], T_draft=case["T_draft"]), emus)
+        out[case["name"]] = gi.trace_summary(bt, blocks.last_cache)
+    blocks = gi.FakeBlocks(4)
+    prompts = gi.sched_prompts(gi.SCHED_CASES[0])
+    bt = sb.ar_generate_batch(blocks, prompts, 12)
+    out["ar_T4"] = gi.trace_summary(bt, blocks.last_cache)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -149,6 +173,7 @@ def main() -> None:
     data.update(gen_cfg3_commit(BSK))
     np.savez_compressed(HERE / "reference_golden.npz", **data)
     (HERE / "reference_kv_log.json").write_text(json.dumps(log) + "\n")
+    (HERE / "reference_scheduler.json").write_text(json.dumps(gen_scheduler(), indent=0) + "\n")
     total = sum(v.nbytes for v in data.values())
     print(f"wrote {len(data)} arrays ({total / 1e6:.2f} MB raw) to {HERE / 'reference_golden.npz'}")
 

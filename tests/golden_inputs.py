@@ -122,3 +122,93 @@ def kv_script():
 def cfg3_accept() -> torch.Tensor:
     """Config 3: per-sequence accepted lengths U{0..8}, seed 3."""
     return torch.randint(0, 9, (32,), generator=gen(3))
+
+
+# ---------------------------------------------------------------------------
+# deterministic stand-in for the model blocks (scheduler golden runs)
+# ---------------------------------------------------------------------------
+def _mix(*xs) -> int:
+    h = 1469598103934665603
+    for x in xs:
+        h ^= (int(x) + 0x9E3779B97F4A7C15) & 0xFFFFFFFFFFFFFFFF
+        h = (h * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
+class FakeCache:
+    """Records the rollbacks a scheduler issues."""
+
+    nbytes = 0
+
+    def __init__(self):
+        self.drops = []
+
+    def drop_positions_at_and_after(self, b, position):
+        self.drops.append((int(b), int(position)))
+
+
+class FakeBlocks:
+    """Union P / R / C interface of the reference's batch blocks
+    (ouro_blocks_batch.py:123-248) with token choices that depend only on
+    (sequence, position, token, depth): the greedy id at full depth for a token
+    at position p is the 'gold' for p+1; at draft depth it agrees with the gold
+    with probability ~ agree."""
+
+    def __init__(self, T_total: int, vocab: int = 50, agree: float = 0.7, seed: int = 0):
+        self.T_total = T_total
+        self.vocab = vocab
+        self.agree_mod = 1000
+        self.agree_thr = int(agree * 1000)
+        self.seed = seed
+
+    def prefill(self, prompt_ids):
+        B = prompt_ids.shape[0]
+        logits = torch.zeros((B, self.vocab))
+        for b in range(B):
+            logits[b, _mix(self.seed, b, int(prompt_ids[b].sum())) % self.vocab] = 1.0
+        self.last_cache = FakeCache()
+        return self.last_cache, logits
+
+    def prelude_union(self, seq_ids, toks, cache):
+        for b, t in zip(seq_ids, toks):
+            t.hidden = (int(b), int(t.token_id), int(t.position))
+            t.static_state = None
+            t.step = 0
+
+    def advance_union(self, seq_ids, toks, cache):
+        for t in toks:
+            t.step += 1
+
+    def coda_argmax_union(self, seq_ids, toks, cache):
+        out = []
+        for b, t in zip(seq_ids, toks):
+            sb, tok, pos = t.hidden
+            gold = _mix(self.seed, 1, sb, tok, pos) % self.vocab
+            if t.step >= self.T_total or _mix(self.seed, 2, sb, tok, pos) % self.agree_mod < self.agree_thr:
+                out.append(gold)
+            else:
+                out.append((gold + 1 + _mix(self.seed, 3, sb, pos) % (self.vocab - 1)) % self.vocab)
+        return out
+
+
+SCHED_CASES = [
+    dict(name="wfd_T4_D1_greedy", T_total=4, T_draft=1, B=3, L=7, new=24, alpha=None),
+    dict(name="wfd_T4_D2_greedy", T_total=4, T_draft=2, B=3, L=5, new=24, alpha=None),
+    dict(name="wfd_T8_D2_emu05", T_total=8, T_draft=2, B=4, L=6, new=20, alpha=0.5),
+    dict(name="wfd_T4_D4_emu1", T_total=4, T_draft=4, B=2, L=4, new=16, alpha=1.0),
+    dict(name="wfd_T6_D3_emu08", T_total=6, T_draft=3, B=3, L=9, new=18, alpha=0.8),
+]
+
+
+def sched_prompts(case) -> torch.Tensor:
+    return torch.randint(0, 50, (case["B"], case["L"]), generator=gen(97))
+
+
+def trace_summary(bt, cache) -> dict:
+    return {
+        "tokens": [list(map(int, t.tokens)) for t in bt.per_seq],
+        "counters": [[t.n_r_calls, t.n_p_calls, t.n_c_calls, t.n_drafts_proposed, t.n_drafts_accepted,
+                      t.n_drafts_rejected, t.n_rollback_events] for t in bt.per_seq],
+        "batch": [bt.n_r_calls, bt.n_p_calls, bt.n_c_calls, bt.r_union_total, bt.r_union_max],
+        "drops": [list(d) for d in cache.drops],
+    }
