@@ -1,0 +1,100 @@
+"""Plain sequential loop decoding of the looped LM, recomputed from scratch for
+every token in float64 on the CPU (test oracle).
+
+The reference's sequential baseline (`ar_generate_parcae_blocks`,
+src/decoding/ar_baseline.py:132-193) runs, per token, the prelude, T_total
+loop steps of the core and the coda with KV caching per (layer, depth) slot.
+Caching only stores values that a full causal recompute over the whole
+sequence produces again, so this oracle recomputes the whole sequence at every
+step: the engine's slot bookkeeping (which depth's K/V lives where, rollback,
+wave ordering) has nothing to hide behind.
+
+Weights come as plain tensors (the names of looped_lm.LoopedLM); the math is
+the same architecture: prelude -> (h <- h + e; core) x T_total -> coda ->
+RMSNorm -> lm_head, blocks = RMSNorm / QKV / rotate-half RoPE / causal GQA
+attention / o_proj / RMSNorm / SwiGLU.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+
+def _rms(x, w, eps):
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+def _rope(x, pos, theta):
+    Dh = x.shape[-1]
+    inv = 1.0 / (theta ** (torch.arange(0, Dh, 2, dtype=torch.float64) / Dh))
+    ang = torch.outer(pos.double(), inv)            # (T, Dh/2)
+    c, s = ang.cos()[:, None, :], ang.sin()[:, None, :]
+    x1, x2 = x[..., : Dh // 2], x[..., Dh // 2:]
+    return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1)
+
+
+def _block(blk, x, cfg):
+    T = x.shape[0]
+    H, Hkv, Dh = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]
+    pos = torch.arange(T)
+    h = _rms(x, blk["norm1"], cfg["norm_eps"]) @ blk["wqkv"]
+    q, k, v = torch.split(h, [H * Dh, Hkv * Dh, Hkv * Dh], dim=-1)
+    q = _rope(q.reshape(T, H, Dh), pos, cfg["rope_theta"])
+    k = _rope(k.reshape(T, Hkv, Dh), pos, cfg["rope_theta"])
+    v = v.reshape(T, Hkv, Dh)
+    G = H // Hkv
+    k = k.repeat_interleave(G, dim=1)
+    v = v.repeat_interleave(G, dim=1)
+    s = torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(Dh)
+    mask = torch.arange(T)[None, :] <= torch.arange(T)[:, None]
+    s = s.masked_fill(~mask[None], float("-inf"))
+    o = torch.einsum("hqk,khd->qhd", torch.softmax(s, dim=-1), v).reshape(T, H * Dh)
+    x = x + o @ blk["wo"]
+    gu = _rms(x, blk["norm2"], cfg["norm_eps"]) @ blk["wgu"]
+    g, u = gu.split(cfg["d_ff"], dim=-1)
+    return x + (torch.nn.functional.silu(g) * u) @ blk["wd"]
+
+
+def last_logits(W: dict, cfg: dict, ids: torch.Tensor) -> torch.Tensor:
+    x = W["embed"][ids]
+    for blk in W["prelude"]:
+        x = _block(blk, x, cfg)
+    e = x
+    h = torch.zeros_like(e)
+    for _ in range(cfg["T_total"]):
+        h = h + e
+        for blk in W["core"]:
+            h = _block(blk, h, cfg)
+    x = h
+    for blk in W["coda"]:
+        x = _block(blk, x, cfg)
+    return _rms(x[-1], W["final_norm"], cfg["norm_eps"]) @ W["lm_head"]
+
+
+def greedy_generate(W: dict, cfg: dict, prompt: list[int], n_new: int) -> list[int]:
+    """First token from the prompt, then n_new - 1 more, each by full recompute."""
+    ids = list(prompt)
+    out = []
+    for _ in range(n_new):
+        tok = int(last_logits(W, cfg, torch.tensor(ids)).argmax())
+        out.append(tok)
+        ids.append(tok)
+    return out
+
+
+def weights_from(model) -> tuple[dict, dict]:
+    """float64 CPU copies of a looped_lm.LoopedLM's weights and its config."""
+    def f(t):
+        return t.detach().to("cpu", torch.float64)
+
+    def blk(b):
+        return {k: f(getattr(b, k)) for k in ("norm1", "wqkv", "wo", "norm2", "wgu", "wd")}
+
+    W = {"embed": f(model.embed), "final_norm": f(model.final_norm), "lm_head": f(model.lm_head),
+         "prelude": [blk(b) for b in model.prelude], "core": [blk(b) for b in model.core],
+         "coda": [blk(b) for b in model.coda]}
+    c = model.cfg
+    cfg = {k: getattr(c, k) for k in ("n_heads", "n_kv_heads", "head_dim", "d_ff", "T_total", "norm_eps",
+                                      "rope_theta")}
+    return W, cfg

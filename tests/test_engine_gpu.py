@@ -1,0 +1,116 @@
+"""End-to-end: the GPU wavefront engine (union P/R/C over the wavefront kernels,
+CUDA graphs) driven by the batch schedulers.
+
+* sequential loop decoding on the engine == the float64 full-recompute oracle;
+* greedy wavefront decoding == sequential loop decoding, token for token, for
+  every T_draft (the lossless claim, README of the reference, scheduler.py:14-17);
+* graph replay == eager launches;
+* emulated acceptance (rollbacks every few ticks) keeps every sequence's
+  commits consistent (alpha = 1: no rejects, exactly N commits).
+fp32 model: no reduced-precision GEMMs, so token equality is a fair test.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import golden_inputs as gi
+
+pytestmark = pytest.mark.gpu
+
+
+def _small_cfg(**kw):
+    from wavefront_decoding_b200.looped_lm import LoopedLMConfig
+    base = dict(vocab=512, d_model=256, n_heads=4, n_kv_heads=2, head_dim=64, d_ff=512, n_prelude=1, n_core=2,
+                n_coda=1, T_total=4)
+    base.update(kw)
+    return LoopedLMConfig(**base)
+
+
+def _engine(cfg, B, S, dtype=torch.float32, graphs=True, seed=0):
+    from wavefront_decoding_b200.engine import WaveEngine
+    from wavefront_decoding_b200.looped_lm import LoopedLM
+    torch.backends.cuda.matmul.allow_tf32 = False
+    model = LoopedLM(cfg, seed=seed, dtype=dtype, device="cuda")
+    return model, WaveEngine(model, B, S, use_graphs=graphs)
+
+
+def _prompts(B, L, vocab, seed=5):
+    return torch.randint(0, vocab, (B, L), generator=gi.gen(seed))
+
+
+def test_engine_ar_matches_full_recompute_oracle(cuda_dev):
+    from oracle import looped_lm as olm
+    from wavefront_decoding_b200 import scheduler as sch
+    cfg = _small_cfg()
+    B, L, N = 2, 12, 10
+    model, eng = _engine(cfg, B, L + N + 16)
+    prompts = _prompts(B, L, cfg.vocab)
+    bt = sch.ar_generate_batch(eng, prompts, N)
+    W, c = olm.weights_from(model)
+    for b in range(B):
+        ids = prompts[b].tolist()
+        for i, tok in enumerate(bt.per_seq[b].tokens):
+            lg = olm.last_logits(W, c, torch.tensor(ids))
+            want = int(lg.argmax())
+            if tok != want:
+                # fp32 vs fp64 may only disagree on a near-tie; the streams diverge after it
+                assert float(lg[want] - lg[tok]) < 1e-4, (b, i, tok, want)
+                break
+            ids.append(tok)
+
+
+@pytest.mark.parametrize("T_draft", [1, 2, 4])
+def test_engine_wfd_equals_sequential(cuda_dev, T_draft):
+    from wavefront_decoding_b200 import scheduler as sch
+    cfg = _small_cfg()
+    B, L, N = 3, 10, 24
+    prompts = _prompts(B, L, cfg.vocab, seed=6)
+    _, eng = _engine(cfg, B, L + N + 16)
+    ar = sch.ar_generate_batch(eng, prompts, N)
+    _, eng2 = _engine(cfg, B, L + N + 16)
+    wfd = sch.generate_wavefront_batch(eng2, prompts, N, sch.SsdPolicy(T_total=4, T_draft=T_draft), None)
+    assert [t.tokens for t in wfd.per_seq] == [t.tokens for t in ar.per_seq]
+    if T_draft < 4:
+        assert sum(t.n_drafts_proposed for t in wfd.per_seq) > 0
+    assert eng2.n_graph_replays > 0
+    from wavefront_decoding_b200 import runtime as rt
+    assert rt.read_device_error(cuda_dev) == 0
+
+
+def test_engine_graphs_equal_eager(cuda_dev):
+    from wavefront_decoding_b200 import scheduler as sch
+    cfg = _small_cfg(n_kv_heads=4)
+    B, L, N = 2, 9, 16
+    prompts = _prompts(B, L, cfg.vocab, seed=8)
+    outs = []
+    for graphs in (True, False):
+        _, eng = _engine(cfg, B, L + N + 16, graphs=graphs)
+        emus = [sch.EmulatedAcceptance(0.6, seed=3 + b) for b in range(B)]
+        bt = sch.generate_wavefront_batch(eng, prompts, N, sch.SsdPolicy(4, 1), emus)
+        outs.append(([t.tokens for t in bt.per_seq], [t.n_rollback_events for t in bt.per_seq]))
+    assert outs[0] == outs[1]
+
+
+def test_engine_emulated_acceptance(cuda_dev):
+    from wavefront_decoding_b200 import scheduler as sch
+    cfg = _small_cfg()
+    B, L, N = 4, 8, 20
+    prompts = _prompts(B, L, cfg.vocab, seed=9)
+    _, eng = _engine(cfg, B, L + N + 16, dtype=torch.bfloat16)
+    emus = [sch.EmulatedAcceptance(1.0, seed=b) for b in range(B)]
+    bt = sch.generate_wavefront_batch(eng, prompts, N, sch.SsdPolicy(4, 2), emus)
+    for t in bt.per_seq:
+        assert len(t.tokens) == N and t.n_drafts_rejected == 0
+    _, eng = _engine(cfg, B, L + N + 16, dtype=torch.bfloat16)
+    emus = [sch.EmulatedAcceptance(0.5, seed=20 + b) for b in range(B)]
+    bt = sch.generate_wavefront_batch(eng, prompts, N, sch.SsdPolicy(4, 1), emus)
+    assert sum(t.n_rollback_events for t in bt.per_seq) > 0
+    for t in bt.per_seq:
+        assert len(t.tokens) == N
+    # after the run every slot length of a sequence stays within its committed span
+    lens = eng.cache.seqlen
+    for b in range(B):
+        assert max(lens[s][b] for s in range(cfg.n_slots)) <= L + N + 2 * cfg.T_total
+    from wavefront_decoding_b200 import runtime as rt
+    assert rt.read_device_error(cuda_dev) == 0

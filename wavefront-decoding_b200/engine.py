@@ -1,0 +1,249 @@
+"""GPU wavefront engine: the union P / R / C blocks over the wavefront kernels,
+with CUDA-graph replay.
+
+Implements the batch-blocks interface the reference's schedulers drive
+(`prefill`, `prelude_union`, `advance_union`, `coda_argmax_union`,
+ouro_blocks_batch.py:123-248, huginn_blocks_batch.py:207-346), B200-first:
+
+* Token state (hidden, injected input) lives in a device pool; an ActiveToken's
+  `hidden` is its pool row, so a union call gathers rows instead of stacking
+  per-token tensors, and writes them back in place.
+* One R tick is one attention launch per core layer for the whole union
+  (`wfd_wave_attn`: append + attention fused, one item table shared by all
+  layers through `slot_offset`), replacing the reference's per-layer
+  write_tokens + gather_pack + attn_varlen (ouro_blocks_batch.py:207-231) and the
+  graph engine's per-row `_fa_varlen` loop (graph_blocks.py:187-194).
+* Prelude and coda tokens of one sequence may share a slot inside one call, so
+  those layers append first (`wfd_append`) and then attend with explicit
+  segments over the cache (`wfd_attn_segments`).
+* Per call the host builds one small int32 table, uploads it with a single
+  pinned copy, and replays the CUDA graph captured for the union-size bucket
+  (the reference captures per WFD phase, graph_blocks.py:82-95, 362-386; here
+  per bucket, so the dynamic scheduler replays graphs every tick).  Rows past
+  the union point at a scratch pool row and a scratch sequence of the cache, so
+  a bucket's graph is valid for any union size up to its capacity.  The only
+  host sync per tick is the greedy-id read-back of the C union, as in the
+  reference (scheduler_batch.py:312).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import attention as wa
+from . import runtime as rt
+from .kv_cache import SlotKVCache
+from .looped_lm import LoopedLM
+
+_BUCKETS = (8, 16, 32, 64, 128, 256, 512, 1024, 2048)
+
+
+def _bucket(n: int) -> int:
+    for b in _BUCKETS:
+        if n <= b:
+            return b
+    raise ValueError(f"union of {n} rows exceeds the largest bucket {_BUCKETS[-1]}")
+
+
+class _Tables:
+    """Device tables of one (kind, bucket) and their pinned staging copy.
+    int32 columns: 0 pool row, 1 position, 2 token id, 3 cache sequence,
+    4 R: slot base (depth * n_core), 5 live (q_len 1) / padding (0),
+    6.. prelude / coda layers: first cache row of the row's (slot, sequence)."""
+
+    def __init__(self, cap: int, n_cols: int, device):
+        self.cap = cap
+        self.n_cols = n_cols
+        self.host = torch.zeros((cap, n_cols), dtype=torch.int32).pin_memory()
+        self.dev = torch.zeros((cap, n_cols), dtype=torch.int32, device=device)
+        self.items = torch.zeros((cap, 5), dtype=torch.int32, device=device)
+        self.row_ids = torch.arange(cap, dtype=torch.int32, device=device)
+        self.ones = torch.ones(cap, dtype=torch.int32, device=device)
+        self.out = torch.zeros(cap, dtype=torch.int32, device=device)
+        self.graph = None
+        self.uploaded = torch.cuda.Event()   # the staging copy may be rewritten once this fired
+        self.pending = False
+
+
+class WaveEngine:
+    def __init__(self, model: LoopedLM, batch_size: int, max_seq_len: int, use_graphs: bool = True):
+        cfg = model.cfg
+        self.model = model
+        self.cfg = cfg
+        self.T_total = cfg.T_total
+        self.B = batch_size
+        self.S = max_seq_len
+        self.device = model.device
+        self.use_graphs = use_graphs
+        # one extra sequence row: the target of padding rows
+        self.cache = SlotKVCache(cfg.n_slots, batch_size + 1, cfg.n_kv_heads, cfg.head_dim, max_seq_len, model.dtype,
+                                 model.device)
+        self.scratch_seq = batch_size
+        self.Kflat = self.cache.K.view(-1, cfg.n_kv_heads, cfg.head_dim)
+        self.Vflat = self.cache.V.view(-1, cfg.n_kv_heads, cfg.head_dim)
+        # state pool: live tokens are at most B * (T_total / T_draft + 2) per tick;
+        # round-robin reuse over this many rows never recycles a live row
+        self.pool_cap = batch_size * 2 * (cfg.T_total + 8)
+        self.scratch_row = self.pool_cap
+        d = cfg.d_model
+        self.pool_h = torch.zeros((self.pool_cap + 1, d), dtype=model.dtype, device=self.device)
+        self.pool_e = torch.zeros((self.pool_cap + 1, d), dtype=model.dtype, device=self.device)
+        self._next_row = 0
+        self.cos, self.sin = model.rope_tables(max_seq_len)
+        self._tables: dict[tuple[str, int], _Tables] = {}
+        rt.reserve_workspace(self.device, _BUCKETS[-1], cfg.head_dim)
+        rt.error_word(self.device)
+        self.n_graph_replays = 0
+        self.n_launch_calls = 0
+
+    # ------------------------------------------------------------------
+    def synchronize(self) -> None:
+        torch.cuda.synchronize(self.device)
+
+    def drop_positions_at_and_after(self, b: int, position: int) -> None:
+        self.cache.drop_positions_at_and_after(b, position)
+
+    def _alloc_rows(self, n: int) -> list[int]:
+        rows = [(self._next_row + i) % self.pool_cap for i in range(n)]
+        self._next_row = (self._next_row + n) % self.pool_cap
+        return rows
+
+    def _seg_layers(self, kind: str) -> list[int]:
+        cfg = self.cfg
+        if kind == "P":
+            return [cfg.slot_prelude(i) for i in range(cfg.n_prelude)]
+        if kind == "C":
+            return [cfg.slot_coda(i) for i in range(cfg.n_coda)]
+        return []
+
+    def _fill(self, kind: str, toks, seq_ids, rows) -> _Tables:
+        cfg = self.cfg
+        n = len(toks)
+        cap = _bucket(n)
+        t = self._tables.get((kind, cap))
+        seg_slots = self._seg_layers(kind)
+        if t is None:
+            t = _Tables(cap, 6 + len(seg_slots), self.device)
+            self._tables[(kind, cap)] = t
+        if t.pending:
+            t.uploaded.synchronize()
+        a = t.host.numpy()
+        a[:] = 0
+        a[:, 0] = self.scratch_row
+        a[:, 3] = self.scratch_seq
+        a[:n, 0] = rows
+        a[:n, 1] = [tk.position for tk in toks]
+        a[:n, 2] = [tk.token_id for tk in toks]
+        a[:n, 3] = seq_ids
+        if kind == "R":
+            a[:n, 4] = [tk.step * cfg.n_core for tk in toks]
+        a[:n, 5] = 1
+        for j, slot in enumerate(seg_slots):
+            a[:, 6 + j] = (slot * (self.B + 1) + a[:, 3].astype(np.int64)) * self.S
+        t.dev.copy_(t.host, non_blocking=True)
+        t.uploaded.record()
+        t.pending = True
+        return t
+
+    # ------------------------------------------------------------------
+    # device-side bodies (captured into graphs)
+    def _segment_block(self, blk, x, t: _Tables, j: int, slot: int, cos, sin):
+        """Prelude / coda layer: append every row, then attend with segments."""
+        m = self.model
+        tab = t.dev
+        q, k, v = m.qkv(blk, x, cos, sin)
+        self.cache.write_tokens(t.ones * slot, tab[:, 3], tab[:, 1], k, v)
+        o = wa.attn_segments(q, self.Kflat, self.Vflat, t.row_ids, tab[:, 5], tab[:, 6 + j], tab[:, 1] + 1, 1,
+                             causal=False)
+        return m.finish_block(blk, x, o)
+
+    def _body(self, kind: str, t: _Tables) -> None:
+        m, cfg = self.model, self.cfg
+        tab = t.dev
+        rows = tab[:, 0].long()
+        pos = tab[:, 1].long()
+        cos, sin = self.cos.index_select(0, pos), self.sin.index_select(0, pos)
+        if kind == "P":
+            x = m.embed.index_select(0, tab[:, 2].long())
+            for j, blk in enumerate(m.prelude):
+                x = self._segment_block(blk, x, t, j, cfg.slot_prelude(j), cos, sin)
+            self.pool_e.index_copy_(0, rows, x)
+            self.pool_h.index_copy_(0, rows, torch.zeros_like(x))
+        elif kind == "R":
+            x = self.pool_h.index_select(0, rows) + self.pool_e.index_select(0, rows)
+            items = t.items
+            items[:, 0] = tab[:, 4]
+            items[:, 1] = tab[:, 3]
+            items[:, 2] = tab[:, 1]
+            items[:, 3] = tab[:, 5]
+            items[:, 4] = t.row_ids
+            for l, blk in enumerate(m.core):
+                q, k, v = m.qkv(blk, x, cos, sin)
+                o = wa.wave_attn(q, k, v, self.cache.K, self.cache.V, items, 1, lens=self.cache.lens,
+                                 slot_offset=cfg.n_prelude + l)
+                x = m.finish_block(blk, x, o)
+            self.pool_h.index_copy_(0, rows, x)
+        else:
+            x = self.pool_h.index_select(0, rows)
+            for j, blk in enumerate(m.coda):
+                x = self._segment_block(blk, x, t, j, cfg.slot_coda(j), cos, sin)
+            t.out.copy_(m.logits(x).argmax(dim=-1).to(torch.int32))
+
+    def _run(self, kind: str, t: _Tables) -> None:
+        self.n_launch_calls += 1
+        if not self.use_graphs:
+            self._body(kind, t)
+            return
+        if t.graph is None:
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self._body(kind, t)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._body(kind, t)
+            t.graph = g
+        t.graph.replay()
+        self.n_graph_replays += 1
+
+    # ------------------------------------------------------------------
+    # reference blocks interface
+    @torch.no_grad()
+    def prefill(self, prompt_ids: torch.Tensor):
+        B, L = prompt_ids.shape
+        assert B == self.B, f"prefill expects (B={self.B}, L) prompt ids"
+        self.cache.lens.zero_()
+        ids = prompt_ids.to(self.device)
+        pad = torch.zeros((1, L), dtype=ids.dtype, device=self.device)
+        last_logits = self.model.prefill_dense(torch.cat([ids, pad]), self.cache)[:B]
+        return self, last_logits
+
+    @torch.no_grad()
+    def prelude_union(self, seq_ids, toks, cache) -> None:
+        rows = self._alloc_rows(len(toks))
+        t = self._fill("P", toks, seq_ids, rows)
+        self._run("P", t)
+        for tk, r in zip(toks, rows):
+            tk.hidden = r
+            tk.static_state = r
+            tk.step = 0
+
+    @torch.no_grad()
+    def advance_union(self, seq_ids, toks, cache) -> None:
+        t = self._fill("R", toks, seq_ids, [tk.hidden for tk in toks])
+        self._run("R", t)
+        for tk in toks:
+            tk.step += 1
+
+    @torch.no_grad()
+    def coda_argmax_union(self, seq_ids, toks, cache) -> list[int]:
+        t = self._fill("C", toks, seq_ids, [tk.hidden for tk in toks])
+        self._run("C", t)
+        return t.out[:len(toks)].tolist()
+
+    # reporting
+    @property
+    def nbytes(self) -> int:
+        return self.cache.nbytes

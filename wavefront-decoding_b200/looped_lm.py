@@ -1,0 +1,179 @@
+"""Random-init looped (recurrent-depth) language model whose attention runs on
+the wavefront kernels.
+
+Architecture (the P / R / C split of the reference's looped models,
+src/decoding/blocks.py:22-116, parcae_blocks.py:283-518,
+huginn_blocks_batch.py:1-31):
+  P  embedding -> n_prelude blocks; its output e is the loop's injected input
+  R  one loop step: x <- x + e (additive input injection), then n_core blocks
+  C  n_coda blocks -> final RMSNorm -> lm_head
+Block: RMSNorm -> fused QKV -> RoPE -> attention over this block's KV slot ->
+o_proj -> residual -> RMSNorm -> SwiGLU -> residual.
+KV slots (kv_cache.py:12-15 of the reference): prelude layer i -> i; core
+(depth r, layer l) -> n_prelude + r * n_core + l; coda layer i ->
+n_prelude + T_total * n_core + i.
+
+Weights are plain tensors; GEMMs are cuBLAS (torch.matmul), attention is
+libwfd_b200.  Prefill attention (the one-shot prompt pass) uses torch's fused
+SDPA; every decode-time attention uses the wavefront kernels.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+
+@dataclass
+class LoopedLMConfig:
+    vocab: int = 32000
+    d_model: int = 512
+    n_heads: int = 8
+    n_kv_heads: int = 8
+    head_dim: int = 64
+    d_ff: int = 1536
+    n_prelude: int = 1
+    n_core: int = 2
+    n_coda: int = 1
+    T_total: int = 4          # loop depth R
+    rope_theta: float = 10000.0
+    norm_eps: float = 1e-6
+    init_std: float = 0.02
+
+    @property
+    def n_slots(self) -> int:
+        return self.n_prelude + self.T_total * self.n_core + self.n_coda
+
+    def slot_prelude(self, i: int) -> int:
+        return i
+
+    def slot_core(self, r: int, l: int) -> int:
+        return self.n_prelude + r * self.n_core + l
+
+    def slot_coda(self, i: int) -> int:
+        return self.n_prelude + self.T_total * self.n_core + i
+
+    def n_params(self) -> int:
+        d, Dh = self.d_model, self.head_dim
+        per_layer = d * (self.n_heads + 2 * self.n_kv_heads) * Dh + self.n_heads * Dh * d + 3 * d * self.d_ff + 2 * d
+        return 2 * self.vocab * d + d + (self.n_prelude + self.n_core + self.n_coda) * per_layer
+
+
+# the configurations BASELINE.json names
+CONFIG1 = LoopedLMConfig()  # vocab 32000, d 512, 8 x 64, SwiGLU 1536, prelude 1 / core 2 x R=4 / coda 1
+CONFIG4 = LoopedLMConfig(vocab=50304, d_model=1536, n_heads=24, n_kv_heads=24, head_dim=64, d_ff=4096,
+                         n_prelude=2, n_core=4, n_coda=2, T_total=8)
+
+
+class Block:
+    def __init__(self, cfg: LoopedLMConfig, g: torch.Generator, dtype, device):
+        d, Dh, H, Hkv = cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+        std = cfg.init_std
+
+        def w(*shape, scale=1.0):
+            return (torch.randn(shape, generator=g) * (std * scale)).to(dtype=dtype, device=device)
+
+        self.norm1 = torch.ones(d, dtype=dtype, device=device)
+        self.wqkv = w(d, (H + 2 * Hkv) * Dh)
+        self.wo = w(H * Dh, d, scale=1.0 / math.sqrt(2.0))
+        self.norm2 = torch.ones(d, dtype=dtype, device=device)
+        self.wgu = w(d, 2 * cfg.d_ff)
+        self.wd = w(cfg.d_ff, d, scale=1.0 / math.sqrt(2.0))
+
+
+class LoopedLM:
+    def __init__(self, cfg: LoopedLMConfig, seed: int = 0, dtype=torch.bfloat16, device="cuda"):
+        self.cfg = cfg
+        self.dtype = dtype
+        self.device = torch.device(device)
+        g = torch.Generator().manual_seed(seed)
+        d = cfg.d_model
+        self.embed = (torch.randn((cfg.vocab, d), generator=g) * 1.0).to(dtype=dtype, device=self.device)
+        self.prelude = [Block(cfg, g, dtype, self.device) for _ in range(cfg.n_prelude)]
+        self.core = [Block(cfg, g, dtype, self.device) for _ in range(cfg.n_core)]
+        self.coda = [Block(cfg, g, dtype, self.device) for _ in range(cfg.n_coda)]
+        self.final_norm = torch.ones(d, dtype=dtype, device=self.device)
+        self.lm_head = (torch.randn((d, cfg.vocab), generator=g) * (1.0 / math.sqrt(d))).to(dtype=dtype,
+                                                                                           device=self.device)
+        self._rope_cache = None
+
+    # ------------------------------------------------------------------
+    def rope_tables(self, max_seq: int):
+        if self._rope_cache is None or self._rope_cache[0].shape[0] < max_seq:
+            Dh = self.cfg.head_dim
+            inv = 1.0 / (self.cfg.rope_theta ** (torch.arange(0, Dh, 2, dtype=torch.float64) / Dh))
+            t = torch.arange(max_seq, dtype=torch.float64)
+            ang = torch.outer(t, inv)
+            self._rope_cache = (ang.cos().float().to(self.device), ang.sin().float().to(self.device))
+        return self._rope_cache
+
+    def rmsnorm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.norm_eps)
+        return (y * w.float()).to(x.dtype)
+
+    @staticmethod
+    def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """Rotate-half RoPE; x (..., T, H, Dh), cos / sin (T, Dh/2) fp32."""
+        half = x.shape[-1] // 2
+        xf = x.float()
+        x1, x2 = xf[..., :half], xf[..., half:]
+        c = cos.unsqueeze(-2)
+        s = sin.unsqueeze(-2)
+        return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1).to(x.dtype)
+
+    def qkv(self, blk: Block, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+        cfg = self.cfg
+        H, Hkv, Dh = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        h = self.rmsnorm(x, blk.norm1)
+        qkv = h @ blk.wqkv
+        q, k, v = torch.split(qkv, [H * Dh, Hkv * Dh, Hkv * Dh], dim=-1)
+        shp = x.shape[:-1]
+        q = self.apply_rope(q.reshape(*shp, H, Dh), cos, sin)
+        k = self.apply_rope(k.reshape(*shp, Hkv, Dh), cos, sin)
+        v = v.reshape(*shp, Hkv, Dh)
+        return q, k, v
+
+    def finish_block(self, blk: Block, x: torch.Tensor, attn: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        x = x + attn.reshape(*x.shape[:-1], cfg.n_heads * cfg.head_dim) @ blk.wo
+        h = self.rmsnorm(x, blk.norm2)
+        gu = h @ blk.wgu
+        g, u = gu.split(cfg.d_ff, dim=-1)
+        return x + (F.silu(g.float()) * u.float()).to(x.dtype) @ blk.wd
+
+    def logits(self, x: torch.Tensor) -> torch.Tensor:
+        return (self.rmsnorm(x, self.final_norm) @ self.lm_head).float()
+
+    # ------------------------------------------------------------------
+    @torch.no_grad()
+    def prefill_dense(self, ids: torch.Tensor, cache) -> torch.Tensor:
+        """Prompt pass for every sequence at positions [0, L): fills every KV
+        slot and returns the full-depth logits at the last position (B, V)."""
+        cfg = self.cfg
+        B, L = ids.shape
+        cos, sin = self.rope_tables(max(L, cache.S))
+        cos, sin = cos[:L], sin[:L]
+
+        def dense_block(blk, x, slot):
+            q, k, v = self.qkv(blk, x, cos, sin)                         # (B, L, H|Hkv, Dh)
+            cache.write_prefill(slot, k, v)
+            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               is_causal=True, enable_gqa=cfg.n_heads != cfg.n_kv_heads)
+            return self.finish_block(blk, x, o.transpose(1, 2))
+
+        x = self.embed[ids]
+        for i, blk in enumerate(self.prelude):
+            x = dense_block(blk, x, cfg.slot_prelude(i))
+        e = x
+        h = torch.zeros_like(e)
+        for r in range(cfg.T_total):
+            h = h + e
+            for l, blk in enumerate(self.core):
+                h = dense_block(blk, h, cfg.slot_core(r, l))
+        x = h
+        for i, blk in enumerate(self.coda):
+            x = dense_block(blk, x, cfg.slot_coda(i))
+        return self.logits(x[:, -1])

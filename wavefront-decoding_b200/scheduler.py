@@ -6,7 +6,7 @@ Mirrors the reference's `src/decoding/scheduler_batch.py` (`generate_wavefront_b
 arguments, decisions and counters, so a trace from either implementation can be
 compared field by field.  The decision logic stays on the host (one token-id
 read-back per tick, as in the reference, `scheduler_batch.py:312`); every tensor
-operation runs in the `blocks` object (the GPU engine in batch_blocks.py).
+operation runs in the `blocks` object (the GPU engine, engine.WaveEngine).
 
 Per tick: P union (tokens queued for the prelude) -> R union (one loop step for
 every live wave token) -> route (commit point: step == T_total -> verify; draft
