@@ -51,8 +51,20 @@ CFG3 = dict(B=32, R=8, H=32, Hkv=8, Dh=128, L0=8192, W=8, seed=2, accept_seed=3)
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # timed attention kernel, from the ncu captures summarised under profiles/
-# (wave_decode_cfg2.md for the CUDA-core kernel, wave_tc_cfg2.md for tcgen05).
-NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920}
+# (wave_decode_cfg2.md for the CUDA-core kernel, wave_tc_cfg2.md / wave_tc_cfg3.md for tcgen05).
+# cfg3 was captured at batch 8 and scaled by the units processed (x4 at batch 32).
+NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
+                     ("cfg2", "tc"): 543_106_816 + 4_962_816,
+                     ("cfg3", "tc"): (2_189_256_960 + 9_662_464) * 4}
+
+
+def ncu_traffic(workload: str, tc: bool, c: dict):
+    """Captured DRAM bytes per launch, scaled to this run's batch (every sequence
+    reads the same bytes), or None when no capture covers the kernel."""
+    t = NCU_TRAFFIC_BYTES.get((workload, "tc" if tc else "cuda_core"))
+    if t is None:
+        return None
+    return int(t * c["B"] / (CFG2 if workload == "cfg2" else CFG3)["B"])
 
 
 def parse():
@@ -422,7 +434,7 @@ def run_wfd(args):
             "wave_rows_per_s": total_rows / (ms * 1e-3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": NCU_TRAFFIC_BYTES.get((args.workload, "tc" if tc else "cuda_core")),
+                         "traffic": ncu_traffic(args.workload, tc, c),
                          "algorithmic_bytes_per_launch": nbytes,
                          "kernel": kernel_name},
             "e2e": {"value": value_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

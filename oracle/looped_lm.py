@@ -25,11 +25,16 @@ def _rms(x, w, eps):
     return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
 
 
-def _rope(x, pos, theta):
+def _rope(x, pos, theta, style="half"):
+    """Pairs (i, i + Dh/2) ("half") or (2i, 2i + 1) ("interleaved") rotate by angle
+    pos * theta^(-2i/Dh)."""
     Dh = x.shape[-1]
     inv = 1.0 / (theta ** (torch.arange(0, Dh, 2, dtype=torch.float64) / Dh))
     ang = torch.outer(pos.double(), inv)            # (T, Dh/2)
     c, s = ang.cos()[:, None, :], ang.sin()[:, None, :]
+    if style == "interleaved":
+        a, b = x[..., 0::2], x[..., 1::2]
+        return torch.stack((a * c - b * s, a * s + b * c), dim=-1).flatten(-2)
     x1, x2 = x[..., : Dh // 2], x[..., Dh // 2:]
     return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1)
 
@@ -40,8 +45,9 @@ def _block(blk, x, cfg):
     pos = torch.arange(T)
     h = _rms(x, blk["norm1"], cfg["norm_eps"]) @ blk["wqkv"]
     q, k, v = torch.split(h, [H * Dh, Hkv * Dh, Hkv * Dh], dim=-1)
-    q = _rope(q.reshape(T, H, Dh), pos, cfg["rope_theta"])
-    k = _rope(k.reshape(T, Hkv, Dh), pos, cfg["rope_theta"])
+    style = cfg.get("rope_style", "half")
+    q = _rope(q.reshape(T, H, Dh), pos, cfg["rope_theta"], style)
+    k = _rope(k.reshape(T, Hkv, Dh), pos, cfg["rope_theta"], style)
     v = v.reshape(T, Hkv, Dh)
     G = H // Hkv
     k = k.repeat_interleave(G, dim=1)
@@ -96,5 +102,5 @@ def weights_from(model) -> tuple[dict, dict]:
          "coda": [blk(b) for b in model.coda]}
     c = model.cfg
     cfg = {k: getattr(c, k) for k in ("n_heads", "n_kv_heads", "head_dim", "d_ff", "T_total", "norm_eps",
-                                      "rope_theta")}
+                                      "rope_theta", "rope_style")}
     return W, cfg

@@ -8,8 +8,13 @@ test time; only the .npz / .json outputs are committed):
 It imports the reference's own `src/decoding/fa4_attention.py` (SDPA backend,
 `set_backend("sdpa")`) and `src/decoding/batch_kv_cache.py` on CPU.  The
 reference imports two helpers from its empty `external/parcae` submodule
-(fa4_attention.py:55-56); they are stubbed below because none of the code paths
-exercised here calls them.
+(fa4_attention.py:55-56); the fixture model's own functions
+(tests/parcae_fixture.py) stand in for them.
+
+Config 1 (end-to-end greedy decoding) runs the reference's own `ParcaeBlocks`
+with `ar_generate_parcae_blocks` and `generate_wavefront_dynamic` over the
+fixture model (seed 0, initial recurrent state "zero"), and stores the tokens,
+counters and final KV slot lengths.
 
 Inputs are drawn from torch CPU generators with fixed seeds and are NOT stored
 (except tiny index tables); the tests regenerate them with the same calls and
@@ -36,11 +41,11 @@ def import_reference(ref_root: str):
     for name in ("parcae_lm", "parcae_lm.modules", "parcae_lm.modules.mixer", "parcae_lm.modules.utils"):
         sys.modules.setdefault(name, types.ModuleType(name))
 
-    def _unused(*a, **k):  # pragma: no cover - never called on these paths
-        raise RuntimeError("parcae_lm stub called")
-
-    sys.modules["parcae_lm.modules.mixer"].norm = _unused
-    sys.modules["parcae_lm.modules.utils"].apply_rotary_emb_complex_like = _unused
+    # the fixture model's own RoPE / qk-norm stand in for parcae_lm's (qk-norm is
+    # off in the fixture and raises if called)
+    import parcae_fixture as pf
+    sys.modules["parcae_lm.modules.mixer"].norm = pf.qk_norm
+    sys.modules["parcae_lm.modules.utils"].apply_rotary_emb_complex_like = pf.apply_rotary_emb_complex_like
     sys.path.insert(0, ref_root)
     import src.decoding.fa4_attention as fa  # noqa: E402
     from src.decoding.batch_kv_cache import BatchStaticKVCache  # noqa: E402
@@ -161,11 +166,62 @@ def gen_scheduler() -> dict:
     return out
 
 
+def gen_config1(n_new: int = 64, T_total: int = 4, drafts=(1, 2, 4)) -> dict:
+    """Config 1: the reference's ParcaeBlocks on the fixture model, greedy, fp32,
+    SDPA backend; AR (ar_baseline.py:132-193) and WFD (scheduler.py:89-225)."""
+    import parcae_fixture as pf
+    from src.decoding.ar_baseline import ar_generate_parcae_blocks
+    from src.decoding.parcae_blocks import ParcaeBlocks
+    from src.decoding.policy import SsdPolicy
+    from src.decoding.scheduler import generate_wavefront_dynamic
+
+    model = pf.ParcaeFixture(seed=0).eval()
+    prompt = pf.config1_prompt()
+
+    def blocks():
+        b = ParcaeBlocks(model, T_total, max_seq_len=pf.MAX_SEQ)
+        b.state_init = "zero"
+        caches = []
+        orig = b.prefill
+
+        def prefill(*a, **k):
+            st, lg = orig(*a, **k)
+            caches.append(st.kv_cache)
+            return st, lg
+
+        b.prefill = prefill
+        return b, caches
+
+    def lens(cache):
+        return {str(k): int(v) for k, v in sorted(cache.seqlen.items())}
+
+    out = {"prompt_head": prompt[:8].tolist(), "n_new": n_new, "T_total": T_total,
+           "weight_sums": pf.weight_sums(model)}
+    b, caches = blocks()
+    toks, _ = ar_generate_parcae_blocks(b, prompt[None], n_new)
+    out["ar"] = {"tokens": [int(t) for t in toks], "seqlen": lens(caches[-1])}
+    for d in drafts:
+        b, caches = blocks()
+        toks, tr = generate_wavefront_dynamic(b, prompt, n_new, SsdPolicy(T_total=T_total, T_draft=d))
+        out[f"wfd_d{d}"] = {"tokens": [int(t) for t in toks], "seqlen": lens(caches[-1]),
+                            **{k: getattr(tr, k) for k in ("n_r_calls", "n_p_calls", "n_c_calls", "n_drafts_proposed",
+                                                           "n_drafts_accepted", "n_drafts_rejected",
+                                                           "n_rollback_events")}}
+        print(f"config1 T_draft={d}: {out[f'wfd_d{d}']['n_drafts_accepted']}/"
+              f"{out[f'wfd_d{d}']['n_drafts_proposed']} drafts accepted")
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", choices=["all", "config1"], default="all")
     args = ap.parse_args()
     fa, BSK = import_reference(args.reference)
+    if args.only in ("all", "config1"):
+        (HERE / "reference_config1.json").write_text(json.dumps(gen_config1(), indent=0) + "\n")
+    if args.only == "config1":
+        return
     data = {}
     data.update(gen_attention(fa))
     kv, log = gen_kv_cache(BSK)

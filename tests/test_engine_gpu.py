@@ -114,3 +114,41 @@ def test_engine_emulated_acceptance(cuda_dev):
         assert max(lens[s][b] for s in range(cfg.n_slots)) <= L + N + 2 * cfg.T_total
     from wavefront_decoding_b200 import runtime as rt
     assert rt.read_device_error(cuda_dev) == 0
+
+
+# ---------------------------------------------------------------------------
+# config 1: the reference's ParcaeBlocks tokens / counters / KV lengths
+# ---------------------------------------------------------------------------
+def _config1_engine():
+    import parcae_fixture as pf
+    from wavefront_decoding_b200.engine import WaveEngine
+    from wavefront_decoding_b200.looped_lm import LoopedLM
+    from test_config1 import GOLD
+    torch.backends.cuda.matmul.allow_tf32 = False
+    m = pf.ParcaeFixture(seed=0)
+    model = LoopedLM(pf.looped_config(m, GOLD["T_total"]), dtype=torch.float32, device="cuda")
+    model.load_weights(pf.to_looped_weights(m))
+    return WaveEngine(model, 1, 256), pf.config1_prompt()[None], GOLD
+
+
+def test_config1_ar_matches_reference(cuda_dev):
+    from wavefront_decoding_b200 import scheduler as sch
+    eng, prompt, gold = _config1_engine()
+    bt = sch.ar_generate_batch(eng, prompt, gold["n_new"])
+    assert bt.per_seq[0].tokens == gold["ar"]["tokens"]
+    lens = eng.cache.seqlen
+    assert {str(s): lens[s][0] for s in range(len(lens))} == gold["ar"]["seqlen"]
+
+
+@pytest.mark.parametrize("T_draft", [1, 2, 4])
+def test_config1_wfd_matches_reference(cuda_dev, T_draft):
+    from wavefront_decoding_b200 import scheduler as sch
+    eng, prompt, gold = _config1_engine()
+    g = gold[f"wfd_d{T_draft}"]
+    bt = sch.generate_wavefront_batch(eng, prompt, gold["n_new"], sch.SsdPolicy(gold["T_total"], T_draft), None)
+    t = bt.per_seq[0]
+    assert t.tokens == g["tokens"] == gold["ar"]["tokens"]
+    for k in ("n_drafts_proposed", "n_drafts_accepted", "n_drafts_rejected", "n_rollback_events"):
+        assert getattr(t, k) == g[k], k
+    lens = eng.cache.seqlen
+    assert {str(s): lens[s][0] for s in range(len(lens))} == g["seqlen"]

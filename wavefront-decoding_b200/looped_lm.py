@@ -39,6 +39,7 @@ class LoopedLMConfig:
     n_coda: int = 1
     T_total: int = 4          # loop depth R
     rope_theta: float = 10000.0
+    rope_style: str = "half"  # "half": dims i, i + Dh/2 rotate together; "interleaved": dims 2i, 2i+1
     norm_eps: float = 1e-6
     init_std: float = 0.02
 
@@ -99,6 +100,25 @@ class LoopedLM:
                                                                                            device=self.device)
         self._rope_cache = None
 
+    def load_weights(self, W: dict) -> "LoopedLM":
+        """Replace every weight from a dict of tensors: embed (V, d), final_norm (d),
+        lm_head (d, V), and lists prelude / core / coda of per-block dicts with
+        norm1, wqkv (d, (H + 2 Hkv) Dh), wo (H Dh, d), norm2, wgu (d, 2 d_ff), wd (d_ff, d)."""
+        def put(t, ref):
+            assert tuple(t.shape) == tuple(ref.shape), (tuple(t.shape), tuple(ref.shape))
+            return t.to(dtype=self.dtype, device=self.device).contiguous()
+
+        self.embed = put(W["embed"], self.embed)
+        self.final_norm = put(W["final_norm"], self.final_norm)
+        self.lm_head = put(W["lm_head"], self.lm_head)
+        for name in ("prelude", "core", "coda"):
+            blocks = getattr(self, name)
+            assert len(W[name]) == len(blocks)
+            for blk, wb in zip(blocks, W[name]):
+                for k in ("norm1", "wqkv", "wo", "norm2", "wgu", "wd"):
+                    setattr(blk, k, put(wb[k], getattr(blk, k)))
+        return self
+
     # ------------------------------------------------------------------
     def rope_tables(self, max_seq: int):
         if self._rope_cache is None or self._rope_cache[0].shape[0] < max_seq:
@@ -114,14 +134,18 @@ class LoopedLM:
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.norm_eps)
         return (y * w.float()).to(x.dtype)
 
-    @staticmethod
-    def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-        """Rotate-half RoPE; x (..., T, H, Dh), cos / sin (T, Dh/2) fp32."""
-        half = x.shape[-1] // 2
+    def apply_rope(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """RoPE on x (..., T, H, Dh) with cos / sin (T, Dh/2) fp32; the pair that
+        rotates by angle i is (i, i + Dh/2) ("half") or (2i, 2i + 1) ("interleaved")."""
         xf = x.float()
-        x1, x2 = xf[..., :half], xf[..., half:]
         c = cos.unsqueeze(-2)
         s = sin.unsqueeze(-2)
+        if self.cfg.rope_style == "interleaved":
+            xp = xf.reshape(*xf.shape[:-1], xf.shape[-1] // 2, 2)
+            a, b = xp[..., 0], xp[..., 1]
+            return torch.stack((a * c - b * s, a * s + b * c), dim=-1).flatten(-2).to(x.dtype)
+        half = x.shape[-1] // 2
+        x1, x2 = xf[..., :half], xf[..., half:]
         return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1).to(x.dtype)
 
     def qkv(self, blk: Block, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
