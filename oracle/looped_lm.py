@@ -39,7 +39,9 @@ def _rope(x, pos, theta, style="half"):
     return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1)
 
 
-def _block(blk, x, cfg):
+def _block(blk, x, cfg, kv_out=None):
+    """One block over positions [0, T); appends the stored (post-RoPE) K and the
+    V, each (T, Hkv, Dh), to kv_out when given."""
     T = x.shape[0]
     H, Hkv, Dh = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]
     pos = torch.arange(T)
@@ -49,6 +51,8 @@ def _block(blk, x, cfg):
     q = _rope(q.reshape(T, H, Dh), pos, cfg["rope_theta"], style)
     k = _rope(k.reshape(T, Hkv, Dh), pos, cfg["rope_theta"], style)
     v = v.reshape(T, Hkv, Dh)
+    if kv_out is not None:
+        kv_out.append((k, v))
     G = H // Hkv
     k = k.repeat_interleave(G, dim=1)
     v = v.repeat_interleave(G, dim=1)
@@ -62,20 +66,50 @@ def _block(blk, x, cfg):
     return x + (torch.nn.functional.silu(g) * u) @ blk["wd"]
 
 
-def last_logits(W: dict, cfg: dict, ids: torch.Tensor) -> torch.Tensor:
+def last_logits(W: dict, cfg: dict, ids: torch.Tensor, draft_depth: int | None = None) -> torch.Tensor:
+    """Logits at the last position of `ids` after the full T_total loop steps.
+    With draft_depth d, the last position leaves the loop after d steps instead
+    (a draft): its coda attends to the earlier positions' full-depth coda K/V
+    and to its own depth-d row, as the draft C pass of a wavefront does
+    (parcae_blocks.py:472-518, the draft copy is taken at step == T_draft,
+    :567-573)."""
     x = W["embed"][ids]
     for blk in W["prelude"]:
         x = _block(blk, x, cfg)
     e = x
     h = torch.zeros_like(e)
-    for _ in range(cfg["T_total"]):
+    h_draft = None
+    for r in range(cfg["T_total"]):
         h = h + e
         for blk in W["core"]:
             h = _block(blk, h, cfg)
-    x = h
+        if draft_depth is not None and r + 1 == draft_depth:
+            h_draft = h[-1:].clone()
+    x = h if h_draft is None else torch.cat((h[:-1], h_draft))
     for blk in W["coda"]:
         x = _block(blk, x, cfg)
     return _rms(x[-1], W["final_norm"], cfg["norm_eps"]) @ W["lm_head"]
+
+
+def slot_kv(W: dict, cfg: dict, ids: torch.Tensor) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """K / V that every slot holds for positions [0, len(ids)) after sequential
+    decoding, indexed by slot id: prelude layer i -> i, core (depth r, layer l)
+    -> n_prelude + r * n_core + l, coda layer i -> n_prelude + T_total * n_core + i
+    (kv_cache.py:12-15).  A causal recompute produces exactly the entries that
+    incremental decoding caches."""
+    kv = []
+    x = W["embed"][ids]
+    for blk in W["prelude"]:
+        x = _block(blk, x, cfg, kv)
+    e = x
+    h = torch.zeros_like(e)
+    for _ in range(cfg["T_total"]):
+        h = h + e
+        for blk in W["core"]:
+            h = _block(blk, h, cfg, kv)
+    for blk in W["coda"]:
+        h = _block(blk, h, cfg, kv)
+    return kv
 
 
 def greedy_generate(W: dict, cfg: dict, prompt: list[int], n_new: int) -> list[int]:

@@ -152,3 +152,38 @@ def test_config1_wfd_matches_reference(cuda_dev, T_draft):
         assert getattr(t, k) == g[k], k
     lens = eng.cache.seqlen
     assert {str(s): lens[s][0] for s in range(len(lens))} == g["seqlen"]
+
+
+def _check_cache_vs_oracle(eng, model, prompts, per_seq, tol):
+    """Every K / V the engine cached for the committed positions equals the
+    full-recompute oracle's: each depth's hidden state was computed exactly once
+    and at the right depth."""
+    from oracle import looped_lm as olm
+    W, c = olm.weights_from(model)
+    K, V = eng.cache.K, eng.cache.V
+    for b, tr in enumerate(per_seq):
+        ids = torch.cat([prompts[b], torch.tensor(tr.tokens[:-1], dtype=prompts.dtype)])
+        ref = olm.slot_kv(W, c, ids)
+        n = ids.numel()
+        assert len(ref) == model.cfg.n_slots
+        for s, (k, v) in enumerate(ref):
+            dk = (K[s, b, :n].double().cpu() - k).abs().max().item()
+            dv = (V[s, b, :n].double().cpu() - v).abs().max().item()
+            assert dk < tol and dv < tol, (b, s, dk, dv)
+
+
+@pytest.mark.parametrize("T_draft", [1, 2, 4])
+def test_engine_cache_matches_oracle(cuda_dev, T_draft):
+    """Stronger than token equality (a looped model that converges in depth hides
+    depth mistakes from argmax): the cached K / V at every slot and committed
+    position, after sequential and after wavefront decoding."""
+    from wavefront_decoding_b200 import scheduler as sch
+    cfg = _small_cfg()
+    B, L, N = 2, 10, 14
+    prompts = _prompts(B, L, cfg.vocab, seed=12)
+    model, eng = _engine(cfg, B, L + N + 16)
+    if T_draft == 4:
+        bt = sch.ar_generate_batch(eng, prompts, N)
+    else:
+        bt = sch.generate_wavefront_batch(eng, prompts, N, sch.SsdPolicy(4, T_draft), None)
+    _check_cache_vs_oracle(eng, model, prompts, bt.per_seq, 2e-4)

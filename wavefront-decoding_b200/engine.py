@@ -51,7 +51,8 @@ class _Tables:
     4 R: slot base (depth * n_core), 5 live (q_len 1) / padding (0),
     6.. prelude / coda layers: first cache row of the row's (slot, sequence)."""
 
-    def __init__(self, cap: int, n_cols: int, device):
+    def __init__(self, kind: str, cap: int, n_cols: int, device):
+        self.kind = kind
         self.cap = cap
         self.n_cols = n_cols
         self.host = torch.zeros((cap, n_cols), dtype=torch.int32).pin_memory()
@@ -123,7 +124,7 @@ class WaveEngine:
         t = self._tables.get((kind, cap))
         seg_slots = self._seg_layers(kind)
         if t is None:
-            t = _Tables(cap, 6 + len(seg_slots), self.device)
+            t = _Tables(kind, cap, 6 + len(seg_slots), self.device)
             self._tables[(kind, cap)] = t
         if t.pending:
             t.uploaded.synchronize()
@@ -144,6 +145,15 @@ class WaveEngine:
         t.uploaded.record()
         t.pending = True
         return t
+
+    def _padding_rows(self, t: _Tables) -> torch.Tensor:
+        """A table of t's shape whose rows are all padding."""
+        pad = torch.zeros_like(t.dev)
+        pad[:, 0] = self.scratch_row
+        pad[:, 3] = self.scratch_seq
+        for j, slot in enumerate(self._seg_layers(t.kind)):
+            pad[:, 6 + j] = (slot * (self.B + 1) + self.scratch_seq) * self.S
+        return pad
 
     # ------------------------------------------------------------------
     # device-side bodies (captured into graphs)
@@ -195,16 +205,24 @@ class WaveEngine:
             self._body(kind, t)
             return
         if t.graph is None:
+            # The R body advances pool rows in place (not idempotent), so the
+            # warm-up runs see a table of padding rows only (scratch pool row,
+            # scratch sequence, q_len 0); the real table goes back before the
+            # first replay.
+            cur = torch.cuda.current_stream(self.device)
+            real = t.dev.clone()
+            t.dev.copy_(self._padding_rows(t))
             side = torch.cuda.Stream(self.device)
-            side.wait_stream(torch.cuda.current_stream(self.device))
+            side.wait_stream(cur)
             with torch.cuda.stream(side):
                 for _ in range(2):
                     self._body(kind, t)
-            torch.cuda.current_stream(self.device).wait_stream(side)
+            cur.wait_stream(side)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 self._body(kind, t)
             t.graph = g
+            t.dev.copy_(real)
         t.graph.replay()
         self.n_graph_replays += 1
 
