@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <utility>
 #include <mutex>
 
 #include "wfd_cache.cuh"
@@ -84,6 +85,25 @@ WsLayout ws_layout(int max_items, int head_dim, int sms, bool tc_only = false) {
   return w;
 }
 
+// Launch with programmatic stream serialization (the kernel calls
+// griddep_wait() before reading its predecessor's outputs).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <typename T, int DH, int NQ>
 int launch_decode_t(const DecodeParams& p, int sms, cudaStream_t st) {
   using C = DecodeCfg<T, DH, NQ>;
@@ -103,7 +123,8 @@ int launch_decode_t(const DecodeParams& p, int sms, cudaStream_t st) {
     attr_set[dev] = true;
   }
   const int grid = sms * occ_cache[dev];
-  wave_decode_kernel<T, DH, NQ><<<grid, C::THREADS, C::SMEM, st>>>(p);
+  if (launch_pdl(wave_decode_kernel<T, DH, NQ>, dim3(grid), dim3(C::THREADS), C::SMEM, st, p) != cudaSuccess)
+    return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
@@ -177,7 +198,8 @@ int launch_tc(const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& 
       return WFD_ERR_CUDA;
     attr_set[dev] = true;
   }
-  wave_tc_kernel<NQP><<<sms, kTcThreads, C::SMEM, st>>>(tk, tv, vp);
+  if (launch_pdl(wave_tc_kernel<NQP>, dim3(sms), dim3(kTcThreads), C::SMEM, st, tk, tv, vp) != cudaSuccess)
+    return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
@@ -285,11 +307,11 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     if (A.k_new != nullptr && A.k_app != nullptr) {
       // the tensor-core kernel reads every key through TMA: append the window
       // rows to the cache first (same stream, so the attention sees them)
-      append_segs_kernel<<<A.n, 256, 0, st>>>(pp.segs, A.n, static_cast<const char*>(A.k_new),
-                                              static_cast<const char*>(A.v_new), static_cast<char*>(A.k_app),
-                                              static_cast<char*>(A.v_app), (long long)A.Hkv * A.Dh * 2,
-                                              k_row_offset, A.lens, A.slot_offset * A.n_seqs);
-      if (cudaGetLastError() != cudaSuccess) return WFD_ERR_CUDA;
+      if (launch_pdl(append_segs_kernel, dim3(A.n), dim3(256), 0, st, (const Seg*)pp.segs, A.n,
+                     static_cast<const char*>(A.k_new), static_cast<const char*>(A.v_new),
+                     static_cast<char*>(A.k_app), static_cast<char*>(A.v_app), (long long)A.Hkv * A.Dh * 2,
+                     k_row_offset, A.lens, A.slot_offset * A.n_seqs) != cudaSuccess)
+        return WFD_ERR_CUDA;
     }
     VerifyParams vp;
     memset(&vp, 0, sizeof(vp));

@@ -50,6 +50,8 @@ __global__ void append_kernel(const char* k_new, const char* v_new, char* kc, ch
 // ahead of the tensor-core kernel, which reads every key through TMA.
 __global__ void append_segs_kernel(const Seg* segs, int n, const char* k_new, const char* v_new, char* kc, char* vc,
                                    long long row_bytes, long long k_row_offset, int32_t* lens, int lens_offset) {
+  griddep_launch_dependents();
+  griddep_wait();  // segs come from the plan kernel
   const int i = blockIdx.x;
   if (i >= n) return;
   const Seg S = segs[i];

@@ -178,6 +178,7 @@ __global__ void __launch_bounds__(128) wave_decode_kernel(const DecodeParams p) 
     fence_mbar_init();
     s_abort = 0;
   }
+  griddep_wait();  // plan outputs (segs, prefix) and the workspace
   __syncthreads();
   unsigned char* const wbase = smem + warp * C::WARP_BYTES;  // this warp's stage ring
   uint64_t* const wbar = full_bar[warp];

@@ -72,6 +72,7 @@ __device__ __forceinline__ long long block_excl_scan(long long x, long long* war
 }
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) {
+  griddep_launch_dependents();  // the attention kernel may run its prologue meanwhile
   __shared__ long long warp_tot[32];
   __shared__ long long s_total;
   long long carry = 0;

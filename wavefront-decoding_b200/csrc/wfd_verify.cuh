@@ -24,7 +24,9 @@
 // bounded and reports through the error word; no multicast, no cluster launch.
 //
 // Window keys are read from the KV cache: the caller appends the window rows
-// (append_segs_kernel) in a launch before this one.
+// (append_segs_kernel) in a launch before this one.  Launched with programmatic
+// stream serialization: barrier set-up and the TMEM allocation overlap the
+// previous kernel; griddep_wait() precedes every read of its outputs.
 #pragma once
 
 #include <cuda.h>
@@ -295,6 +297,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  griddep_wait();  // plan outputs, appended window rows and the workspace
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -307,13 +310,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     a = (long long)blockIdx.x * share;
     b = (a + share < total) ? a + share : total;
   }
+  // first segment of this CTA's share: the largest i with Hkv * prefix[i] <= a
+  // (prefix is non-decreasing).  A CTA-wide k-ary search: every round the 192
+  // threads probe 192 pivots of [lo, hi] at once, so up to 192 segments take
+  // one round of loads instead of a chain of dependent ones.
   int seg0 = 0;
   if (a < b) {
     int lo = 0, hi = p.n_segs - 1;
     while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if ((long long)p.Hkv * p.prefix[mid] <= a) lo = mid;
-      else hi = mid - 1;
+      const int span = hi - lo;
+      int piv = -1;
+      if (span <= kTcThreads) {
+        if (tid < span) piv = lo + 1 + tid;
+      } else {
+        piv = lo + (int)(((long long)(tid + 1) * span) / (kTcThreads + 1));
+      }
+      const int c = __syncthreads_count(piv >= 0 && (long long)p.Hkv * p.prefix[piv] <= a);
+      if (span <= kTcThreads) {
+        lo = hi = lo + c;
+      } else {
+        const int nlo = c == 0 ? lo : lo + (int)(((long long)c * span) / (kTcThreads + 1));
+        const int nhi = c == kTcThreads ? hi : lo + (int)(((long long)(c + 1) * span) / (kTcThreads + 1)) - 1;
+        lo = nlo;
+        hi = nhi;
+      }
     }
     seg0 = lo;
   }
@@ -620,15 +640,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else {
         const int slot = (ustart < a) ? 2 * (int)blockIdx.x : 2 * (int)blockIdx.x + 1;
         float* pb = p.ws_part + (size_t)slot * C::PART_FLOATS;
-        // every thread holds the same m[]; thread n publishes column n's (m, l)
-#pragma unroll
-        for (int n = 0; n < NQP; ++n) {
-          if (stid == n) {
-            pb[n] = mst[n];
-            pb[NQP + n] = lb[n] + lb[NQP + n] + lb[2 * NQP + n] + lb[3 * NQP + n];
-          }
-          pb[2 * NQP + n * 128 + dim] = oacc[n];
+        // every thread holds the same m[]; thread n publishes column n's (m, l);
+        // O^T only for the unit's query columns (the merge reads no others)
+        if (stid < NQP) {
+          pb[stid] = mst[stid];
+          pb[NQP + stid] = lb[stid] + lb[NQP + stid] + lb[2 * NQP + stid] + lb[3 * NQP + stid];
         }
+#pragma unroll
+        for (int n = 0; n < NQP; ++n)
+          if (n < nvec) pb[2 * NQP + n * 128 + dim] = oacc[n];
         __threadfence();
         softmax_bar();
         if (stid == 0) {
@@ -638,27 +658,56 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         softmax_bar();
         if (s_flag) {
           __threadfence();
-          for (int n = 0; n < nvec && n < NQP; ++n) {
-            float M = NEG_INF;
-            for (int k = 0; k < n_contrib; ++k) {
-              const int cc = c_first + k;
-              const int sl = (k == 0) ? 2 * cc + 1 : 2 * cc;
-              M = fmaxf(M, ld_cg_f32(p.ws_part + (size_t)sl * C::PART_FLOATS + n));
+          // Online merge, columns in chunks of MCH: this CTA's own (m, l, O) come
+          // from shared memory and registers; for every other contributor all
+          // loads of a chunk are independent (one round trip per contributor).
+          constexpr int MCH = NQP < 16 ? NQP : 16;
+          const int k_own = (int)blockIdx.x - c_first;
+#pragma unroll
+          for (int c0 = 0; c0 < NQP; c0 += MCH) {
+            if (c0 < nvec) {
+              float M[MCH], Ls[MCH], acc[MCH];
+#pragma unroll
+              for (int j = 0; j < MCH; ++j) {
+                M[j] = mst[c0 + j];
+                Ls[j] = lb[c0 + j] + lb[NQP + c0 + j] + lb[2 * NQP + c0 + j] + lb[3 * NQP + c0 + j];
+                acc[j] = oacc[c0 + j];
+              }
+              for (int k = 0; k < n_contrib; ++k) {
+                if (k == k_own) continue;
+                const int cc = c_first + k;
+                const int sl = (k == 0) ? 2 * cc + 1 : 2 * cc;
+                const float* base = p.ws_part + (size_t)sl * C::PART_FLOATS;
+                float mk[MCH], lk[MCH], ok[MCH];
+#pragma unroll
+                for (int j = 0; j < MCH; ++j) {
+                  mk[j] = ld_cg_f32(base + c0 + j);
+                  lk[j] = ld_cg_f32(base + NQP + c0 + j);
+                  ok[j] = (c0 + j < nvec) ? ld_cg_f32(base + 2 * NQP + (c0 + j) * 128 + dim) : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < MCH; ++j) {
+                  const float nm = fmaxf(M[j], mk[j]);
+                  if (nm != NEG_INF) {
+                    const float wa = (M[j] == NEG_INF) ? 0.f : fast_exp2(M[j] - nm);
+                    const float wb = (mk[j] == NEG_INF) ? 0.f : fast_exp2(mk[j] - nm);
+                    Ls[j] = Ls[j] * wa + lk[j] * wb;
+                    acc[j] = acc[j] * wa + ok[j] * wb;
+                    M[j] = nm;
+                  }
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < MCH; ++j) {
+                const int n = c0 + j;
+                if (n < nvec) {
+                  const int v = qg * NQP + n;
+                  const int row = v / p.G, g = v % p.G;
+                  static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * 128 + dim] =
+                      __float2bfloat16_rn(Ls[j] > 0.f ? acc[j] / Ls[j] : 0.f);
+                }
+              }
             }
-            float Ls = 0.f, acc = 0.f;
-            for (int k = 0; k < n_contrib; ++k) {
-              const int cc = c_first + k;
-              const int sl = (k == 0) ? 2 * cc + 1 : 2 * cc;
-              const float* base = p.ws_part + (size_t)sl * C::PART_FLOATS;
-              const float mk = ld_cg_f32(base + n);
-              const float wgt = (mk == NEG_INF) ? 0.f : fast_exp2(mk - M);
-              Ls += wgt * ld_cg_f32(base + NQP + n);
-              acc += wgt * ld_cg_f32(base + 2 * NQP + n * 128 + dim);
-            }
-            const int v = qg * NQP + n;
-            const int row = v / p.G, g = v % p.G;
-            static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * 128 + dim] =
-                __float2bfloat16_rn(Ls > 0.f ? acc / Ls : 0.f);
           }
           if (stid == 0) p.ws_cnt[c_first] = 0;
         }
