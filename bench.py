@@ -48,6 +48,7 @@ FALLBACK_HBM_GBS = 6650.0
 
 CFG2 = dict(B=8, R=8, H=16, Hkv=4, Dh=128, S=4096, seed=1)
 CFG3 = dict(B=32, R=8, H=32, Hkv=8, Dh=128, L0=8192, W=8, seed=2, accept_seed=3)
+CFG4 = dict(B=64, L=1024, new=256, seed=4, model_seed=0, emu_seed=5)
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # timed attention kernel, from the ncu captures summarised under profiles/
@@ -73,8 +74,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=4000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2")
-    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (default: the config's)")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU (cfg2 / cfg3) or in total over all GPUs (cfg4); default: the config's")
+    ap.add_argument("--t-draft", type=int, default=2, help="cfg4: draft depth T_draft")
+    ap.add_argument("--new-tokens", type=int, default=None, help="cfg4: generated tokens per sequence")
+    ap.add_argument("--alpha", type=float, default=None,
+                    help="cfg4: emulated draft acceptance rate (default: greedy gold == draft)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", type=int, default=-1, choices=[-1, 0, 1],
@@ -256,6 +262,11 @@ def run_reference(args):
     """--impl reference: the reference's CPU path, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload == "cfg4":
+        print(json.dumps({"impl": "reference", "unavailable": "cfg4 (end-to-end 381M-parameter model, 64 x 1024 "
+                          "prompts, 256 tokens) is not timed on the host cores; the reference arm covers the "
+                          "attention configs 2 and 3"}), flush=True)
         return
     if args.workload == "cfg2":
         c, q, K, V, kn, vn, items = cfg2_cpu_inputs(CFG2["seed"], args.batch)
@@ -462,10 +473,142 @@ def run_wfd(args):
         print(json.dumps(line), flush=True)
 
 
+def run_cfg4(args):
+    """Config 4: end-to-end greedy wavefront decoding of the looped LM (random
+    init, bf16) through the engine and scheduler; one step = one generation of
+    `new` tokens for this rank's sequences (prefill included in e2e only)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from wavefront_decoding_b200 import runtime as rt
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.engine import WaveEngine
+    from wavefront_decoding_b200.looped_lm import CONFIG4, LoopedLM
+
+    cfg = CONFIG4
+    Bg = args.batch or CFG4["B"]
+    if Bg % world:
+        raise SystemExit(f"global batch {Bg} is not divisible by {world} ranks")
+    Bl = Bg // world
+    L, new = CFG4["L"], args.new_tokens or CFG4["new"]
+    prompts_all = torch.randint(0, cfg.vocab, (Bg, L), generator=torch.Generator().manual_seed(CFG4["seed"]))
+    prompts = prompts_all[rank * Bl:(rank + 1) * Bl].contiguous().pin_memory()
+    model = LoopedLM(cfg, seed=CFG4["model_seed"], dtype=torch.bfloat16, device=dev)
+    eng = WaveEngine(model, Bl, L + new + 2 * cfg.T_total + 8)
+    policy = sch.SsdPolicy(cfg.T_total, args.t_draft)
+
+    ev_all0, ev_dec0, ev_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+
+    def generate():
+        emus = None
+        if args.alpha is not None:
+            emus = [sch.EmulatedAcceptance(args.alpha, seed=CFG4["emu_seed"] * 1_000_003 + rank * Bl + b)
+                    for b in range(Bl)]
+        orig = eng.prefill
+
+        def prefill(ids):
+            out = orig(ids)
+            ev_dec0.record()
+            return out
+
+        eng.prefill = prefill
+        try:
+            ev_all0.record()
+            bt = sch.generate_wavefront_batch(eng, prompts, new, policy, emus)
+            ev_end.record()
+            torch.cuda.synchronize()
+        finally:
+            del eng.prefill
+        return bt, ev_dec0.elapsed_time(ev_end), ev_all0.elapsed_time(ev_end)
+
+    for _ in range(max(1, args.warmup)):
+        generate()
+    rt.read_device_error(dev)
+    eng.reset_counters()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    dec_ms = all_ms = 0.0
+    tokens = proposed = accepted = ticks = 0
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            bt, d_ms, a_ms = generate()
+            dec_ms += d_ms
+            all_ms += a_ms
+            tokens += bt.n_tokens
+            proposed += sum(t.n_drafts_proposed for t in bt.per_seq)
+            accepted += sum(t.n_drafts_accepted for t in bt.per_seq)
+            ticks += bt.n_r_calls
+    torch.cuda.synchronize()
+    rt.read_device_error(dev)
+    kv_bytes = eng.kv_read_bytes
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        t = torch.tensor([dec_ms, all_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dec_max, all_max = t.tolist()
+        c = torch.tensor([tokens, proposed, accepted, kv_bytes], dtype=torch.float64, device=dev)
+        dist.all_reduce(c, op=dist.ReduceOp.SUM)
+        tot_tokens, tot_prop, tot_acc, tot_kv = c.tolist()
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    else:
+        dec_max, all_max = dec_ms, all_ms
+        tot_tokens, tot_prop, tot_acc, tot_kv = tokens, proposed, accepted, kv_bytes
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    value = tot_tokens / (dec_max * 1e-3)
+    kv_gbs = kv_bytes / (dec_ms * 1e-3) / 1e9      # rank 0's attention KV reads over its decode time
+    h2d = prompts.numel() * prompts.element_size()
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(1, args.warmup), "ms_per_step": dec_max / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, "
+        "uniform random prompt ids)",
+        "config": {"workload": "cfg4_looped_lm_e2e_greedy_decode",
+                   "model": f"looped LM {cfg.n_params() / 1e6:.0f}M params: vocab {cfg.vocab}, d {cfg.d_model}, "
+                            f"{cfg.n_heads}x{cfg.head_dim} heads (kv {cfg.n_kv_heads}), SwiGLU {cfg.d_ff}, "
+                            f"prelude {cfg.n_prelude} / core {cfg.n_core} x R={cfg.T_total} / coda {cfg.n_coda}",
+                   "global_batch": Bg, "batch_per_gpu": Bl, "prompt_len": L, "new_tokens": new,
+                   "T_draft": args.t_draft,
+                   "acceptance": "greedy gold == draft" if args.alpha is None else f"emulated Bernoulli({args.alpha})",
+                   "parallelism": f"sequences sharded, {world} rank(s), no collective on the hot path",
+                   "timing": "decode region per generation, CUDA events, max over ranks; "
+                             "KV working set > L2, no flush"},
+        "tokens_per_s_per_gpu": value / world,
+        "acceptance_rate": (tot_acc / tot_prop) if tot_prop else None,
+        "ticks_per_generation": ticks / args.steps,
+        "roofline": {"bound": "hbm", "achieved": kv_gbs, "peak": peak, "unit": "GB/s", "frac": kv_gbs / peak,
+                     "peak_kind": peak_kind, "traffic": None,
+                     "note": "attention K/V bytes read by live rows over the whole decode wall time "
+                             "(GEMMs, host scheduling and launches included in the time)"},
+        "e2e": {"value": tot_tokens / (all_max * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": eng.d2h_bytes // args.steps, "ms_per_step": all_max / args.steps,
+                "includes": "prefill, prompt upload from pinned host memory, per-tick greedy-id read-back"},
+        "gpu_launches": eng.wfd_launches,
+        "clocks": clk.summary(),
+        "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg4":
+        run_cfg4(args)
     else:
         run_wfd(args)
 

@@ -212,6 +212,35 @@ int wfd_gather_pack(const void* k_cache, const void* v_cache, void* k_pack, void
                     int32_t max_seq, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t* d_err,
                     void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Looped-LM block helpers used by the wavefront engine around the attention
+ * (fused element-wise work of one transformer block; fp32 arithmetic, bf16 or
+ * f32 storage).  The reference runs these as framework modules (norm, RoPE in
+ * fa4_attention.compute_qkv, fa4_attention.py:140-160, the SwiGLU MLP), so they
+ * have no C counterpart in it.
+ * ------------------------------------------------------------------------- */
+
+/* RMSNorm: y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w for n rows of d
+ * (d % 8 == 0; x, w, y 16-byte aligned; y does not overlap x). */
+int wfd_rmsnorm(const void* x, const void* w, void* y, int32_t n, int32_t d, float eps, int32_t dtype,
+                void* stream);
+
+/* Split a fused QKV projection qkv (n, (H + 2 Hkv) * Dh) into q (n, H, Dh),
+ * k (n, Hkv, Dh) rotated by RoPE and v (n, Hkv, Dh).  style 0 rotates dims
+ * (i, i + Dh/2), style 1 dims (2i, 2i + 1), by angle pos * theta_i with cos / sin
+ * tables (max_pos, Dh/2) fp32.  Row r's position is pos[r * pos_stride] (device
+ * int32), or r % pos_period when pos is NULL.  A position outside [0, max_pos)
+ * sets the bad-position bit of the device error word d_err (wfd_read_error)
+ * and uses position 0. */
+int wfd_rope_split(const void* qkv, const float* cos_tab, const float* sin_tab, const int32_t* pos,
+                   int32_t pos_stride, int32_t pos_period, int32_t max_pos, void* q, void* k, void* v, int32_t n,
+                   int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t style, int32_t dtype,
+                   int32_t* d_err, void* stream);
+
+/* SwiGLU gate: out (n, dff) = silu(g) * u where gu (n, 2 dff) = [g | u] per row
+ * (dff % 8 == 0). */
+int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,91 @@
+"""Fused looped-LM block kernels (RMSNorm, RoPE + QKV split, SwiGLU gate)
+against plain fp32 torch arithmetic of the same op."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import golden_inputs as gi
+
+pytestmark = pytest.mark.gpu
+
+
+def _tol(dt):
+    return 1e-5 if dt == torch.float32 else 2e-2
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n,d", [(1, 256), (37, 512), (200, 1536)])
+def test_rmsnorm(cuda_dev, dt, n, d):
+    from wavefront_decoding_b200 import fused
+    g = gi.gen(31)
+    x = (torch.randn((n, d), generator=g) * 3).to(dt).to(cuda_dev)
+    w = (torch.rand((d,), generator=g) + 0.5).to(dt).to(cuda_dev)
+    y = fused.rmsnorm(x, w, 1e-6)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    assert (y.float() - ref).abs().max().item() <= _tol(dt) * max(1.0, ref.abs().max().item())
+
+
+def _rope_ref(x, pos, cos, sin, interleaved):
+    xf = x.float()
+    c, s = cos[pos][:, None, :], sin[pos][:, None, :]
+    if interleaved:
+        a, b = xf[..., 0::2], xf[..., 1::2]
+        return torch.stack((a * c - b * s, a * s + b * c), dim=-1).flatten(-2)
+    h = x.shape[-1] // 2
+    a, b = xf[..., :h], xf[..., h:]
+    return torch.cat((a * c - b * s, b * c + a * s), dim=-1)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("interleaved", [False, True])
+@pytest.mark.parametrize("H,Hkv,Dh", [(8, 8, 64), (16, 4, 128), (24, 24, 64)])
+def test_rope_split(cuda_dev, dt, interleaved, H, Hkv, Dh):
+    from wavefront_decoding_b200 import fused
+    g = gi.gen(32)
+    n, S = 45, 300
+    qkv = torch.randn((n, (H + 2 * Hkv) * Dh), generator=g).to(dt).to(cuda_dev)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, Dh, 2, dtype=torch.float64) / Dh))
+    ang = torch.outer(torch.arange(S, dtype=torch.float64), inv)
+    cos, sin = ang.cos().float().to(cuda_dev), ang.sin().float().to(cuda_dev)
+    # positions as a strided column of an int32 table (as the engine passes them)
+    tab = torch.randint(0, S, (n, 3), generator=g, dtype=torch.int32).to(cuda_dev)
+    pos = tab[:, 1]
+    q, k, v = fused.rope_split(qkv, cos, sin, H, Hkv, Dh, pos=pos, interleaved=interleaved)
+    qs, ks, vs = torch.split(qkv, [H * Dh, Hkv * Dh, Hkv * Dh], dim=-1)
+    pl = pos.long()
+    tol = _tol(dt) * 4
+    assert (q.float() - _rope_ref(qs.reshape(n, H, Dh), pl, cos, sin, interleaved)).abs().max().item() <= tol
+    assert (k.float() - _rope_ref(ks.reshape(n, Hkv, Dh), pl, cos, sin, interleaved)).abs().max().item() <= tol
+    assert torch.equal(v, vs.reshape(n, Hkv, Dh))
+    # period form: rows are L consecutive positions per sequence
+    L = 9
+    q2, k2, _ = fused.rope_split(qkv, cos, sin, H, Hkv, Dh, pos_period=L, interleaved=interleaved)
+    pp = torch.arange(n, device=cuda_dev) % L
+    assert (q2.float() - _rope_ref(qs.reshape(n, H, Dh), pp, cos, sin, interleaved)).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_silu_mul(cuda_dev, dt):
+    from wavefront_decoding_b200 import fused
+    g = gi.gen(33)
+    gu = (torch.randn((70, 2 * 4096), generator=g) * 2).to(dt).to(cuda_dev)
+    out = fused.silu_mul(gu)
+    a, b = gu.float().split(4096, dim=-1)
+    ref = torch.nn.functional.silu(a) * b
+    assert (out.float() - ref).abs().max().item() <= _tol(dt) * max(1.0, ref.abs().max().item())
+
+
+def test_rope_bad_position_sets_error(cuda_dev):
+    from wavefront_decoding_b200 import _abi, fused
+    from wavefront_decoding_b200 import runtime as rt
+    assert rt.read_device_error(cuda_dev) == 0
+    qkv = torch.zeros((2, 3 * 64), device=cuda_dev)
+    cos = torch.ones((4, 32), device=cuda_dev)
+    sin = torch.zeros((4, 32), device=cuda_dev)
+    pos = torch.tensor([1, 7], dtype=torch.int32, device=cuda_dev)   # 7 >= 4 table rows
+    fused.rope_split(qkv, cos, sin, 1, 1, 64, pos=pos)
+    with pytest.raises(_abi.WfdError):
+        rt.read_device_error(cuda_dev)           # reads and clears the word
+    assert rt.read_device_error(cuda_dev) == 0

@@ -23,6 +23,7 @@ EXPORTED = (
     "wfd_wave_attn", "wfd_wave_attn_static", "wfd_wave_attn_kernel", "wfd_attn_varlen", "wfd_attn_segments",
     "wfd_append",
     "wfd_write_prefill", "wfd_commit_drop", "wfd_commit_window", "wfd_gather_pack",
+    "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul",
 )
 
 
@@ -69,6 +70,12 @@ _SIGS = {
     "wfd_commit_window": ([_P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     # kc vc kp vp slots seqs cu_k n n_slots n_seqs max_seq Hkv Dh dtype err stream
     "wfd_gather_pack": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
+    # x w y n d eps dtype stream
+    "wfd_rmsnorm": ([_P, _P, _P, _I, _I, _F, _I, _P], _I),
+    # qkv cos sin pos pos_stride pos_period max_pos q k v n H Hkv Dh style dtype err stream
+    "wfd_rope_split": ([_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P], _I),
+    # gu out n dff dtype stream
+    "wfd_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
 }
 
 _lock = threading.Lock()

@@ -13,6 +13,7 @@
 #include "wfd_cache.cuh"
 #include "wfd_common.cuh"
 #include "wfd_decode.cuh"
+#include "wfd_model.cuh"
 #include "wfd_plan.cuh"
 #include "wfd_verify.cuh"
 
@@ -692,3 +693,82 @@ int wfd_gather_pack(const void* k_cache, const void* v_cache, void* k_pack, void
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// looped-LM block helpers
+// ---------------------------------------------------------------------------
+namespace {
+int model_grid(long long work) {
+  const int sms = current_sms();
+  long long g = (work + kModelThreads - 1) / kModelThreads;
+  const long long cap = (long long)(sms > 0 ? sms : 148) * 8;
+  if (g > cap) g = cap;
+  return g < 1 ? 1 : (int)g;
+}
+}  // namespace
+
+extern "C" int wfd_rmsnorm(const void* x, const void* w, void* y, int32_t n, int32_t d, float eps, int32_t dtype,
+                           void* stream) {
+  if (n < 0 || d <= 0 || d % 8 != 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!x || !w || !y) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return WFD_ERR_ALIGNMENT;
+  const int grid = (n + kModelThreads / 32 - 1) / (kModelThreads / 32);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == WFD_DTYPE_BF16)
+    rmsnorm_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                                   static_cast<const __nv_bfloat16*>(w),
+                                                                   static_cast<__nv_bfloat16*>(y), n, d, eps);
+  else if (dtype == WFD_DTYPE_F32)
+    rmsnorm_kernel<float><<<grid, kModelThreads, 0, st>>>(static_cast<const float*>(x), static_cast<const float*>(w),
+                                                         static_cast<float*>(y), n, d, eps);
+  else
+    return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+extern "C" int wfd_rope_split(const void* qkv, const float* cos_tab, const float* sin_tab, const int32_t* pos,
+                              int32_t pos_stride, int32_t pos_period, int32_t max_pos, void* q, void* k, void* v,
+                              int32_t n, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t style,
+                              int32_t dtype, int32_t* d_err, void* stream) {
+  if (n < 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 2 != 0 || max_pos <= 0)
+    return WFD_ERR_INVALID_ARG;
+  if (style != 0 && style != 1) return WFD_ERR_INVALID_ARG;
+  if (!pos && pos_period <= 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!qkv || !cos_tab || !sin_tab || !q || !k || !v || !d_err) return WFD_ERR_INVALID_ARG;
+  const long long work = (long long)n * (n_heads + 2 * n_kv_heads) * (head_dim / 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = model_grid(work);
+  if (dtype == WFD_DTYPE_BF16)
+    rope_split_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(qkv), cos_tab, sin_tab, pos, pos_stride, pos_period,
+        static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), n, n_heads,
+        n_kv_heads, head_dim, style, max_pos, d_err);
+  else if (dtype == WFD_DTYPE_F32)
+    rope_split_kernel<float><<<grid, kModelThreads, 0, st>>>(
+        static_cast<const float*>(qkv), cos_tab, sin_tab, pos, pos_stride, pos_period, static_cast<float*>(q),
+        static_cast<float*>(k), static_cast<float*>(v), n, n_heads, n_kv_heads, head_dim, style, max_pos, d_err);
+  else
+    return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+extern "C" int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, int32_t dtype, void* stream) {
+  if (n < 0 || dff <= 0 || dff % 8 != 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!gu || !out) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(gu) || !aligned16(out)) return WFD_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = model_grid((long long)n * (dff / 8));
+  if (dtype == WFD_DTYPE_BF16)
+    silu_mul_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(gu),
+                                                                    static_cast<__nv_bfloat16*>(out), n, dff);
+  else if (dtype == WFD_DTYPE_F32)
+    silu_mul_kernel<float><<<grid, kModelThreads, 0, st>>>(static_cast<const float*>(gu), static_cast<float*>(out),
+                                                          n, dff);
+  else
+    return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+

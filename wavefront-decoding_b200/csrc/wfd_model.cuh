@@ -1,0 +1,153 @@
+// Fused element-wise kernels of the looped-LM blocks that surround the
+// wavefront attention in the engine: RMSNorm, the RoPE + split of a fused QKV
+// projection, and the SwiGLU gate.  Each replaces a chain of framework
+// element-wise launches (fp32 up-cast, pow / mean / rsqrt / mul, slicing,
+// concatenation, down-cast) by one launch that reads its input once and writes
+// its output once; all arithmetic is fp32 whatever the storage type.
+#pragma once
+
+#include "wfd_common.cuh"
+
+namespace wfd {
+
+constexpr int kModelThreads = 256;
+
+template <typename T>
+struct Vec8;  // 8 elements in one 16-byte (bf16) or two 16-byte (f32) accesses
+
+template <>
+struct Vec8<__nv_bfloat16> {
+  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  __device__ __forceinline__ static void store(__nv_bfloat16* p, const float (&v)[8]) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+};
+
+template <>
+struct Vec8<float> {
+  __device__ __forceinline__ static void load(const float* p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  __device__ __forceinline__ static void store(float* p, const float (&v)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T x);
+template <>
+__device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <typename T>
+__device__ __forceinline__ T from_f(float x);
+template <>
+__device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w, one warp per row, d % 8 == 0.
+template <typename T>
+__global__ void __launch_bounds__(kModelThreads) rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                                 T* __restrict__ y, int n, int d, float eps) {
+  const int row = blockIdx.x * (kModelThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  const T* xr = x + (long long)row * d;
+  T* yr = y + (long long)row * d;
+  float ss = 0.f;
+  for (int c = lane * 8; c < d; c += 256) {
+    float v[8];
+    Vec8<T>::load(xr + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / (float)d + eps);
+  for (int c = lane * 8; c < d; c += 256) {
+    float v[8], g[8];
+    Vec8<T>::load(xr + c, v);
+    Vec8<T>::load(w + c, g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
+    Vec8<T>::store(yr + c, v);
+  }
+}
+
+// qkv (n, (H + 2 Hkv) * Dh) -> q (n, H, Dh) and k (n, Hkv, Dh) rotated by RoPE at
+// each row's position, v (n, Hkv, Dh) copied.  The rotation pairs dims (i, i + Dh/2)
+// (style 0) or (2i, 2i + 1) (style 1) by the angle of frequency i; cos / sin are
+// (positions, Dh/2) fp32 tables.  Row r's position is pos[r * pos_stride], or
+// r % pos_period when pos is null (a prompt of pos_period tokens per sequence).
+template <typename T>
+__global__ void __launch_bounds__(kModelThreads)
+    rope_split_kernel(const T* __restrict__ qkv, const float* __restrict__ cosb, const float* __restrict__ sinb,
+                      const int32_t* __restrict__ pos, int pos_stride, int pos_period, T* __restrict__ q,
+                      T* __restrict__ k, T* __restrict__ v, int n, int H, int Hkv, int Dh, int style, int max_pos,
+                      int* err) {
+  const int half = Dh >> 1;
+  const int heads = H + 2 * Hkv;
+  const long long per_row = (long long)heads * half;  // element pairs per row
+  const long long total = (long long)n * per_row;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(e / per_row);
+    const int rem = (int)(e - (long long)r * per_row);
+    const int hh = rem / half, i = rem - hh * half;
+    const T* src = qkv + (long long)r * heads * Dh + (long long)hh * Dh;
+    const int i0 = style ? 2 * i : i, i1 = style ? 2 * i + 1 : i + half;
+    const float a = to_f(src[i0]), b = to_f(src[i1]);
+    if (hh >= H + Hkv) {  // v: plain copy
+      T* dst = v + ((long long)r * Hkv + (hh - H - Hkv)) * Dh;
+      dst[i0] = src[i0];
+      dst[i1] = src[i1];
+      continue;
+    }
+    int p = pos ? pos[(long long)r * pos_stride] : (r % pos_period);
+    if (p < 0 || p >= max_pos) {
+      set_error(err, kErrBadPos);
+      p = 0;
+    }
+    const float c = cosb[(long long)p * half + i], s = sinb[(long long)p * half + i];
+    T* dst = hh < H ? q + ((long long)r * H + hh) * Dh : k + ((long long)r * Hkv + (hh - H)) * Dh;
+    dst[i0] = from_f<T>(a * c - b * s);
+    dst[i1] = from_f<T>(b * c + a * s);
+  }
+}
+
+// out (n, dff) = silu(g) * u for gu (n, 2 dff) = [g | u] per row, dff % 8 == 0.
+template <typename T>
+__global__ void __launch_bounds__(kModelThreads) silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out,
+                                                                  int n, int dff) {
+  const int vpr = dff / 8;
+  const long long total = (long long)n * vpr;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(e / vpr), c = (int)(e - (long long)r * vpr) * 8;
+    float g[8], u[8];
+    Vec8<T>::load(gu + (long long)r * 2 * dff + c, g);
+    Vec8<T>::load(gu + (long long)r * 2 * dff + dff + c, u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) g[i] = g[i] / (1.f + expf(-g[i])) * u[i];
+    Vec8<T>::store(out + (long long)r * dff + c, g);
+  }
+}
+
+}  // namespace wfd

@@ -90,12 +90,23 @@ class WaveEngine:
         self.pool_h = torch.zeros((self.pool_cap + 1, d), dtype=model.dtype, device=self.device)
         self.pool_e = torch.zeros((self.pool_cap + 1, d), dtype=model.dtype, device=self.device)
         self._next_row = 0
-        self.cos, self.sin = model.rope_tables(max_seq_len)
+        model.rope_tables(max_seq_len)
         self._tables: dict[tuple[str, int], _Tables] = {}
         rt.reserve_workspace(self.device, _BUCKETS[-1], cfg.head_dim)
         rt.error_word(self.device)
         self.n_graph_replays = 0
         self.n_launch_calls = 0
+        # accounting (host side, exact): K/V bytes the attention of live rows
+        # reads, libwfd kernel launches, bytes read back per C union
+        self._row_bytes = cfg.n_kv_heads * cfg.head_dim * torch.finfo(model.dtype).bits // 8
+        tc = model.dtype == torch.bfloat16 and cfg.head_dim == 128
+        # wave_attn: plan + (window append + tcgen05 kernel | fused decode kernel);
+        # prelude / coda layers: append + plan + segment attention
+        self._launches = {"P": 3 * cfg.n_prelude, "R": (3 if tc else 2) * cfg.n_core, "C": 3 * cfg.n_coda}
+        self._layers = {"P": cfg.n_prelude, "R": cfg.n_core, "C": cfg.n_coda}
+        self.kv_read_bytes = 0
+        self.wfd_launches = 0
+        self.d2h_bytes = 0
 
     # ------------------------------------------------------------------
     def synchronize(self) -> None:
@@ -144,7 +155,15 @@ class WaveEngine:
         t.dev.copy_(t.host, non_blocking=True)
         t.uploaded.record()
         t.pending = True
+        keys = int(a[:n, 1].sum()) + n                      # k_len = position + 1 per live row
+        self.kv_read_bytes += keys * self._layers[kind] * 2 * self._row_bytes
+        self.wfd_launches += self._launches[kind]
         return t
+
+    def reset_counters(self) -> None:
+        self.kv_read_bytes = 0
+        self.wfd_launches = 0
+        self.d2h_bytes = 0
 
     def _padding_rows(self, t: _Tables) -> torch.Tensor:
         """A table of t's shape whose rows are all padding."""
@@ -157,11 +176,11 @@ class WaveEngine:
 
     # ------------------------------------------------------------------
     # device-side bodies (captured into graphs)
-    def _segment_block(self, blk, x, t: _Tables, j: int, slot: int, cos, sin):
+    def _segment_block(self, blk, x, t: _Tables, j: int, slot: int):
         """Prelude / coda layer: append every row, then attend with segments."""
         m = self.model
         tab = t.dev
-        q, k, v = m.qkv(blk, x, cos, sin)
+        q, k, v = m.qkv(blk, x, pos=tab[:, 1])
         self.cache.write_tokens(t.ones * slot, tab[:, 3], tab[:, 1], k, v)
         o = wa.attn_segments(q, self.Kflat, self.Vflat, t.row_ids, tab[:, 5], tab[:, 6 + j], tab[:, 1] + 1, 1,
                              causal=False)
@@ -171,12 +190,10 @@ class WaveEngine:
         m, cfg = self.model, self.cfg
         tab = t.dev
         rows = tab[:, 0].long()
-        pos = tab[:, 1].long()
-        cos, sin = self.cos.index_select(0, pos), self.sin.index_select(0, pos)
         if kind == "P":
             x = m.embed.index_select(0, tab[:, 2].long())
             for j, blk in enumerate(m.prelude):
-                x = self._segment_block(blk, x, t, j, cfg.slot_prelude(j), cos, sin)
+                x = self._segment_block(blk, x, t, j, cfg.slot_prelude(j))
             self.pool_e.index_copy_(0, rows, x)
             self.pool_h.index_copy_(0, rows, torch.zeros_like(x))
         elif kind == "R":
@@ -188,7 +205,7 @@ class WaveEngine:
             items[:, 3] = tab[:, 5]
             items[:, 4] = t.row_ids
             for l, blk in enumerate(m.core):
-                q, k, v = m.qkv(blk, x, cos, sin)
+                q, k, v = m.qkv(blk, x, pos=tab[:, 1])
                 o = wa.wave_attn(q, k, v, self.cache.K, self.cache.V, items, 1, lens=self.cache.lens,
                                  slot_offset=cfg.n_prelude + l)
                 x = m.finish_block(blk, x, o)
@@ -196,7 +213,7 @@ class WaveEngine:
         else:
             x = self.pool_h.index_select(0, rows)
             for j, blk in enumerate(m.coda):
-                x = self._segment_block(blk, x, t, j, cfg.slot_coda(j), cos, sin)
+                x = self._segment_block(blk, x, t, j, cfg.slot_coda(j))
             t.out.copy_(m.logits(x).argmax(dim=-1).to(torch.int32))
 
     def _run(self, kind: str, t: _Tables) -> None:
@@ -259,6 +276,7 @@ class WaveEngine:
     def coda_argmax_union(self, seq_ids, toks, cache) -> list[int]:
         t = self._fill("C", toks, seq_ids, [tk.hidden for tk in toks])
         self._run("C", t)
+        self.d2h_bytes += 4 * len(toks)
         return t.out[:len(toks)].tolist()
 
     # reporting

@@ -13,9 +13,11 @@ KV slots (kv_cache.py:12-15 of the reference): prelude layer i -> i; core
 (depth r, layer l) -> n_prelude + r * n_core + l; coda layer i ->
 n_prelude + T_total * n_core + i.
 
-Weights are plain tensors; GEMMs are cuBLAS (torch.matmul), attention is
-libwfd_b200.  Prefill attention (the one-shot prompt pass) uses torch's fused
-SDPA; every decode-time attention uses the wavefront kernels.
+Weights are plain tensors; GEMMs are cuBLAS (torch.matmul / addmm, residual adds
+in the GEMM epilogue), attention and the element-wise block work (RMSNorm, RoPE
++ QKV split, SwiGLU gate) are libwfd_b200 kernels.  Prefill attention (the
+one-shot prompt pass) uses torch's fused SDPA; every decode-time attention uses
+the wavefront kernels.
 """
 from __future__ import annotations
 
@@ -24,6 +26,8 @@ from dataclasses import dataclass
 
 import torch
 import torch.nn.functional as F
+
+from . import fused
 
 
 @dataclass
@@ -121,55 +125,43 @@ class LoopedLM:
 
     # ------------------------------------------------------------------
     def rope_tables(self, max_seq: int):
+        """(max_seq, Dh/2) fp32 cos / sin tables (grown on demand, kept on the device)."""
         if self._rope_cache is None or self._rope_cache[0].shape[0] < max_seq:
             Dh = self.cfg.head_dim
             inv = 1.0 / (self.cfg.rope_theta ** (torch.arange(0, Dh, 2, dtype=torch.float64) / Dh))
             t = torch.arange(max_seq, dtype=torch.float64)
             ang = torch.outer(t, inv)
-            self._rope_cache = (ang.cos().float().to(self.device), ang.sin().float().to(self.device))
+            self._rope_cache = (ang.cos().float().contiguous().to(self.device),
+                                ang.sin().float().contiguous().to(self.device))
         return self._rope_cache
 
     def rmsnorm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.norm_eps)
-        return (y * w.float()).to(x.dtype)
+        return fused.rmsnorm(x, w, self.cfg.norm_eps)
 
-    def apply_rope(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-        """RoPE on x (..., T, H, Dh) with cos / sin (T, Dh/2) fp32; the pair that
-        rotates by angle i is (i, i + Dh/2) ("half") or (2i, 2i + 1) ("interleaved")."""
-        xf = x.float()
-        c = cos.unsqueeze(-2)
-        s = sin.unsqueeze(-2)
-        if self.cfg.rope_style == "interleaved":
-            xp = xf.reshape(*xf.shape[:-1], xf.shape[-1] // 2, 2)
-            a, b = xp[..., 0], xp[..., 1]
-            return torch.stack((a * c - b * s, a * s + b * c), dim=-1).flatten(-2).to(x.dtype)
-        half = x.shape[-1] // 2
-        x1, x2 = xf[..., :half], xf[..., half:]
-        return torch.cat((x1 * c - x2 * s, x2 * c + x1 * s), dim=-1).to(x.dtype)
-
-    def qkv(self, blk: Block, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    def qkv(self, blk: Block, x: torch.Tensor, pos: torch.Tensor | None = None, pos_period: int = 0):
+        """Norm, fused QKV projection, RoPE.  x (n, d) with positions `pos` (int32,
+        one per row), or x (B, L, d) at positions 0..L-1 (pos_period = L).
+        Returns contiguous q (.., H, Dh), k / v (.., Hkv, Dh)."""
         cfg = self.cfg
-        H, Hkv, Dh = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
-        h = self.rmsnorm(x, blk.norm1)
+        lead = x.shape[:-1]
+        h = self.rmsnorm(x, blk.norm1).reshape(-1, cfg.d_model)
         qkv = h @ blk.wqkv
-        q, k, v = torch.split(qkv, [H * Dh, Hkv * Dh, Hkv * Dh], dim=-1)
-        shp = x.shape[:-1]
-        q = self.apply_rope(q.reshape(*shp, H, Dh), cos, sin)
-        k = self.apply_rope(k.reshape(*shp, Hkv, Dh), cos, sin)
-        v = v.reshape(*shp, Hkv, Dh)
-        return q, k, v
+        cos, sin = self._rope_cache
+        q, k, v = fused.rope_split(qkv, cos, sin, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, pos=pos,
+                                   pos_period=pos_period, interleaved=cfg.rope_style == "interleaved")
+        return (q.view(*lead, cfg.n_heads, cfg.head_dim), k.view(*lead, cfg.n_kv_heads, cfg.head_dim),
+                v.view(*lead, cfg.n_kv_heads, cfg.head_dim))
 
     def finish_block(self, blk: Block, x: torch.Tensor, attn: torch.Tensor) -> torch.Tensor:
+        """x + o_proj(attn), then x + SwiGLU(norm(x)); residual adds ride on the GEMMs."""
         cfg = self.cfg
-        x = x + attn.reshape(*x.shape[:-1], cfg.n_heads * cfg.head_dim) @ blk.wo
-        h = self.rmsnorm(x, blk.norm2)
-        gu = h @ blk.wgu
-        g, u = gu.split(cfg.d_ff, dim=-1)
-        return x + (F.silu(g.float()) * u.float()).to(x.dtype) @ blk.wd
+        shp = x.shape
+        x2 = torch.addmm(x.reshape(-1, cfg.d_model), attn.reshape(-1, cfg.n_heads * cfg.head_dim), blk.wo)
+        a = fused.silu_mul(self.rmsnorm(x2, blk.norm2) @ blk.wgu)
+        return torch.addmm(x2, a, blk.wd).view(shp)
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
-        return (self.rmsnorm(x, self.final_norm) @ self.lm_head).float()
+        return (self.rmsnorm(x.contiguous(), self.final_norm) @ self.lm_head).float()
 
     # ------------------------------------------------------------------
     @torch.no_grad()
@@ -178,11 +170,10 @@ class LoopedLM:
         slot and returns the full-depth logits at the last position (B, V)."""
         cfg = self.cfg
         B, L = ids.shape
-        cos, sin = self.rope_tables(max(L, cache.S))
-        cos, sin = cos[:L], sin[:L]
+        self.rope_tables(max(L, cache.S))
 
         def dense_block(blk, x, slot):
-            q, k, v = self.qkv(blk, x, cos, sin)                         # (B, L, H|Hkv, Dh)
+            q, k, v = self.qkv(blk, x, pos_period=L)                     # (B, L, H|Hkv, Dh)
             cache.write_prefill(slot, k, v)
             o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                                is_causal=True, enable_gqa=cfg.n_heads != cfg.n_kv_heads)
