@@ -81,6 +81,8 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=None, help="cfg4: generated tokens per sequence")
     ap.add_argument("--alpha", type=float, default=None,
                     help="cfg4: emulated draft acceptance rate (default: greedy gold == draft)")
+    ap.add_argument("--scheduler", choices=["device", "host"], default="device",
+                    help="cfg4: route / settle on the GPU (one graph per tick) or on the host")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", type=int, default=-1, choices=[-1, 0, 1],
@@ -492,6 +494,7 @@ def run_cfg4(args):
     __graft_entry__.load_package()
     from wavefront_decoding_b200 import runtime as rt
     from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import DeviceWave
     from wavefront_decoding_b200.engine import WaveEngine
     from wavefront_decoding_b200.looped_lm import CONFIG4, LoopedLM
 
@@ -506,6 +509,7 @@ def run_cfg4(args):
     model = LoopedLM(cfg, seed=CFG4["model_seed"], dtype=torch.bfloat16, device=dev)
     eng = WaveEngine(model, Bl, L + new + 2 * cfg.T_total + 8)
     policy = sch.SsdPolicy(cfg.T_total, args.t_draft)
+    dwave = DeviceWave(eng, new, policy) if args.scheduler == "device" else None
 
     ev_all0, ev_dec0, ev_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
 
@@ -524,7 +528,10 @@ def run_cfg4(args):
         eng.prefill = prefill
         try:
             ev_all0.record()
-            bt = sch.generate_wavefront_batch(eng, prompts, new, policy, emus)
+            if dwave is not None:
+                bt = dwave.generate(prompts, emus)
+            else:
+                bt = sch.generate_wavefront_batch(eng, prompts, new, policy, emus)
             ev_end.record()
             torch.cuda.synchronize()
         finally:
@@ -540,6 +547,9 @@ def run_cfg4(args):
     torch.cuda.synchronize()
     dec_ms = all_ms = 0.0
     tokens = proposed = accepted = ticks = 0
+    kv_dev = launches_dev = 0
+    # libwfd kernels of one device tick: 3 scheduling kernels + the P / R / C bodies
+    tick_launches = 3 + sum(eng._launches.values())
     with ClockSampler(local) as clk:
         for _ in range(args.steps):
             bt, d_ms, a_ms = generate()
@@ -549,9 +559,13 @@ def run_cfg4(args):
             proposed += sum(t.n_drafts_proposed for t in bt.per_seq)
             accepted += sum(t.n_drafts_accepted for t in bt.per_seq)
             ticks += bt.n_r_calls
+            if dwave is not None:
+                kv_dev += dwave.kv_read_bytes
+                launches_dev += tick_launches * dwave.ticks_replayed
     torch.cuda.synchronize()
     rt.read_device_error(dev)
-    kv_bytes = eng.kv_read_bytes
+    kv_bytes = eng.kv_read_bytes if dwave is None else kv_dev
+    launches = eng.wfd_launches if dwave is None else launches_dev
     if world > 1:
         dist.barrier(device_ids=[local])
         t = torch.tensor([dec_ms, all_ms], dtype=torch.float64, device=dev)
@@ -581,7 +595,7 @@ def run_cfg4(args):
                             f"{cfg.n_heads}x{cfg.head_dim} heads (kv {cfg.n_kv_heads}), SwiGLU {cfg.d_ff}, "
                             f"prelude {cfg.n_prelude} / core {cfg.n_core} x R={cfg.T_total} / coda {cfg.n_coda}",
                    "global_batch": Bg, "batch_per_gpu": Bl, "prompt_len": L, "new_tokens": new,
-                   "T_draft": args.t_draft,
+                   "T_draft": args.t_draft, "scheduler": args.scheduler,
                    "acceptance": "greedy gold == draft" if args.alpha is None else f"emulated Bernoulli({args.alpha})",
                    "parallelism": f"sequences sharded, {world} rank(s), no collective on the hot path",
                    "timing": "decode region per generation, CUDA events, max over ranks; "
@@ -594,9 +608,10 @@ def run_cfg4(args):
                      "note": "attention K/V bytes read by live rows over the whole decode wall time "
                              "(GEMMs, host scheduling and launches included in the time)"},
         "e2e": {"value": tot_tokens / (all_max * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": eng.d2h_bytes // args.steps, "ms_per_step": all_max / args.steps,
+                "d2h_bytes_per_step": eng.d2h_bytes // args.steps if dwave is None else dwave.d2h_bytes,
+                "ms_per_step": all_max / args.steps,
                 "includes": "prefill, prompt upload from pinned host memory, per-tick greedy-id read-back"},
-        "gpu_launches": eng.wfd_launches,
+        "gpu_launches": launches,
         "clocks": clk.summary(),
         "cpu_baseline": None,
     }

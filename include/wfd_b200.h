@@ -241,6 +241,42 @@ int wfd_rope_split(const void* qkv, const float* cos_tab, const float* sin_tab, 
  * (dff % 8 == 0). */
 int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, int32_t dtype, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Device-side wavefront scheduling (route / settle of scheduler_batch.py:268-360
+ * as kernels, so one CUDA graph runs a whole tick; no counterpart in the
+ * reference, whose scheduler runs on the host with one read-back per tick).
+ * Token slot j of sequence b is entry b * W + j of the slot arrays and pool row
+ * b * W + j of the engine.  State: 0 free, 1 queued for the prelude, 2 in the
+ * wave.  Tables use the engine's int32 union-row layout (pool row, position,
+ * token, cache sequence, slot base, live, per-layer first cache rows).
+ * ------------------------------------------------------------------------- */
+typedef struct {
+  int32_t *alive, *state, *tok, *pos, *step;     /* token slots (B * W) */
+  int32_t *n_commit, *done, *committed, *seq_ct; /* (B), (B), (B, max_new), (B, 8) */
+  const uint8_t* emu;                            /* (B, emu_len) accept draws, NULL = greedy */
+  int32_t *emu_ctr, *batch_ct;                   /* (B), (8) */
+  unsigned long long* keys;                      /* (3) sum of k_len over P / R / C rows */
+  int32_t *c_slot, *lens, *err;                  /* (2B), KV lengths (n_kv_slots, lens_stride), error word */
+  int32_t *p_tab, *r_tab, *c_tab;                /* (B, p_cols), (r_cap, 6), (2B, c_cols) */
+  const int32_t* c_out;                          /* (2B) greedy ids of the C union */
+  int32_t B, W, T_total, T_draft, max_new, emu_len;
+  int32_t n_core, n_kv_slots, lens_stride, max_seq;
+  int32_t p_cols, c_cols, r_cap;
+  int32_t scratch_row, scratch_seq;
+  int32_t p_slot0, n_prelude, c_slot0, n_coda;
+} wfd_sched_params;
+
+/* Before the P union: queue -> wave for each sequence's queued token (P table
+ * row b), compacted R table of every live token.  B <= 1024, W <= 32. */
+int wfd_sched_pre_tick(const wfd_sched_params* p, void* stream);
+/* After the R union: advance steps, route commit points (C row 2b) and draft
+ * points (C row 2b + 1). */
+int wfd_sched_route(const wfd_sched_params* p, void* stream);
+/* After the C union: accept / reject the successor of each commit point,
+ * cascade rollback (KV lengths truncated), queue the next token and the new
+ * leading-edge draft, commit tokens and per-sequence counters. */
+int wfd_sched_settle(const wfd_sched_params* p, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

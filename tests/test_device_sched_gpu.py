@@ -1,0 +1,103 @@
+"""Device-side wavefront scheduling (route / settle kernels, one CUDA graph per
+tick) against the host scheduler that mirrors the reference
+(scheduler.generate_wavefront_batch): same tokens, every per-sequence and batch
+counter, and the same final KV slot lengths; plus config 1 against the
+reference's own ParcaeBlocks golden and the cached K/V against the oracle."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from test_engine_gpu import _check_cache_vs_oracle, _config1_engine, _engine, _prompts, _small_cfg
+
+pytestmark = pytest.mark.gpu
+
+_CT = ("n_p_calls", "n_r_calls", "n_c_calls", "n_drafts_proposed", "n_drafts_accepted", "n_drafts_rejected",
+       "n_rollback_events")
+
+
+def _summary(bt, eng, B):
+    lens = eng.cache.lens[:, :B].cpu().tolist()
+    return ([t.tokens for t in bt.per_seq], [[getattr(t, k) for k in _CT] for t in bt.per_seq],
+            [bt.n_r_calls, bt.n_p_calls, bt.n_c_calls, bt.r_union_total, bt.r_union_max], lens)
+
+
+def _both(cfg, B, L, N, T_draft, alpha=None, seed=0, pseed=21, dtype=torch.float32):
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import generate_wavefront_device
+    prompts = _prompts(B, L, cfg.vocab, seed=pseed)
+    pol = sch.SsdPolicy(cfg.T_total, T_draft)
+
+    def emus():
+        return None if alpha is None else [sch.EmulatedAcceptance(alpha, seed=50 + b) for b in range(B)]
+
+    _, eh = _engine(cfg, B, L + N + 2 * cfg.T_total + 8, dtype=dtype, seed=seed)
+    host = sch.generate_wavefront_batch(eh, prompts, N, pol, emus())
+    model, ed = _engine(cfg, B, L + N + 2 * cfg.T_total + 8, dtype=dtype, seed=seed)
+    dev = generate_wavefront_device(ed, prompts, N, pol, emus())
+    return _summary(host, eh, B), _summary(dev, ed, B), (model, ed, prompts, dev)
+
+
+@pytest.mark.parametrize("T_draft", [1, 2, 4])
+def test_device_matches_host_greedy(cuda_dev, T_draft):
+    cfg = _small_cfg()
+    h, d, _ = _both(cfg, 3, 10, 24, T_draft)
+    assert d == h
+
+
+@pytest.mark.parametrize("alpha,T_draft", [(0.5, 1), (0.8, 2), (0.3, 2)])
+def test_device_matches_host_emulated(cuda_dev, alpha, T_draft):
+    cfg = _small_cfg(n_kv_heads=4)
+    h, d, _ = _both(cfg, 5, 9, 30, T_draft, alpha=alpha)
+    assert d == h
+    assert sum(x[6] for x in d[1]) > 0          # rollbacks exercised
+
+
+def test_device_cache_matches_oracle(cuda_dev):
+    cfg = _small_cfg()
+    _, _, (model, eng, prompts, bt) = _both(cfg, 2, 10, 14, 2)
+    _check_cache_vs_oracle(eng, model, prompts, bt.per_seq, 2e-4)
+
+
+def test_device_graph_equals_eager(cuda_dev):
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import generate_wavefront_device
+    cfg = _small_cfg()
+    B, L, N = 4, 8, 20
+    prompts = _prompts(B, L, cfg.vocab, seed=23)
+    outs = []
+    for graph in (True, False):
+        _, eng = _engine(cfg, B, L + N + 16)
+        emus = [sch.EmulatedAcceptance(0.6, seed=3 + b) for b in range(B)]
+        bt = generate_wavefront_device(eng, prompts, N, sch.SsdPolicy(4, 1), emus, use_graph=graph)
+        outs.append(_summary(bt, eng, B))
+    assert outs[0] == outs[1]
+
+
+@pytest.mark.parametrize("T_draft", [1, 2, 4])
+def test_device_config1_matches_reference(cuda_dev, T_draft):
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import generate_wavefront_device
+    eng, prompt, gold = _config1_engine()
+    g = gold[f"wfd_d{T_draft}"]
+    bt = generate_wavefront_device(eng, prompt, gold["n_new"], sch.SsdPolicy(gold["T_total"], T_draft))
+    t = bt.per_seq[0]
+    assert t.tokens == g["tokens"] == gold["ar"]["tokens"]
+    for k in ("n_drafts_proposed", "n_drafts_accepted", "n_drafts_rejected", "n_rollback_events"):
+        assert getattr(t, k) == g[k], k
+    lens = eng.cache.seqlen
+    assert {str(s): lens[s][0] for s in range(len(lens))} == g["seqlen"]
+
+
+def test_device_repeat_generation_reuses_graph(cuda_dev):
+    """A DeviceWave generates twice with one captured graph; same result."""
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import DeviceWave
+    cfg = _small_cfg()
+    B, L, N = 3, 7, 12
+    prompts = _prompts(B, L, cfg.vocab, seed=24)
+    _, eng = _engine(cfg, B, L + N + 16)
+    dw = DeviceWave(eng, N, sch.SsdPolicy(4, 2))
+    a = _summary(dw.generate(prompts), eng, B)
+    b = _summary(dw.generate(prompts), eng, B)
+    assert a == b and len(dw._graphs) == 1

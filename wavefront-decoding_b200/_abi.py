@@ -24,6 +24,7 @@ EXPORTED = (
     "wfd_append",
     "wfd_write_prefill", "wfd_commit_drop", "wfd_commit_window", "wfd_gather_pack",
     "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul",
+    "wfd_sched_pre_tick", "wfd_sched_route", "wfd_sched_settle",
 )
 
 
@@ -38,6 +39,17 @@ class WfdError(RuntimeError):
 class wfd_item(ctypes.Structure):
     _fields_ = [("slot", ctypes.c_int32), ("seq", ctypes.c_int32), ("pos0", ctypes.c_int32),
                 ("q_len", ctypes.c_int32), ("q_row0", ctypes.c_int32)]
+
+
+class wfd_sched_params(ctypes.Structure):
+    """include/wfd_b200.h: wfd_sched_params (field order and types must match)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "alive", "state", "tok", "pos", "step", "n_commit", "done", "committed", "seq_ct", "emu", "emu_ctr",
+        "batch_ct", "keys", "c_slot", "lens", "err", "p_tab", "r_tab", "c_tab", "c_out")] + \
+        [(n, ctypes.c_int32) for n in (
+            "B", "W", "T_total", "T_draft", "max_new", "emu_len", "n_core", "n_kv_slots", "lens_stride",
+            "max_seq", "p_cols", "c_cols", "r_cap", "scratch_row", "scratch_seq", "p_slot0", "n_prelude",
+            "c_slot0", "n_coda")]
 
 
 _P = ctypes.c_void_p
@@ -76,6 +88,10 @@ _SIGS = {
     "wfd_rope_split": ([_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     # gu out n dff dtype stream
     "wfd_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
+    # const wfd_sched_params*, stream
+    "wfd_sched_pre_tick": ([_P, _P], _I),
+    "wfd_sched_route": ([_P, _P], _I),
+    "wfd_sched_settle": ([_P, _P], _I),
 }
 
 _lock = threading.Lock()

@@ -5,6 +5,7 @@
 // allocates device memory or synchronises (except wfd_read_error, whose job is
 // to read the device error word).
 #include <cmath>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <utility>
@@ -14,6 +15,7 @@
 #include "wfd_common.cuh"
 #include "wfd_decode.cuh"
 #include "wfd_model.cuh"
+#include "wfd_sched.cuh"
 #include "wfd_plan.cuh"
 #include "wfd_verify.cuh"
 
@@ -769,6 +771,51 @@ extern "C" int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, i
                                                           n, dff);
   else
     return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// device-side wavefront scheduling
+// ---------------------------------------------------------------------------
+static_assert(sizeof(wfd_sched_params) == sizeof(wfd::SchedParams), "wfd_sched_params layout");
+static_assert(offsetof(wfd_sched_params, c_out) == offsetof(wfd::SchedParams, c_out), "wfd_sched_params layout");
+static_assert(offsetof(wfd_sched_params, n_coda) == offsetof(wfd::SchedParams, n_coda), "wfd_sched_params layout");
+
+namespace {
+int sched_check(const wfd_sched_params* p) {
+  if (!p) return WFD_ERR_INVALID_ARG;
+  if (p->B <= 0 || p->B > kSchedThreads || p->W <= 0 || p->W > kSchedMaxW) return WFD_ERR_UNSUPPORTED;
+  if (p->T_draft < 1 || p->T_total < p->T_draft || p->max_new < 1 || p->r_cap < 1) return WFD_ERR_INVALID_ARG;
+  if (p->p_cols < 6 || p->c_cols < 6 || p->emu_len < 0) return WFD_ERR_INVALID_ARG;
+  if (!p->alive || !p->state || !p->tok || !p->pos || !p->step || !p->n_commit || !p->done || !p->committed ||
+      !p->seq_ct || !p->emu_ctr || !p->batch_ct || !p->keys || !p->c_slot || !p->lens || !p->err || !p->p_tab ||
+      !p->r_tab || !p->c_tab || !p->c_out)
+    return WFD_ERR_INVALID_ARG;
+  return WFD_OK;
+}
+}  // namespace
+
+extern "C" int wfd_sched_pre_tick(const wfd_sched_params* p, void* stream) {
+  const int rc = sched_check(p);
+  if (rc != WFD_OK) return rc;
+  sched_pre_tick_kernel<<<1, kSchedThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      *reinterpret_cast<const SchedParams*>(p));
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+extern "C" int wfd_sched_route(const wfd_sched_params* p, void* stream) {
+  const int rc = sched_check(p);
+  if (rc != WFD_OK) return rc;
+  sched_route_kernel<<<1, kSchedThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      *reinterpret_cast<const SchedParams*>(p));
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+extern "C" int wfd_sched_settle(const wfd_sched_params* p, void* stream) {
+  const int rc = sched_check(p);
+  if (rc != WFD_OK) return rc;
+  sched_settle_kernel<<<(p->B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      *reinterpret_cast<const SchedParams*>(p));
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
