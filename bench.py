@@ -2,7 +2,8 @@
 """Benchmark: wavefront decode / verify attention on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wfd|reference]
-                    [--workload cfg2|cfg3] [--kernel -1|0|1]
+                    [--workload cfg2|cfg3|cfg4] [--kernel -1|0|1] [--batch B]
+                    [--t-draft D] [--scheduler device|host] [--alpha A] [--new-tokens T]
 
 Default workload: one step = one wavefront decode tick of
 the isolated attention op: B=8 sequences x R=8 loop-depth slots, Hq=16 / Hkv=4
@@ -16,6 +17,14 @@ R=8, Hq=32 / Hkv=8, Dh=128, bf16; slot r holds 8192 - r positions and gets an
 8-row causal draft window; a step is the fused append + verify attention and
 the accept commit (per-sequence accepted lengths U{0..8}, seed 3).  Q, K, V
 ~ N(0,1) drawn on the device from seed 2 (8.6 GB of KV does not fit a CPU draw).
+
+--workload cfg4: end-to-end greedy wavefront decoding of
+the random-init looped LM (vocab 50304, d 1536, 24 x 64 heads, SwiGLU 4096,
+prelude 2 / core 4 x R=8 / coda 2, bf16) through the engine and the device
+scheduler; 64 prompts of 1024 uniform token ids (seed 4) split over the ranks
+(strong scaling; --batch sets the total), 256 new tokens, T_draft 2 (--t-draft).
+One step = one generation; value = committed tokens / decode time (CUDA events,
+max over ranks), e2e includes the prefill and the host copies.
 
 value : algorithmic KV-read GB/s with every input resident in HBM (one CUDA
         graph per step), max time over ranks.
@@ -68,10 +77,27 @@ def ncu_traffic(workload: str, tc: bool, c: dict):
     return int(t * c["B"] / (CFG2 if workload == "cfg2" else CFG3)["B"])
 
 
+def init_dist(dev, timeout_s: int):
+    """NCCL process group for this rank; NCCL's start-up banner (printed on fd 1
+    when the environment enables it) goes to stderr so rank 0's stdout stays
+    the one JSON line."""
+    import torch.distributed as dist
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=dev)
+        dist.barrier(device_ids=[dev.index])
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
     ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2")
@@ -161,12 +187,20 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        self.first = []
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return self
+        # the timed region starts once sampling is live (nvidia-smi takes a
+        # moment to print its first line)
+        import select
+        r, _, _ = select.select([self.proc.stdout], [], [], 10.0)
+        if r:
+            self.first = [self.proc.stdout.readline()]
         return self
 
     def __exit__(self, *exc):
@@ -178,7 +212,7 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
                 out = ""
-            self.lines = [ln for ln in (out or "").splitlines() if ln.strip()]
+            self.lines = [ln for ln in self.first + (out or "").splitlines() if ln.strip()]
 
     def summary(self):
         rows = []
@@ -319,7 +353,7 @@ def run_wfd(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        init_dist(dev, 300)
 
     import __graft_entry__
     __graft_entry__.load_package()
@@ -413,17 +447,8 @@ def run_wfd(args):
     ms_e2e = ev0.elapsed_time(ev1) / e2e_steps
     rt.read_device_error(dev)
 
-    if world > 1:
-        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_e2e = t.tolist()
-        counters = torch.tensor([nbytes, rows], dtype=torch.float64, device=dev)
-        gathered = [torch.zeros_like(counters) for _ in range(world)]
-        dist.all_gather(gathered, counters)
-        total_bytes = sum(float(x[0]) for x in gathered)
-        total_rows = sum(float(x[1]) for x in gathered)
-    else:
-        total_bytes, total_rows = float(nbytes), float(rows)
+    from wavefront_decoding_b200.parallel import reduce_over_ranks
+    (ms, ms_e2e), (total_bytes, total_rows) = reduce_over_ranks([ms, ms_e2e], [nbytes, rows], dev)
 
     value = total_bytes / (ms * 1e-3) / 1e9
     value_e2e = total_bytes / (ms_e2e * 1e-3) / 1e9
@@ -488,7 +513,7 @@ def run_cfg4(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+        init_dist(dev, 600)
 
     import __graft_entry__
     __graft_entry__.load_package()
@@ -498,14 +523,16 @@ def run_cfg4(args):
     from wavefront_decoding_b200.engine import WaveEngine
     from wavefront_decoding_b200.looped_lm import CONFIG4, LoopedLM
 
+    from wavefront_decoding_b200.parallel import reduce_over_ranks, shard_range
     cfg = CONFIG4
     Bg = args.batch or CFG4["B"]
-    if Bg % world:
-        raise SystemExit(f"global batch {Bg} is not divisible by {world} ranks")
-    Bl = Bg // world
+    s0, s1 = shard_range(Bg, world, rank)
+    Bl = s1 - s0
+    if Bl < 1:
+        raise SystemExit(f"global batch {Bg} leaves rank {rank} of {world} without sequences")
     L, new = CFG4["L"], args.new_tokens or CFG4["new"]
     prompts_all = torch.randint(0, cfg.vocab, (Bg, L), generator=torch.Generator().manual_seed(CFG4["seed"]))
-    prompts = prompts_all[rank * Bl:(rank + 1) * Bl].contiguous().pin_memory()
+    prompts = prompts_all[s0:s1].contiguous().pin_memory()
     model = LoopedLM(cfg, seed=CFG4["model_seed"], dtype=torch.bfloat16, device=dev)
     eng = WaveEngine(model, Bl, L + new + 2 * cfg.T_total + 8)
     policy = sch.SsdPolicy(cfg.T_total, args.t_draft)
@@ -568,17 +595,11 @@ def run_cfg4(args):
     launches = eng.wfd_launches if dwave is None else launches_dev
     if world > 1:
         dist.barrier(device_ids=[local])
-        t = torch.tensor([dec_ms, all_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dec_max, all_max = t.tolist()
-        c = torch.tensor([tokens, proposed, accepted, kv_bytes], dtype=torch.float64, device=dev)
-        dist.all_reduce(c, op=dist.ReduceOp.SUM)
-        tot_tokens, tot_prop, tot_acc, tot_kv = c.tolist()
+    (dec_max, all_max), (tot_tokens, tot_prop, tot_acc, tot_kv) = reduce_over_ranks(
+        [dec_ms, all_ms], [tokens, proposed, accepted, kv_bytes], dev)
+    if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
-    else:
-        dec_max, all_max = dec_ms, all_ms
-        tot_tokens, tot_prop, tot_acc, tot_kv = tokens, proposed, accepted, kv_bytes
     if rank != 0:
         return
     peak, peak_kind = measured_peak()
@@ -594,7 +615,8 @@ def run_cfg4(args):
                    "model": f"looped LM {cfg.n_params() / 1e6:.0f}M params: vocab {cfg.vocab}, d {cfg.d_model}, "
                             f"{cfg.n_heads}x{cfg.head_dim} heads (kv {cfg.n_kv_heads}), SwiGLU {cfg.d_ff}, "
                             f"prelude {cfg.n_prelude} / core {cfg.n_core} x R={cfg.T_total} / coda {cfg.n_coda}",
-                   "global_batch": Bg, "batch_per_gpu": Bl, "prompt_len": L, "new_tokens": new,
+                   "global_batch": Bg, "batch_per_gpu": Bl if Bg % world == 0 else f"{Bg // world}-{-(-Bg // world)}",
+                   "prompt_len": L, "new_tokens": new,
                    "T_draft": args.t_draft, "scheduler": args.scheduler,
                    "acceptance": "greedy gold == draft" if args.alpha is None else f"emulated Bernoulli({args.alpha})",
                    "parallelism": f"sequences sharded, {world} rank(s), no collective on the hot path",
