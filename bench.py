@@ -58,6 +58,9 @@ FALLBACK_HBM_GBS = 6650.0
 CFG2 = dict(B=8, R=8, H=16, Hkv=4, Dh=128, S=4096, seed=1)
 CFG3 = dict(B=32, R=8, H=32, Hkv=8, Dh=128, L0=8192, W=8, seed=2, accept_seed=3)
 CFG4 = dict(B=64, L=1024, new=256, seed=4, model_seed=0, emu_seed=5)
+# config 5 as stated needs 9.1 GB of KV per sequence (128 / GPU: 1.17 TB); the stated
+# reduction measured here: one layer's 16 loop-depth slots, 64 sequences per GPU (137 GB)
+CFG5 = dict(B=64, R=16, H=32, Hkv=8, Dh=128, L0=32768, W=8, seed=5, alpha=0.8)
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # timed attention kernel, from the ncu captures summarised under profiles/
@@ -100,13 +103,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (cfg2 / cfg3) or in total over all GPUs (cfg4); default: the config's")
     ap.add_argument("--t-draft", type=int, default=2, help="cfg4: draft depth T_draft")
     ap.add_argument("--new-tokens", type=int, default=None, help="cfg4: generated tokens per sequence")
     ap.add_argument("--alpha", type=float, default=None,
-                    help="cfg4: emulated draft acceptance rate (default: greedy gold == draft)")
+                    help="cfg4: emulated draft acceptance rate (default: greedy gold == draft); "
+                         "cfg5: Bernoulli draft acceptance (default 0.8)")
     ap.add_argument("--scheduler", choices=["device", "host"], default="device",
                     help="cfg4: route / settle on the GPU (one graph per tick) or on the host")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
@@ -152,11 +156,16 @@ def cfg2_cpu_inputs(seed: int, batch: int | None = None):
     return c, q, K, V, kn, vn, items
 
 
-def cfg3_device_inputs(dev, seed: int, batch: int | None = None):
+def cfg3_device_inputs(dev, seed: int, batch: int | None = None, base: dict | None = None,
+                       alpha: float | None = None):
+    """Verify-window workload (config 3; config 5 with base=CFG5): q, K, V ~ N(0,1)
+    drawn on the device, per-sequence accepted lengths for the commit."""
     import torch
-    c = dict(CFG3)
+    c = dict(base or CFG3)
     if batch:
         c["B"] = batch
+    if alpha is not None:
+        c["alpha"] = alpha
     B, R, H, Hkv, Dh, L0, W = c["B"], c["R"], c["H"], c["Hkv"], c["Dh"], c["L0"], c["W"]
     g = torch.Generator(device=dev).manual_seed(seed)
     q = torch.randn((B, R, W, H, Dh), generator=g, device=dev, dtype=torch.bfloat16)
@@ -171,8 +180,17 @@ def cfg3_device_inputs(dev, seed: int, batch: int | None = None):
     idx_p = torch.tensor([p + j for r, b, p, w, _ in items for j in range(w)], device=dev)
     kn = K[idx_r, idx_b, idx_p].contiguous()
     vn = V[idx_r, idx_b, idx_p].contiguous()
-    accept = torch.randint(0, 9, (32,), generator=torch.Generator().manual_seed(c["accept_seed"]))
-    acc_items = torch.tensor([int(accept[b % 32]) for r, b, p, w, _ in items], dtype=torch.int32, device=dev)
+    if "alpha" in c:
+        # config 5: Bernoulli(alpha) draft outcomes, seed 5; a sequence keeps the
+        # drafts before its first rejection, in every depth slot
+        ok = torch.rand((B, W), generator=torch.Generator().manual_seed(c["seed"])) < c["alpha"]
+        lead = torch.cumprod(ok.int(), dim=1).sum(dim=1)
+        acc_seq = [int(x) for x in lead]
+    else:
+        accept = torch.randint(0, 9, (32,), generator=torch.Generator().manual_seed(c["accept_seed"]))
+        acc_seq = [int(accept[b % 32]) for b in range(B)]
+    c["accepted"] = acc_seq
+    acc_items = torch.tensor([acc_seq[b] for r, b, p, w, _ in items], dtype=torch.int32, device=dev)
     return c, q, K, V, kn, vn, items, acc_items
 
 
@@ -313,9 +331,11 @@ def run_reference(args):
         if dev is None:
             print(json.dumps({"impl": "reference", "unavailable": "cfg3 inputs are drawn on the GPU"}))
             return
-        c, q, K, V, kn, vn, items, _ = cfg3_device_inputs(dev, CFG3["seed"], args.batch)
+        base = CFG3 if args.workload == "cfg3" else CFG5
+        c, q, K, V, kn, vn, items, _ = cfg3_device_inputs(dev, base["seed"], args.batch, base,
+                                                          args.alpha if args.workload == "cfg5" else None)
         K, V, q, kn, vn, items = cfg3_cpu_sample(K, V, q, kn, vn, items)
-        label = "cfg3 verify"
+        label = f"{args.workload} verify"
     base, n, dt = cpu_baseline(q, K, V, kn, vn, items, 90.0, warmup=max(1, args.warmup), steps=max(1, args.steps),
                                label=label)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
@@ -332,10 +352,17 @@ def workload_config(name, c, world, rows=None):
         d = {"workload": "cfg2_wavefront_decode_attention", "batch_per_gpu": c["B"], "slots": c["R"],
              "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "4096-r",
              "l2": "KV working set 537 MB > 126 MB L2, no flush"}
-    else:
+    elif name == "cfg3":
         d = {"workload": "cfg3_wavefront_verify_attention_plus_commit", "batch_per_gpu": c["B"], "slots": c["R"],
              "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "8192-r + 8-row window",
              "window": c["W"], "l2": "KV working set > 126 MB L2, no flush"}
+    else:
+        d = {"workload": "cfg5_long_context_verify_plus_commit (stated reduction: one layer's 16 loop-depth "
+                         "slots, 64 sequences per GPU; the full model needs 1.17 TB of KV per GPU)",
+             "batch_per_gpu": c["B"], "slots": c["R"], "n_heads": c["H"], "n_kv_heads": c["Hkv"],
+             "head_dim": c["Dh"], "slot_len": "32768-r + 8-row window", "window": c["W"],
+             "acceptance": f"Bernoulli({c['alpha']}) seed {c['seed']}, accepted prefix per sequence",
+             "l2": "KV working set 137 GB > L2, no flush"}
     d["parallelism"] = f"sequences sharded, {world} rank(s)"
     d["timing"] = "CUDA graph replay"
     if rows is not None:
@@ -367,7 +394,9 @@ def run_wfd(args):
         acc = None
         max_q = 1
     else:
-        c, qd, Kd, Vd, knd, vnd, items, acc = cfg3_device_inputs(dev, CFG3["seed"] + rank, args.batch)
+        base = CFG3 if args.workload == "cfg3" else CFG5
+        c, qd, Kd, Vd, knd, vnd, items, acc = cfg3_device_inputs(dev, base["seed"] + rank, args.batch, base,
+                                                                 args.alpha if args.workload == "cfg5" else None)
         max_q = c["W"]
         q = kn = vn = K = V = None
     H, Hkv, Dh = c["H"], c["Hkv"], c["Dh"]
@@ -480,9 +509,13 @@ def run_wfd(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
-        if args.workload == "cfg3":
+        if args.workload in ("cfg3", "cfg5"):
             flops = sum((p0 + ql) for _, _, p0, ql, _ in items) * Hkv * (H // Hkv) * max_q * Dh * 4
             line["tensor_tflops"] = flops / (ms * 1e-3) / 1e12
+        if args.workload == "cfg5":
+            # tokens one verify step commits per sequence: accepted drafts + the corrected / bonus token
+            line["tokens_per_s"] = world * sum(a + 1 for a in c["accepted"]) / (ms * 1e-3)
+            line["accepted_mean"] = sum(c["accepted"]) / len(c["accepted"])
     if world > 1:
         dist.barrier(device_ids=[local])
         del g
@@ -493,7 +526,8 @@ def run_wfd(args):
                 base, _, _ = cpu_baseline(q, K, V, kn, vn, items, args.cpu_seconds)
             else:
                 Kc, Vc, qc, knc, vnc, itc = cfg3_cpu_sample(Kd, Vd, qd, knd, vnd, items)
-                base, _, _ = cpu_baseline(qc, Kc, Vc, knc, vnc, itc, args.cpu_seconds, label="cfg3 verify")
+                base, _, _ = cpu_baseline(qc, Kc, Vc, knc, vnc, itc, args.cpu_seconds,
+                                          label=f"{args.workload} verify")
             line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
         else:
             line["cpu_baseline"] = None
