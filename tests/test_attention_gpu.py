@@ -285,7 +285,7 @@ def test_cfg2_full_size_vs_oracle(cuda_dev):
 # tcgen05 tensor-core kernel (kernel=1): decode rows and verify windows
 # ---------------------------------------------------------------------------
 TC_CASES = [
-    # (name, n_slots, B, S, H, Hkv, items)      Dh = 128, bf16
+    # (name, n_slots, B, S, H, Hkv, items)      Dh = 128 (Dh = 64 where the name ends in _d64), bf16
     ("tc_decode_gqa4", 4, 3, 300, 16, 4, [[r, b, 250 - 7 * r + b, 1, r * 3 + b] for r in range(4) for b in range(3)]),
     ("tc_first_and_full", 2, 2, 200, 8, 2, [[0, 0, 0, 1, 0], [1, 1, 199, 1, 1], [0, 1, 127, 1, 2], [1, 0, 128, 1, 3]]),
     ("tc_window8_gqa4", 3, 2, 400, 16, 4, [[r, b, 300 - 50 * r + 3 * b, 8, (r * 2 + b) * 8]
@@ -293,13 +293,22 @@ TC_CASES = [
     ("tc_window_ragged", 2, 3, 300, 8, 2, [[0, 0, 5, 3, 0], [1, 2, 250, 8, 3], [0, 1, 130, 6, 11], [1, 0, 0, 2, 17]]),
     ("tc_window16_qgroups", 2, 2, 500, 16, 4, [[0, 0, 400, 16, 0], [1, 1, 37, 12, 16]]),
     ("tc_mha", 2, 2, 300, 4, 4, [[0, 0, 150, 1, 0], [1, 1, 260, 8, 1]]),
+    ("tc_decode_mha_d64", 4, 3, 400, 6, 6, [[r, b, 390 - 9 * r - b, 1, r * 3 + b] for r in range(4) for b in range(3)]),
+    ("tc_first_and_full_d64", 2, 2, 200, 4, 4, [[0, 0, 0, 1, 0], [1, 1, 199, 1, 1], [0, 1, 127, 1, 2],
+                                                 [1, 0, 128, 1, 3]]),
+    ("tc_window8_gqa4_d64", 3, 2, 400, 16, 4, [[r, b, 300 - 50 * r + 3 * b, 8, (r * 2 + b) * 8]
+                                               for r in range(3) for b in range(2)]),
+    ("tc_window_ragged_d64", 2, 3, 300, 8, 2, [[0, 0, 5, 3, 0], [1, 2, 250, 8, 3], [0, 1, 130, 6, 11],
+                                                [1, 0, 0, 2, 17]]),
+    ("tc_window16_qgroups_d64", 2, 2, 500, 16, 4, [[0, 0, 400, 16, 0], [1, 1, 37, 12, 16]]),
 ]
 
 
 @pytest.mark.parametrize("case", TC_CASES, ids=[c[0] for c in TC_CASES])
 def test_tc_kernel_vs_oracle(cuda_dev, case):
     name, n_slots, B, S, H, Hkv, items = case
-    K, V, q, kn, vn = _wave_case(sum(map(ord, name)), n_slots, B, S, H, Hkv, 128, items, torch.bfloat16)
+    Dh = 64 if name.endswith("_d64") else 128
+    K, V, q, kn, vn = _wave_case(sum(map(ord, name)), n_slots, B, S, H, Hkv, Dh, items, torch.bfloat16)
     max_q = max(it[3] for it in items)
     out, Kd, Vd, lens = _run_wave(cuda_dev, K, V, q, kn, vn, items, max_q, kernel=1)
     no_device_error(cuda_dev)
@@ -310,7 +319,8 @@ def test_tc_kernel_vs_oracle(cuda_dev, case):
         assert int(lens[slot, seq]) == p0 + ql
 
 
-def test_tc_kernel_balanced_split(cuda_dev):
+@pytest.mark.parametrize("Dh,H,Hkv,max_ql", [(128, 16, 4, 8), (64, 12, 12, 8), (64, 12, 12, 1), (128, 16, 4, 1)])
+def test_tc_kernel_balanced_split(cuda_dev, Dh, H, Hkv, max_ql):
     """Many units of very different lengths over the persistent grid; the
     second and third launches check the arrival counters were left zeroed."""
     rng = np.random.default_rng(3)
@@ -318,16 +328,16 @@ def test_tc_kernel_balanced_split(cuda_dev):
     items = []
     for r in range(n_slots):
         for b in range(B):
-            ql = int(rng.integers(1, 9))
+            ql = int(rng.integers(1, max_ql + 1))
             items.append([r, b, int(rng.integers(0, S - ql)), ql, 0])
     row = 0
     for it in items:
         it[4] = row
         row += it[3]
-    K, V, q, kn, vn = _wave_case(31, n_slots, B, S, 16, 4, 128, items, torch.bfloat16)
+    K, V, q, kn, vn = _wave_case(31, n_slots, B, S, H, Hkv, Dh, items, torch.bfloat16)
     ref, _ = _oracle_wave(K, V, q, kn, vn, items)
     for _ in range(3):
-        out, _, _, _ = _run_wave(cuda_dev, K, V, q, kn, vn, items, 8, kernel=1)
+        out, _, _, _ = _run_wave(cuda_dev, K, V, q, kn, vn, items, max_ql, kernel=1)
         assert maxdiff(out, ref) < TOL_BF16
     no_device_error(cuda_dev)
 

@@ -175,13 +175,13 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// (Dh=128, Hkv, rows) bf16 key / value buffer; box = 64 dims x 1 head x 128 rows,
-// 128-byte swizzle (the UMMA SWIZZLE_128B layout); rows past the end read as 0.
-bool make_kv_map(CUtensorMap* m, const void* base, long long rows, int Hkv) {
+// (Dh, Hkv, rows) bf16 key / value buffer (Dh 64 or 128); box = 64 dims x 1 head x
+// 128 rows, 128-byte swizzle (the UMMA SWIZZLE_128B layout); rows past the end read as 0.
+bool make_kv_map(CUtensorMap* m, const void* base, long long rows, int Hkv, int Dh) {
   EncodeTiledFn fn = encode_tiled();
   if (!fn) return false;
-  cuuint64_t dims[3] = {128, (cuuint64_t)Hkv, (cuuint64_t)rows};
-  cuuint64_t strides[2] = {128 * 2, (cuuint64_t)Hkv * 128 * 2};
+  cuuint64_t dims[3] = {(cuuint64_t)Dh, (cuuint64_t)Hkv, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)Dh * 2, (cuuint64_t)Hkv * Dh * 2};
   cuuint32_t box[3] = {64, 1, (cuuint32_t)kTcTile};
   cuuint32_t es[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
@@ -189,29 +189,46 @@ bool make_kv_map(CUtensorMap* m, const void* base, long long rows, int Hkv) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NQP>
+template <int NQP, int DH, int NA>
 int launch_tc(const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& tv, int sms, cudaStream_t st) {
-  using C = TcCfg<NQP>;
+  using C = TcCfg<NQP, DH>;
   static bool attr_set[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(wave_tc_kernel<NQP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+    if (cudaFuncSetAttribute(wave_tc_kernel<NQP, DH, NA>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
         cudaSuccess)
       return WFD_ERR_CUDA;
     attr_set[dev] = true;
   }
-  if (launch_pdl(wave_tc_kernel<NQP>, dim3(sms), dim3(kTcThreads), C::SMEM, st, tk, tv, vp) != cudaSuccess)
+  if (launch_pdl(wave_tc_kernel<NQP, DH, NA>, dim3(sms), dim3(kTcThreads), C::SMEM, st, tk, tv, vp) != cudaSuccess)
     return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
-int launch_verify(int nqp, const VerifyParams& vp, const void* k, const void* v, long long rows, int Hkv, int sms,
-                  cudaStream_t st) {
+// active query columns of the softmax: every unit has at most G * max_q vectors
+int verify_active(int nqp, int G, int max_q) {
+  if (nqp == 32) return 32;
+  const long long nv = (long long)G * max_q;
+  return nv <= 1 ? 1 : nv <= 4 ? 4 : 16;
+}
+
+template <int DH>
+int launch_tc_dh(int nqp, int na, const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& tv, int sms,
+                 cudaStream_t st) {
+  if (nqp == 32) return launch_tc<32, DH, 32>(vp, tk, tv, sms, st);
+  if (na == 1) return launch_tc<16, DH, 1>(vp, tk, tv, sms, st);
+  if (na == 4) return launch_tc<16, DH, 4>(vp, tk, tv, sms, st);
+  return launch_tc<16, DH, 16>(vp, tk, tv, sms, st);
+}
+
+int launch_verify(int nqp, int na, const VerifyParams& vp, const void* k, const void* v, long long rows, int Hkv,
+                  int Dh, int sms, cudaStream_t st) {
   if (rows <= 0 || rows >= (1ll << 31)) return WFD_ERR_UNSUPPORTED;  // TMA row coordinates are int32
+  if (Dh != 64 && Dh != 128) return WFD_ERR_UNSUPPORTED;
   CUtensorMap tk, tv;
-  if (!make_kv_map(&tk, k, rows, Hkv) || !make_kv_map(&tv, v, rows, Hkv)) return WFD_ERR_CUDA;
-  return nqp == 16 ? launch_tc<16>(vp, tk, tv, sms, st) : launch_tc<32>(vp, tk, tv, sms, st);
+  if (!make_kv_map(&tk, k, rows, Hkv, Dh) || !make_kv_map(&tv, v, rows, Hkv, Dh)) return WFD_ERR_CUDA;
+  return Dh == 128 ? launch_tc_dh<128>(nqp, na, vp, tk, tv, sms, st) : launch_tc_dh<64>(nqp, na, vp, tk, tv, sms, st);
 }
 
 // Common core of every attention entry point: plan, then attend.
@@ -253,10 +270,13 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   const int max_q = A.max_q < 1 ? 1 : A.max_q;
   int which = A.which;
   const bool tc_ok = verify_supported(A.dtype, A.Dh, G, max_q) && A.key_rows > 0 && A.key_rows < (1ll << 31);
-  // bf16 / Dh=128 runs on the tensor cores for decode rows too: measured on
-  // B200 (config 2) the CUDA-core kernel is issue-bound at 54 % of HBM peak,
-  // the tcgen05 kernel reaches 71 %.  fp32 and Dh=64 stay on the CUDA cores.
-  if (which < 0) which = tc_ok ? 1 : 0;
+  // bf16 runs on the tensor cores, decode rows included: measured on B200, config
+  // 2 (GQA 4, Dh 128): CUDA-core kernel 54 % of HBM peak (issue-bound), tcgen05
+  // kernel 81 %; GQA 4 at Dh 64: 41 % vs 60 %.  Single-row MHA at Dh 64 (one
+  // query column per kv head) is the exception: 54 % vs 52 %, so it stays on the
+  // CUDA cores, as does fp32 (tcgen05 would take it as tf32).
+  const bool mha_d64_decode = A.Dh == 64 && (long long)G * max_q == 1;
+  if (which < 0) which = (tc_ok && !mha_d64_decode) ? 1 : 0;
   if (which == 1 && !tc_ok) return WFD_ERR_UNSUPPORTED;
 
   const WsLayout L = ws_layout(A.n, A.Dh, sms, which == 1);
@@ -332,7 +352,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     vp.ws_part = reinterpret_cast<float*>(ws + L.part);
     vp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
     vp.err = A.err;
-    return launch_verify(NQ, vp, A.k, A.v, A.key_rows, A.Hkv, sms, st);
+    return launch_verify(NQ, verify_active(NQ, G, max_q), vp, A.k, A.v, A.key_rows, A.Hkv, A.Dh, sms, st);
   }
 
   DecodeParams dp;

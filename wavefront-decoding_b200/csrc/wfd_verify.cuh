@@ -1,10 +1,14 @@
 // K2 — wavefront verify / decode attention on the 5th-generation tensor cores
-// (tcgen05 + TMEM + TMA, sm_100a), bf16 inputs, Dh = 128.
+// (tcgen05 + TMEM + TMA, sm_100a), bf16 inputs, Dh = 128 or 64.
 //
 // Swap-AB formulation: per 128-key tile of one (segment, query group, kv head)
 // unit
-//     S^T[128 keys x N]  = K_tile[128 x 128] . Q^T           (A = K, K-major)
+//     S^T[128 keys x N]  = K_tile[128 x Dh] . Q^T            (A = K, K-major)
 //     O^T[128 dims x N] += V_tile^T[128 x 128 keys] . P^T     (A = V, MN-major)
+// For Dh = 64 the P.V MMA keeps M = 128: its upper 64 rows read the shared memory
+// after the tile (the next stage, or a guard region after the last one) and land
+// in TMEM lanes that are never read back; a stage is then half as large, so the
+// ring holds twice as many.
 // where N = NQP (16 or 32) >= the unit's query vectors (window rows x GQA
 // group): the tensor core's M = 128 dimension runs over keys (then over head
 // dims), so a handful of query rows still fill the instruction.  Accumulators
@@ -54,22 +58,27 @@ struct VerifyParams {
   int* err;
 };
 
-template <int NQP>
+template <int NQP, int DH>
 struct TcCfg {
-  static constexpr int STAGES = 3;
+  static constexpr int KB = DH / 64;                       // 64-dim boxes per K (and per V) tile
+  static constexpr int STAGES = DH == 128 ? 3 : 6;
   static constexpr int BOX_BYTES = kTcTile * 128;          // 128 rows x 64 bf16
-  static constexpr int KV_STAGE = 4 * BOX_BYTES;           // K box0, K box1, V box0, V box1
-  static constexpr int Q_BYTES = NQP * 256;                // 2 boxes of NQP rows x 128 B
+  static constexpr int KV_STAGE = 2 * KB * BOX_BYTES;      // K boxes, then V boxes
+  static constexpr int GUARD = DH == 128 ? 0 : BOX_BYTES;  // read by the M = 128 P.V MMA of the last stage
+  static constexpr int Q_BYTES = NQP * DH * 2;             // KB boxes of NQP rows x 128 B
   static constexpr int P_ROWB = NQP * 2;                   // one key row of P^T
   static constexpr int P_BYTES = kTcTile * P_ROWB;
   static constexpr int P_SWZ_BITS = NQP == 16 ? 1 : 2;     // Swizzle<1,4,3> (32B) / <2,4,3> (64B)
   static constexpr uint64_t P_LAYOUT = NQP == 16 ? 6 : 4;  // UMMA layout SWIZZLE_32B / SWIZZLE_64B
   static constexpr int P_ATOM = 8 * P_ROWB;                // 8 key rows
   static constexpr int RED_FLOATS = 2 * 4 * NQP;           // double-buffered per-warp column values
-  static constexpr int SMEM = STAGES * KV_STAGE + Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + (2 * NQP + 4) * 4 + 1024;
+  static constexpr int SMEM =
+      STAGES * KV_STAGE + GUARD + Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + (2 * NQP + 4) * 4 + 1024;
   static constexpr int TMEM_COLS = NQP == 16 ? 64 : 128;   // S (x2) and O accumulators
-  static constexpr int PART_FLOATS = NQP * (128 + 2);
+  static constexpr int PART_FLOATS = NQP * (DH + 2);
   static_assert(NQP == 16 || NQP == 32, "N of the swap-AB MMA");
+  static_assert(DH == 64 || DH == 128, "head dim");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 // Any window size runs on the tensor cores: more than kVerifyMaxRows query
@@ -77,7 +86,7 @@ struct TcCfg {
 inline bool verify_supported(int dtype, int dh, int G, int max_q) {
   (void)G;
   (void)max_q;
-  return dtype == WFD_DTYPE_BF16 && dh == 128;
+  return dtype == WFD_DTYPE_BF16 && (dh == 128 || dh == 64);
 }
 inline int verify_rows(int G, int max_q) { return (long long)G * max_q <= 16 ? 16 : 32; }
 
@@ -204,7 +213,7 @@ __device__ __forceinline__ float warp_col_reduce(float (&w)[N], int lane) {
     }
   }
   float r = w[0];
-  constexpr int LOGN = N == 16 ? 4 : 5;
+  constexpr int LOGN = N == 1 ? 0 : N == 2 ? 1 : N == 4 ? 2 : N == 8 ? 3 : N == 16 ? 4 : 5;
 #pragma unroll
   for (int l = LOGN; l < 5; ++l) {
     const float got = __shfl_xor_sync(0xffffffffu, r, 1 << l);
@@ -215,7 +224,8 @@ __device__ __forceinline__ float warp_col_reduce(float (&w)[N], int lane) {
 
 template <int N>
 __device__ __forceinline__ int reduced_col(int lane) {
-  constexpr int LOGN = N == 16 ? 4 : 5;
+  constexpr int LOGN = N == 1 ? 0 : N == 2 ? 1 : N == 4 ? 2 : N == 8 ? 3 : N == 16 ? 4 : 5;
+  if (LOGN == 0) return 0;
   return (int)(__brev((unsigned)(lane & (N - 1))) >> (32 - LOGN));
 }
 
@@ -241,19 +251,25 @@ struct UnitIter {
   }
 };
 
-template <int NQP>
+// NA = query columns the softmax works on (the MMA always computes NQP): 1 for
+// MHA decode rows, 4 for GQA-4 decode rows, else NQP.  Every unit has at most NA
+// query vectors; P^T columns >= NA are zeroed once and never written again.
+template <int NQP, int DH, int NA>
 __global__ void __launch_bounds__(kTcThreads, 1)
     wave_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                    const VerifyParams p) {
-  using C = TcCfg<NQP>;
+  using C = TcCfg<NQP, DH>;
   constexpr int STAGES = C::STAGES;
+  constexpr int KB = C::KB;
+  static_assert(NA == 1 || NA == 4 || NA == 16 || NA == 32, "active query columns");
+  static_assert(NA <= NQP, "active query columns");
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* kvs = smem;                               // STAGES x (K0 K1 V0 V1)
-  unsigned char* qs = kvs + STAGES * C::KV_STAGE;          // Q^T operand (K-major, SW128)
+  unsigned char* qs = kvs + STAGES * C::KV_STAGE + C::GUARD;  // Q^T operand (K-major, SW128)
   unsigned char* ps = qs + C::Q_BYTES;                     // P^T operand (MN-major)
   float* red = reinterpret_cast<float*>(ps + C::P_BYTES);  // [2][4][NQP] column maxima
   float* lred = red + C::RED_FLOATS;                       // [2][4][NQP] column sums
@@ -357,10 +373,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           unsigned char* dst = kvs + stage * C::KV_STAGE;
           const int row = (int)(row0 + (long long)t * kTcTile);
           mbar_arrive_expect_tx(&bar_full[stage], (uint32_t)C::KV_STAGE);
-          tma_load_3d(dst, &tm_k, 0, h, row, &bar_full[stage]);
-          tma_load_3d(dst + C::BOX_BYTES, &tm_k, 64, h, row, &bar_full[stage]);
-          tma_load_3d(dst + 2 * C::BOX_BYTES, &tm_v, 0, h, row, &bar_full[stage]);
-          tma_load_3d(dst + 3 * C::BOX_BYTES, &tm_v, 64, h, row, &bar_full[stage]);
+#pragma unroll
+          for (int bx = 0; bx < KB; ++bx) {
+            tma_load_3d(dst + bx * C::BOX_BYTES, &tm_k, 64 * bx, h, row, &bar_full[stage]);
+            tma_load_3d(dst + (KB + bx) * C::BOX_BYTES, &tm_v, 64 * bx, h, row, &bar_full[stage]);
+          }
         }
         __syncwarp();
       }
@@ -396,7 +413,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (go && lane == 0) {
             const uint32_t k_addr = smem_u32(kvs + stage * C::KV_STAGE);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < DH / 16; ++j) {
               // K step j: dims 16j..16j+15 = box j/4, byte 32*(j%4) inside the 128B row
               const uint32_t koff = (uint32_t)((j >> 2) * C::BOX_BYTES + (j & 3) * 32);
               const uint32_t qoff = (uint32_t)((j >> 2) * (NQP * 128) + (j & 3) * 32);
@@ -414,7 +431,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t tp = it + t - 1;
           const int stage = (int)(tp % STAGES);
           if (go && lane == 0) {
-            const uint32_t v_addr = smem_u32(kvs + stage * C::KV_STAGE + 2 * C::BOX_BYTES);
+            const uint32_t v_addr = smem_u32(kvs + stage * C::KV_STAGE + KB * C::BOX_BYTES);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               // K step j: keys 16j..16j+15 = two 8-row groups of both V boxes / of P^T
@@ -444,20 +461,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int u, r_lo, r_hi;
     long long ustart;
     uint32_t it = 0, pv = 0, units = 0;
-    constexpr int PCH = NQP / 8;  // 16-byte chunks per P^T row
+    constexpr int PCHA = (NA + 7) / 8;  // 16-byte chunks of a P^T row holding active columns
+    for (int c = stid; c < C::P_BYTES / 16; c += 128) reinterpret_cast<uint4*>(ps)[c] = make_uint4(0, 0, 0, 0);
+    fence_async_smem();
     while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
       const int h = u % p.Hkv, qg = u / p.Hkv;
       const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
       const int nvec = S.q_len * p.G - qg * NQP;  // query vectors of this group (may exceed NQP)
       // ---- Q^T operand: row n = query vector qg*NQP + n
-      for (int c = stid; c < NQP * 16; c += 128) {
-        const int n = c >> 4, ch = c & 15;
+      for (int c = stid; c < NQP * (DH / 8); c += 128) {
+        const int n = c / (DH / 8), ch = c % (DH / 8);
         uint4 val = make_uint4(0, 0, 0, 0);
         if (n < nvec) {
           const int v = qg * NQP + n;
           const int row = v / p.G, g = v % p.G;
           val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
-                         ((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * 128 + ch * 8);
+                         ((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + ch * 8);
         }
         const int box = ch >> 3, cc = ch & 7;
         const uint32_t off = (uint32_t)(box * NQP * 128 + n * 128 + ((cc ^ (n & 7)) << 4));
@@ -470,9 +489,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // running column maxima live in shared memory (mst, log2-scaled), owned
       // by lanes 0..NQP-1 of the first softmax warp
       if (sw == 0 && lane < NQP) mst[lane] = NEG_INF;
-      float lp[NQP], oacc[NQP];
+      float lp[NA], oacc[NA];
 #pragma unroll
-      for (int n = 0; n < NQP; ++n) {
+      for (int n = 0; n < NA; ++n) {
         lp[n] = 0.f;
         oacc[n] = 0.f;
       }
@@ -496,15 +515,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int thr = p.causal ? (key - (S.k_len - S.q_len)) * p.G - qg * NQP : -(1 << 30);
         const int nlim = kvalid ? nvec : 0;
 #pragma unroll
-        for (int n = 0; n < NQP; ++n) s[n] = (n < nlim && n >= thr) ? s[n] : NEG_INF;  // raw (unscaled) scores
+        for (int n = 0; n < NA; ++n) s[n] = (n < nlim && n >= thr) ? s[n] : NEG_INF;  // raw (unscaled) scores
         // column maxima over the tile's 128 keys
         float* rb = red + (ti & 1u) * (4 * NQP);
         {
-          float w[NQP];
+          float w[NA];
 #pragma unroll
-          for (int n = 0; n < NQP; ++n) w[n] = s[n];
-          const float r = warp_col_reduce<NQP, true>(w, lane);
-          if (lane < NQP) rb[sw * NQP + reduced_col<NQP>(lane)] = r;
+          for (int n = 0; n < NA; ++n) w[n] = s[n];
+          const float r = warp_col_reduce<NA, true>(w, lane);
+          if (lane < NA) rb[sw * NA + reduced_col<NA>(lane)] = r;
         }
         softmax_bar();
         // column owner: new running max (moved only when the tile exceeds it by
@@ -512,8 +531,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // is exact) and the rescale factor alpha
         if (sw == 0) {
           float alpha = 1.f;
-          if (lane < NQP) {
-            const float tmax = fmaxf(fmaxf(rb[lane], rb[NQP + lane]), fmaxf(rb[2 * NQP + lane], rb[3 * NQP + lane]));
+          if (lane < NA) {
+            const float tmax = fmaxf(fmaxf(rb[lane], rb[NA + lane]), fmaxf(rb[2 * NA + lane], rb[3 * NA + lane]));
             const float mo = mst[lane];
             if (tmax != NEG_INF) {
               const float ts = tmax * c2;
@@ -533,12 +552,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int stage = (int)(ti % STAGES);
         if (!kvalid) {
           // rows past the unit may hold anything (even NaN): zero this key's V row
-          unsigned char* vrow = kvs + stage * C::KV_STAGE + 2 * C::BOX_BYTES + my_row * 128;
+          unsigned char* vrow = kvs + stage * C::KV_STAGE + KB * C::BOX_BYTES + my_row * 128;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(vrow + C::BOX_BYTES + c * 16) = make_uint4(0, 0, 0, 0);
-          }
+          for (int bx = 0; bx < KB; ++bx)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(vrow + bx * C::BOX_BYTES + c * 16) = make_uint4(0, 0, 0, 0);
         }
         // the previous tile's P.V: its MMA is done once o_full fires, which also
         // frees the P^T buffer.  oacc holds O_{t-2} already rescaled to m_{t-1}.
@@ -553,27 +572,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (lane == 0) mbar_arrive(&bar_ofree);
           ++pv;
 #pragma unroll
-          for (int n = 0; n < NQP; ++n) oacc[n] += o[n];
+          for (int n = 0; n < NA; ++n) oacc[n] += o[n];
         }
         // rescale the running sums when some column's max moved
         if (*rflag) {
+          if constexpr (NA >= 4) {
 #pragma unroll
-          for (int n4 = 0; n4 < NQP / 4; ++n4) {
-            const float4 a4 = reinterpret_cast<const float4*>(ast)[n4];
-            const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+            for (int n4 = 0; n4 < NA / 4; ++n4) {
+              const float4 a4 = reinterpret_cast<const float4*>(ast)[n4];
+              const float av[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              lp[n4 * 4 + e] *= av[e];
-              oacc[n4 * 4 + e] *= av[e];
+              for (int e = 0; e < 4; ++e) {
+                lp[n4 * 4 + e] *= av[e];
+                oacc[n4 * 4 + e] *= av[e];
+              }
+            }
+          } else {
+#pragma unroll
+            for (int n = 0; n < NA; ++n) {
+              lp[n] *= ast[n];
+              oacc[n] *= ast[n];
             }
           }
         }
-        // probabilities of this key; P^T row (bf16, swizzled MN-major)
+        // probabilities of this key; P^T row (bf16, swizzled MN-major), active chunks only
 #pragma unroll
-        for (int c = 0; c < PCH; ++c) {
-          const float4 m0 = reinterpret_cast<const float4*>(mst)[2 * c];
-          const float4 m1 = reinterpret_cast<const float4*>(mst)[2 * c + 1];
-          const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+        for (int c = 0; c < PCHA; ++c) {
+          float mv[8];
+          if constexpr (NA >= 8) {
+            const float4 m0 = reinterpret_cast<const float4*>(mst)[2 * c];
+            const float4 m1 = reinterpret_cast<const float4*>(mst)[2 * c + 1];
+            mv[0] = m0.x; mv[1] = m0.y; mv[2] = m0.z; mv[3] = m0.w;
+            mv[4] = m1.x; mv[5] = m1.y; mv[6] = m1.z; mv[7] = m1.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mv[e] = e < NA ? mst[e] : 0.f;
+          }
           uint32_t w4[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -581,8 +615,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int n = c * 8 + 2 * i + e;
-              pr2[e] = (s[n] == NEG_INF) ? 0.f : fast_exp2(fmaf(s[n], c2, -mv[2 * i + e]));
-              lp[n] += pr2[e];
+              if (n < NA) {
+                pr2[e] = (s[n] == NEG_INF) ? 0.f : fast_exp2(fmaf(s[n], c2, -mv[2 * i + e]));
+                lp[n] += pr2[e];
+              } else {
+                pr2[e] = 0.f;
+              }
             }
             __nv_bfloat162 h2 = __floats2bfloat162_rn(pr2[0], pr2[1]);
             w4[i] = *reinterpret_cast<uint32_t*>(&h2);
@@ -606,7 +644,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) mbar_arrive(&bar_ofree);
         ++pv;
 #pragma unroll
-        for (int n = 0; n < NQP; ++n) oacc[n] += o[n];
+        for (int n = 0; n < NA; ++n) oacc[n] += o[n];
       }
       it += n_t;
       ++units;
@@ -614,26 +652,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // ---- column sums of the unnormalised probabilities over the 128 threads
       float* lb = lred + (units & 1u) * (4 * NQP);
       {
-        float w[NQP];
+        float w[NA];
 #pragma unroll
-        for (int n = 0; n < NQP; ++n) w[n] = lp[n];
-        const float r = warp_col_reduce<NQP, false>(w, lane);
-        if (lane < NQP) lb[sw * NQP + reduced_col<NQP>(lane)] = r;
+        for (int n = 0; n < NA; ++n) w[n] = lp[n];
+        const float r = warp_col_reduce<NA, false>(w, lane);
+        if (lane < NA) lb[sw * NA + reduced_col<NA>(lane)] = r;
       }
       softmax_bar();
 
       const int c_first = (int)(ustart / share);
       const int c_last = (int)((ustart + S.k_len - 1) / share);
       const int n_contrib = c_last - c_first + 1;
-      const int dim = my_row;  // O^T TMEM lane == head dim
+      const int dim = my_row;  // O^T TMEM lane == head dim (lanes >= DH hold nothing)
+      const bool dim_ok = dim < DH;
       if (n_contrib == 1) {
 #pragma unroll
-        for (int n = 0; n < NQP; ++n) {
-          if (n < nvec) {
-            const float L = lb[n] + lb[NQP + n] + lb[2 * NQP + n] + lb[3 * NQP + n];
+        for (int n = 0; n < NA; ++n) {
+          if (n < nvec && dim_ok) {
+            const float L = lb[n] + lb[NA + n] + lb[2 * NA + n] + lb[3 * NA + n];
             const int v = qg * NQP + n;
             const int row = v / p.G, g = v % p.G;
-            static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * 128 + dim] =
+            static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + dim] =
                 __float2bfloat16_rn(L > 0.f ? oacc[n] / L : 0.f);
           }
         }
@@ -642,13 +681,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         float* pb = p.ws_part + (size_t)slot * C::PART_FLOATS;
         // every thread holds the same m[]; thread n publishes column n's (m, l);
         // O^T only for the unit's query columns (the merge reads no others)
-        if (stid < NQP) {
+        if (stid < NA) {
           pb[stid] = mst[stid];
-          pb[NQP + stid] = lb[stid] + lb[NQP + stid] + lb[2 * NQP + stid] + lb[3 * NQP + stid];
+          pb[NQP + stid] = lb[stid] + lb[NA + stid] + lb[2 * NA + stid] + lb[3 * NA + stid];
         }
 #pragma unroll
-        for (int n = 0; n < NQP; ++n)
-          if (n < nvec) pb[2 * NQP + n * 128 + dim] = oacc[n];
+        for (int n = 0; n < NA; ++n)
+          if (n < nvec && dim_ok) pb[2 * NQP + n * DH + dim] = oacc[n];
         __threadfence();
         softmax_bar();
         if (stid == 0) {
@@ -656,21 +695,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           s_flag = (prev == n_contrib - 1) ? 1 : 0;
         }
         softmax_bar();
-        if (s_flag) {
+        if (s_flag && dim_ok) {
           __threadfence();
           // Online merge, columns in chunks of MCH: this CTA's own (m, l, O) come
           // from shared memory and registers; for every other contributor all
           // loads of a chunk are independent (one round trip per contributor).
-          constexpr int MCH = NQP < 16 ? NQP : 16;
+          constexpr int MCH = NA < 16 ? NA : 16;
           const int k_own = (int)blockIdx.x - c_first;
 #pragma unroll
-          for (int c0 = 0; c0 < NQP; c0 += MCH) {
+          for (int c0 = 0; c0 < NA; c0 += MCH) {
             if (c0 < nvec) {
               float M[MCH], Ls[MCH], acc[MCH];
 #pragma unroll
               for (int j = 0; j < MCH; ++j) {
                 M[j] = mst[c0 + j];
-                Ls[j] = lb[c0 + j] + lb[NQP + c0 + j] + lb[2 * NQP + c0 + j] + lb[3 * NQP + c0 + j];
+                Ls[j] = lb[c0 + j] + lb[NA + c0 + j] + lb[2 * NA + c0 + j] + lb[3 * NA + c0 + j];
                 acc[j] = oacc[c0 + j];
               }
               for (int k = 0; k < n_contrib; ++k) {
@@ -683,7 +722,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int j = 0; j < MCH; ++j) {
                   mk[j] = ld_cg_f32(base + c0 + j);
                   lk[j] = ld_cg_f32(base + NQP + c0 + j);
-                  ok[j] = (c0 + j < nvec) ? ld_cg_f32(base + 2 * NQP + (c0 + j) * 128 + dim) : 0.f;
+                  ok[j] = (c0 + j < nvec) ? ld_cg_f32(base + 2 * NQP + (c0 + j) * DH + dim) : 0.f;
                 }
 #pragma unroll
                 for (int j = 0; j < MCH; ++j) {
@@ -703,14 +742,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (n < nvec) {
                   const int v = qg * NQP + n;
                   const int row = v / p.G, g = v % p.G;
-                  static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * 128 + dim] =
+                  static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + dim] =
                       __float2bfloat16_rn(Ls[j] > 0.f ? acc[j] / Ls[j] : 0.f);
                 }
               }
             }
           }
-          if (stid == 0) p.ws_cnt[c_first] = 0;
         }
+        if (s_flag && stid == 0) p.ws_cnt[c_first] = 0;
         softmax_bar();  // s_flag is re-written by the next unit
       }
     }
