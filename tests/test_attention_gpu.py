@@ -301,6 +301,13 @@ TC_CASES = [
     ("tc_window_ragged_d64", 2, 3, 300, 8, 2, [[0, 0, 5, 3, 0], [1, 2, 250, 8, 3], [0, 1, 130, 6, 11],
                                                 [1, 0, 0, 2, 17]]),
     ("tc_window16_qgroups_d64", 2, 2, 500, 16, 4, [[0, 0, 400, 16, 0], [1, 1, 37, 12, 16]]),
+    # head_dim 64 with an even kv-head count runs as head pairs on the 128-dim kernel
+    ("tc_window8_mha_pair_d64", 2, 3, 300, 6, 6, [[r, b, 200 - 30 * r + 7 * b, 8, (r * 3 + b) * 8]
+                                                   for r in range(2) for b in range(3)]),
+    ("tc_window4_gqa2_pair_d64", 3, 2, 300, 8, 4, [[0, 0, 10, 4, 0], [1, 1, 250, 3, 4], [2, 0, 0, 2, 7],
+                                                    [2, 1, 131, 4, 9]]),
+    ("tc_decode_mha_odd_d64", 2, 2, 300, 3, 3, [[r, b, 280 - 40 * r - b, 1, r * 2 + b] for r in range(2)
+                                                 for b in range(2)]),
 ]
 
 

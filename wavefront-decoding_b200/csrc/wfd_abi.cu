@@ -222,13 +222,14 @@ int launch_tc_dh(int nqp, int na, const VerifyParams& vp, const CUtensorMap& tk,
   return launch_tc<16, DH, 16>(vp, tk, tv, sms, st);
 }
 
+// Dh: the cache's head dim (tensor maps); kdh: the kernel's (128 for head pairs).
 int launch_verify(int nqp, int na, const VerifyParams& vp, const void* k, const void* v, long long rows, int Hkv,
-                  int Dh, int sms, cudaStream_t st) {
+                  int Dh, int kdh, int sms, cudaStream_t st) {
   if (rows <= 0 || rows >= (1ll << 31)) return WFD_ERR_UNSUPPORTED;  // TMA row coordinates are int32
-  if (Dh != 64 && Dh != 128) return WFD_ERR_UNSUPPORTED;
+  if ((Dh != 64 && Dh != 128) || (kdh != Dh && !(Dh == 64 && kdh == 128 && vp.pair))) return WFD_ERR_UNSUPPORTED;
   CUtensorMap tk, tv;
   if (!make_kv_map(&tk, k, rows, Hkv, Dh) || !make_kv_map(&tv, v, rows, Hkv, Dh)) return WFD_ERR_CUDA;
-  return Dh == 128 ? launch_tc_dh<128>(nqp, na, vp, tk, tv, sms, st) : launch_tc_dh<64>(nqp, na, vp, tk, tv, sms, st);
+  return kdh == 128 ? launch_tc_dh<128>(nqp, na, vp, tk, tv, sms, st) : launch_tc_dh<64>(nqp, na, vp, tk, tv, sms, st);
 }
 
 // Common core of every attention entry point: plan, then attend.
@@ -272,14 +273,18 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   const bool tc_ok = verify_supported(A.dtype, A.Dh, G, max_q) && A.key_rows > 0 && A.key_rows < (1ll << 31);
   // bf16 runs on the tensor cores, decode rows included: measured on B200, config
   // 2 (GQA 4, Dh 128): CUDA-core kernel 54 % of HBM peak (issue-bound), tcgen05
-  // kernel 81 %; GQA 4 at Dh 64: 41 % vs 60 %.  Single-row MHA at Dh 64 (one
-  // query column per kv head) is the exception: 54 % vs 52 %, so it stays on the
-  // CUDA cores, as does fp32 (tcgen05 would take it as tf32).
-  const bool mha_d64_decode = A.Dh == 64 && (long long)G * max_q == 1;
-  if (which < 0) which = (tc_ok && !mha_d64_decode) ? 1 : 0;
+  // kernel 81 %.  Head_dim 64 with an even kv-head count runs as pairs of heads
+  // on the 128-dim kernel (the 64-dim tile is bound by the tensor-core issue
+  // rate, not HBM); single-row MHA at head_dim 64 with an odd kv-head count stays
+  // on the CUDA cores (54 % vs 52 %), as does fp32 (tcgen05 would take it as tf32).
+  const bool pair_ok = A.Dh == 64 && A.Hkv % 2 == 0 && 2ll * G * max_q <= kVerifyMaxRows;
+  const bool odd_mha_d64_decode = A.Dh == 64 && !pair_ok && (long long)G * max_q == 1;
+  if (which < 0) which = (tc_ok && !odd_mha_d64_decode) ? 1 : 0;
   if (which == 1 && !tc_ok) return WFD_ERR_UNSUPPORTED;
+  const bool pair = which == 1 && pair_ok;
+  const int Gv = pair ? 2 * G : G;  // query vectors per unit and kv (pair) head
 
-  const WsLayout L = ws_layout(A.n, A.Dh, sms, which == 1);
+  const WsLayout L = ws_layout(A.n, pair ? 128 : A.Dh, sms, which == 1);
   if (A.ws_bytes < L.total || !aligned16(A.ws)) return WFD_ERR_WORKSPACE;
   char* ws = static_cast<char*>(A.ws);
 
@@ -289,7 +294,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     const int cap = nq_cap(A.dtype, A.Dh);
     if (NQ > cap) NQ = cap;
   } else {
-    NQ = verify_rows(G, max_q);
+    NQ = verify_rows(Gv, max_q);
   }
 
   PlanParams pp;
@@ -309,7 +314,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   pp.s_q_len = A.s_q_len;
   pp.s_k_row0 = A.s_k_row0;
   pp.s_k_len = A.s_k_len;
-  pp.G = G;
+  pp.G = which == 1 ? Gv : G;
   pp.NQ = NQ;
   pp.qg_split = 1;
   pp.segs = reinterpret_cast<Seg*>(ws + L.segs);
@@ -344,15 +349,17 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     vp.prefix = pp.prefix;
     vp.n_segs = A.n;
     vp.Hq = A.Hq;
-    vp.Hkv = A.Hkv;
+    vp.Hkv = pair ? A.Hkv / 2 : A.Hkv;
     vp.G = G;
+    vp.pair = pair ? 1 : 0;
     vp.scale_log2 = scale * log2e;
     vp.causal = A.causal;
     vp.k_row_offset = k_row_offset;
     vp.ws_part = reinterpret_cast<float*>(ws + L.part);
     vp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
     vp.err = A.err;
-    return launch_verify(NQ, verify_active(NQ, G, max_q), vp, A.k, A.v, A.key_rows, A.Hkv, A.Dh, sms, st);
+    return launch_verify(NQ, verify_active(NQ, Gv, max_q), vp, A.k, A.v, A.key_rows, A.Hkv, A.Dh, pair ? 128 : A.Dh,
+                         sms, st);
   }
 
   DecodeParams dp;

@@ -27,6 +27,14 @@
 // that straddle CTAs are merged by the last CTA to arrive.  Every wait is
 // bounded and reports through the error word; no multicast, no cluster launch.
 //
+// Head pairs (head_dim 64): with `pair` set, a unit is two consecutive kv heads
+// of a head_dim-64 cache read as one 128-dim head (the two 64-dim boxes are the
+// two heads).  Q^T is block-diagonal: query column n of head e (e = 0, 1) holds
+// its 64 dims in half e and zeros in the other, so S^T = K.Q^T gives each column
+// its own head's scores, and O^T rows [64e, 64e + 64) of column n are its output
+// (the other half is discarded).  The MMA count per byte is then that of
+// head_dim 128: the tensor-core issue rate, not the HBM, bounds a 64-dim tile.
+//
 // Window keys are read from the KV cache: the caller appends the window rows
 // (append_segs_kernel) in a launch before this one.  Launched with programmatic
 // stream serialization: barrier set-up and the TMEM allocation overlap the
@@ -53,6 +61,7 @@ struct VerifyParams {
   float scale_log2;
   int causal;
   long long k_row_offset;
+  int pair;  // 1: units are pairs of head_dim-64 kv heads (Hkv counts pairs, DH == 128)
   float* ws_part;
   int* ws_cnt;
   int* err;
@@ -375,8 +384,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           mbar_arrive_expect_tx(&bar_full[stage], (uint32_t)C::KV_STAGE);
 #pragma unroll
           for (int bx = 0; bx < KB; ++bx) {
-            tma_load_3d(dst + bx * C::BOX_BYTES, &tm_k, 64 * bx, h, row, &bar_full[stage]);
-            tma_load_3d(dst + (KB + bx) * C::BOX_BYTES, &tm_v, 64 * bx, h, row, &bar_full[stage]);
+            // box bx: dims 64bx.. of head h, or (pair) head 2h + bx
+            const int cx = p.pair ? 0 : 64 * bx, ch = p.pair ? 2 * h + bx : h;
+            tma_load_3d(dst + bx * C::BOX_BYTES, &tm_k, cx, ch, row, &bar_full[stage]);
+            tma_load_3d(dst + (KB + bx) * C::BOX_BYTES, &tm_v, cx, ch, row, &bar_full[stage]);
           }
         }
         __syncwarp();
@@ -467,16 +478,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
       const int h = u % p.Hkv, qg = u / p.Hkv;
       const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
-      const int nvec = S.q_len * p.G - qg * NQP;  // query vectors of this group (may exceed NQP)
-      // ---- Q^T operand: row n = query vector qg*NQP + n
+      const int nvh = S.q_len * p.G;                                   // query vectors per kv head
+      const int nvec = (p.pair ? 2 * nvh : nvh) - qg * NQP;  // of this unit / group (may exceed NQP)
+      // ---- Q^T operand: row n = query vector qg*NQP + n (pair: n < nvh head 2h, else 2h + 1)
       for (int c = stid; c < NQP * (DH / 8); c += 128) {
         const int n = c / (DH / 8), ch = c % (DH / 8);
         uint4 val = make_uint4(0, 0, 0, 0);
         if (n < nvec) {
-          const int v = qg * NQP + n;
-          const int row = v / p.G, g = v % p.G;
-          val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
-                         ((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + ch * 8);
+          if (p.pair) {
+            const int e = n >= nvh ? 1 : 0, v = n - e * nvh;
+            const int row = v / p.G, g = v % p.G;
+            if ((ch >> 3) == e)
+              val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
+                             ((long long)(S.q_row0 + row) * p.Hq + (2 * h + e) * p.G + g) * 64 + (ch & 7) * 8);
+          } else {
+            const int v = qg * NQP + n;
+            const int row = v / p.G, g = v % p.G;
+            val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
+                           ((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + ch * 8);
+          }
         }
         const int box = ch >> 3, cc = ch & 7;
         const uint32_t off = (uint32_t)(box * NQP * 128 + n * 128 + ((cc ^ (n & 7)) << 4));
@@ -515,7 +535,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int thr = p.causal ? (key - (S.k_len - S.q_len)) * p.G - qg * NQP : -(1 << 30);
         const int nlim = kvalid ? nvec : 0;
 #pragma unroll
-        for (int n = 0; n < NA; ++n) s[n] = (n < nlim && n >= thr) ? s[n] : NEG_INF;  // raw (unscaled) scores
+        for (int n = 0; n < NA; ++n) {
+          const int vn = (p.pair && n >= nvh) ? n - nvh : n;  // vector index within its head
+          s[n] = (n < nlim && vn >= thr) ? s[n] : NEG_INF;    // raw (unscaled) scores
+        }
         // column maxima over the tile's 128 keys
         float* rb = red + (ti & 1u) * (4 * NQP);
         {
@@ -665,15 +688,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int n_contrib = c_last - c_first + 1;
       const int dim = my_row;  // O^T TMEM lane == head dim (lanes >= DH hold nothing)
       const bool dim_ok = dim < DH;
+      // output element of query column n held by this thread's O^T row, or -1
+      auto out_at = [&](int n) -> long long {
+        if (p.pair) {
+          const int e = n >= nvh ? 1 : 0;
+          if ((dim >> 6) != e) return -1;
+          const int v = n - e * nvh;
+          const int row = v / p.G, g = v % p.G;
+          return ((long long)(S.q_row0 + row) * p.Hq + (2 * h + e) * p.G + g) * 64 + (dim & 63);
+        }
+        const int v = qg * NQP + n;
+        const int row = v / p.G, g = v % p.G;
+        return ((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + dim;
+      };
       if (n_contrib == 1) {
 #pragma unroll
         for (int n = 0; n < NA; ++n) {
           if (n < nvec && dim_ok) {
             const float L = lb[n] + lb[NA + n] + lb[2 * NA + n] + lb[3 * NA + n];
-            const int v = qg * NQP + n;
-            const int row = v / p.G, g = v % p.G;
-            static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + dim] =
-                __float2bfloat16_rn(L > 0.f ? oacc[n] / L : 0.f);
+            const long long oi = out_at(n);
+            if (oi >= 0) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(L > 0.f ? oacc[n] / L : 0.f);
           }
         }
       } else {
@@ -740,10 +774,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               for (int j = 0; j < MCH; ++j) {
                 const int n = c0 + j;
                 if (n < nvec) {
-                  const int v = qg * NQP + n;
-                  const int row = v / p.G, g = v % p.G;
-                  static_cast<__nv_bfloat16*>(p.out)[((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + dim] =
-                      __float2bfloat16_rn(Ls[j] > 0.f ? acc[j] / Ls[j] : 0.f);
+                  const long long oi = out_at(n);
+                  if (oi >= 0)
+                    static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(Ls[j] > 0.f ? acc[j] / Ls[j] : 0.f);
                 }
               }
             }

@@ -99,8 +99,10 @@ class WaveEngine:
         # accounting (host side, exact): K/V bytes the attention of live rows
         # reads, libwfd kernel launches, bytes read back per C union
         self._row_bytes = cfg.n_kv_heads * cfg.head_dim * torch.finfo(model.dtype).bits // 8
-        # the library's kernel choice for single-row waves: tcgen05 for bf16 except MHA at head_dim 64
-        tc = model.dtype == torch.bfloat16 and (cfg.head_dim == 128 or cfg.n_heads != cfg.n_kv_heads)
+        # the library's kernel choice for single-row waves: tcgen05 for bf16 except
+        # MHA at head_dim 64 with an odd kv-head count
+        tc = model.dtype == torch.bfloat16 and not (cfg.head_dim == 64 and cfg.n_heads == cfg.n_kv_heads
+                                                     and cfg.n_kv_heads % 2 == 1)
         # wave_attn: plan + (window append + tcgen05 kernel | fused decode kernel);
         # prelude / coda layers: append + plan + segment attention
         self._launches = {"P": 3 * cfg.n_prelude, "R": (3 if tc else 2) * cfg.n_core, "C": 3 * cfg.n_coda}
