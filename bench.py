@@ -58,17 +58,22 @@ FALLBACK_HBM_GBS = 6650.0
 CFG2 = dict(B=8, R=8, H=16, Hkv=4, Dh=128, S=4096, seed=1)
 CFG3 = dict(B=32, R=8, H=32, Hkv=8, Dh=128, L0=8192, W=8, seed=2, accept_seed=3)
 CFG4 = dict(B=64, L=1024, new=256, seed=4, model_seed=0, emu_seed=5)
+# the attention op of one config-4 R tick: 64 sequences x 8 loop depths, MHA 24 x 64,
+# slot r holding 1100 - r positions (1024-token prompts plus ~76 generated tokens)
+CFG4A = dict(B=64, R=8, H=24, Hkv=24, Dh=64, S=1100, seed=4)
 # config 5 as stated needs 9.1 GB of KV per sequence (128 / GPU: 1.17 TB); the stated
 # reduction measured here: one layer's 16 loop-depth slots, 64 sequences per GPU (137 GB)
 CFG5 = dict(B=64, R=16, H=32, Hkv=8, Dh=128, L0=32768, W=8, seed=5, alpha=0.8)
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # timed attention kernel, from the ncu captures summarised under profiles/
-# (wave_decode_cfg2.md for the CUDA-core kernel, wave_tc_cfg2.md / wave_tc_cfg3.md for tcgen05).
+# (wave_decode_cfg2.md for the CUDA-core kernel, wave_tc_cfg2.md / wave_tc_cfg3.md /
+# wave_tc_cfg4attn.md for tcgen05).
 # cfg3 was captured at batch 8 and scaled by the units processed (x4 at batch 32).
 NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
-                     ("cfg2", "tc"): 543_106_816 + 4_962_816,
-                     ("cfg3", "tc"): (2_189_256_960 + 9_662_464) * 4}
+                     ("cfg2", "tc"): 543_091_968 + 6_767_104,
+                     ("cfg3", "tc"): (2_189_533_696 + 10_547_456) * 4,
+                     ("cfg4attn", "tc"): 3_631_410_688 + 8_572_672}
 
 
 def ncu_traffic(workload: str, tc: bool, c: dict):
@@ -77,7 +82,8 @@ def ncu_traffic(workload: str, tc: bool, c: dict):
     t = NCU_TRAFFIC_BYTES.get((workload, "tc" if tc else "cuda_core"))
     if t is None:
         return None
-    return int(t * c["B"] / (CFG2 if workload == "cfg2" else CFG3)["B"])
+    base = {"cfg2": CFG2, "cfg3": CFG3, "cfg4attn": CFG4A, "cfg5": CFG5}[workload]
+    return int(t * c["B"] / base["B"])
 
 
 def init_dist(dev, timeout_s: int):
@@ -103,7 +109,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4attn", "cfg5"], default="cfg2")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (cfg2 / cfg3) or in total over all GPUs (cfg4); default: the config's")
     ap.add_argument("--t-draft", type=int, default=2, help="cfg4: draft depth T_draft")
@@ -192,6 +198,24 @@ def cfg3_device_inputs(dev, seed: int, batch: int | None = None, base: dict | No
     c["accepted"] = acc_seq
     acc_items = torch.tensor([acc_seq[b] for r, b, p, w, _ in items], dtype=torch.int32, device=dev)
     return c, q, K, V, kn, vn, items, acc_items
+
+
+def decode_device_inputs(dev, c: dict, seed: int):
+    """Single-row wavefront decode inputs drawn on the device: q (B*R, H, Dh), K / V
+    (R, B, S + 8, Hkv, Dh) ~ N(0,1); slot r of each sequence appends its row at
+    S - r - 1 (the row already drawn there, so repeated steps append identical
+    data) and attends S - r keys."""
+    import torch
+    B, R, H, Hkv, Dh, S = c["B"], c["R"], c["H"], c["Hkv"], c["Dh"], c["S"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn((B * R, H, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    K = torch.randn((R, B, S + 8, Hkv, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    V = torch.randn((R, B, S + 8, Hkv, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    items = [[r, b, S - r - 1, 1, b * R + r] for b in range(B) for r in range(R)]
+    ir = torch.tensor([it[0] for it in items], device=dev)
+    ib = torch.tensor([it[1] for it in items], device=dev)
+    ip = torch.tensor([it[2] for it in items], device=dev)
+    return c, q, K, V, K[ir, ib, ip].contiguous(), V[ir, ib, ip].contiguous(), items
 
 
 class ClockSampler:
@@ -331,9 +355,13 @@ def run_reference(args):
         if dev is None:
             print(json.dumps({"impl": "reference", "unavailable": "cfg3 inputs are drawn on the GPU"}))
             return
-        base = CFG3 if args.workload == "cfg3" else CFG5
-        c, q, K, V, kn, vn, items, _ = cfg3_device_inputs(dev, base["seed"], args.batch, base,
-                                                          args.alpha if args.workload == "cfg5" else None)
+        if args.workload == "cfg4attn":
+            c = dict(CFG4A, **({"B": args.batch} if args.batch else {}))
+            c, q, K, V, kn, vn, items = decode_device_inputs(dev, c, c["seed"])
+        else:
+            base = CFG3 if args.workload == "cfg3" else CFG5
+            c, q, K, V, kn, vn, items, _ = cfg3_device_inputs(dev, base["seed"], args.batch, base,
+                                                              args.alpha if args.workload == "cfg5" else None)
         K, V, q, kn, vn, items = cfg3_cpu_sample(K, V, q, kn, vn, items)
         label = f"{args.workload} verify"
     base, n, dt = cpu_baseline(q, K, V, kn, vn, items, 90.0, warmup=max(1, args.warmup), steps=max(1, args.steps),
@@ -352,6 +380,10 @@ def workload_config(name, c, world, rows=None):
         d = {"workload": "cfg2_wavefront_decode_attention", "batch_per_gpu": c["B"], "slots": c["R"],
              "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "4096-r",
              "l2": "KV working set 537 MB > 126 MB L2, no flush"}
+    elif name == "cfg4attn":
+        d = {"workload": "cfg4_tick_attention (the wavefront decode attention of one config-4 R tick)",
+             "batch_per_gpu": c["B"], "slots": c["R"], "n_heads": c["H"], "n_kv_heads": c["Hkv"],
+             "head_dim": c["Dh"], "slot_len": f"{c['S']}-r", "l2": "KV working set 3.5 GB > L2, no flush"}
     elif name == "cfg3":
         d = {"workload": "cfg3_wavefront_verify_attention_plus_commit", "batch_per_gpu": c["B"], "slots": c["R"],
              "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "8192-r + 8-row window",
@@ -393,6 +425,14 @@ def run_wfd(args):
         qd, Kd, Vd, knd, vnd = q.to(dev), K.to(dev), V.to(dev), kn.to(dev), vn.to(dev)
         acc = None
         max_q = 1
+    elif args.workload == "cfg4attn":
+        c = dict(CFG4A)
+        if args.batch:
+            c["B"] = args.batch
+        c, qd, Kd, Vd, knd, vnd, items = decode_device_inputs(dev, c, c["seed"] + rank)
+        acc = None
+        max_q = 1
+        q = kn = vn = K = V = None
     else:
         base = CFG3 if args.workload == "cfg3" else CFG5
         c, qd, Kd, Vd, knd, vnd, items, acc = cfg3_device_inputs(dev, base["seed"] + rank, args.batch, base,
