@@ -201,7 +201,8 @@ int launch_tc(const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& 
       return WFD_ERR_CUDA;
     attr_set[dev] = true;
   }
-  if (launch_pdl(wave_tc_kernel<NQP, DH, NA>, dim3(sms), dim3(kTcThreads), C::SMEM, st, tk, tv, vp) != cudaSuccess)
+  if (launch_pdl(wave_tc_kernel<NQP, DH, NA>, dim3(sms), dim3(tc_threads(NQP)), C::SMEM, st, tk, tv, vp) !=
+      cudaSuccess)
     return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }

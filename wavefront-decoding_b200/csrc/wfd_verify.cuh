@@ -15,13 +15,14 @@
 // live in TMEM; each of the four softmax warps owns one 32-lane TMEM quadrant
 // (= 32 keys of S^T, then 32 head dims of O^T).
 //
-// Warp roles (192 threads, one CTA per SM):
+// Warp roles (one CTA per SM; 192 threads, 320 for 32 query columns):
 //   warp 0      TMA producer: K and V tiles (2 boxes of 64 dims each, 128B
 //               swizzle) into a STAGES-deep ring, mbarrier complete_tx
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one lane issues)
-//   warps 2..5  softmax / correction: S^T from TMEM, column maxima across the
-//               128 keys, exp2, P^T (bf16) to shared memory, O^T accumulated
-//               in registers with the online-softmax rescale
+//   warps 2..   softmax / correction, 4 warps per slice of 16 query columns
+//               (warp w reads TMEM lane quadrant w % 4): S^T from TMEM, column
+//               maxima across the 128 keys, exp2, P^T (bf16) to shared memory,
+//               O^T accumulated in registers with the online-softmax rescale
 // The persistent grid splits the flattened (segment, query group, kv head,
 // key) space into equal key shares exactly like the CUDA-core kernel; units
 // that straddle CTAs are merged by the last CTA to arrive.  Every wait is
@@ -49,7 +50,8 @@ namespace wfd {
 
 constexpr int kVerifyMaxRows = 32;  // query vectors per unit (larger windows -> query groups)
 constexpr int kTcTile = 128;        // keys per tile == MMA M
-constexpr int kTcThreads = 192;
+// threads: TMA warp + MMA warp + 4 softmax warps per 16 query columns
+__host__ __device__ constexpr int tc_threads(int nqp) { return nqp == 32 ? 320 : 192; }
 
 struct VerifyParams {
   const void* q;
@@ -146,7 +148,8 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory"); }
 
 // 32 TMEM lanes x 32-bit, N consecutive columns -> N registers per thread
 template <int N>
@@ -264,7 +267,7 @@ struct UnitIter {
 // MHA decode rows, 4 for GQA-4 decode rows, else NQP.  Every unit has at most NA
 // query vectors; P^T columns >= NA are zeroed once and never written again.
 template <int NQP, int DH, int NA>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(tc_threads(NQP), 1)
     wave_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                    const VerifyParams p) {
   using C = TcCfg<NQP, DH>;
@@ -272,6 +275,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   constexpr int KB = C::KB;
   static_assert(NA == 1 || NA == 4 || NA == 16 || NA == 32, "active query columns");
   static_assert(NA <= NQP, "active query columns");
+  constexpr int THREADS = tc_threads(NQP);
+  constexpr int H2 = NQP == 32 ? 2 : 1;  // column slices of the softmax (4 warps each)
+  constexpr int NL = NA / H2;            // active query columns per softmax thread
+  constexpr int LW = NQP / H2;           // TMEM columns one tcgen05.ld reads per slice
+  constexpr int SMT = 128 * H2;          // softmax threads
+  static_assert(THREADS == 64 + SMT, "warp roles");
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   extern __shared__ unsigned char smem_raw[];
@@ -284,7 +293,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   float* lred = red + C::RED_FLOATS;                       // [2][4][NQP] column sums
   float* mst = lred + C::RED_FLOATS;                       // [NQP] running column max (log2-scaled)
   float* ast = mst + NQP;                                  // [NQP] this tile's rescale factors
-  int* rflag = reinterpret_cast<int*>(ast + NQP);          // any factor != 1 this tile
+  int* rflag = reinterpret_cast<int*>(ast + NQP);          // [H2] any factor != 1 this tile
 
   __shared__ __align__(8) uint64_t bar_full[STAGES];
   __shared__ __align__(8) uint64_t bar_empty[STAGES];
@@ -307,11 +316,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar_sfull[s], 1);
-      mbar_init(&bar_sfree[s], 4);
+      mbar_init(&bar_sfree[s], 4 * H2);
     }
     mbar_init(&bar_pfull, 1);
     mbar_init(&bar_ofull, 1);
-    mbar_init(&bar_ofree, 4);
+    mbar_init(&bar_ofree, 4 * H2);
     mbar_init(&bar_qready, 1);
     fence_mbar_init();
     s_abort = 0;
@@ -345,17 +354,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     while (lo < hi) {
       const int span = hi - lo;
       int piv = -1;
-      if (span <= kTcThreads) {
+      if (span <= THREADS) {
         if (tid < span) piv = lo + 1 + tid;
       } else {
-        piv = lo + (int)(((long long)(tid + 1) * span) / (kTcThreads + 1));
+        piv = lo + (int)(((long long)(tid + 1) * span) / (THREADS + 1));
       }
       const int c = __syncthreads_count(piv >= 0 && (long long)p.Hkv * p.prefix[piv] <= a);
-      if (span <= kTcThreads) {
+      if (span <= THREADS) {
         lo = hi = lo + c;
       } else {
-        const int nlo = c == 0 ? lo : lo + (int)(((long long)c * span) / (kTcThreads + 1));
-        const int nhi = c == kTcThreads ? hi : lo + (int)(((long long)(c + 1) * span) / (kTcThreads + 1)) - 1;
+        const int nlo = c == 0 ? lo : lo + (int)(((long long)c * span) / (THREADS + 1));
+        const int nhi = c == THREADS ? hi : lo + (int)(((long long)(c + 1) * span) / (THREADS + 1)) - 1;
         lo = nlo;
         hi = nhi;
       }
@@ -462,9 +471,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax warps
-    const int sw = warp - 2;            // 0..3
+    // 4 * H2 warps: warp w reads TMEM lane quadrant w % 4 (32 keys of S^T, then 32
+    // head dims of O^T) and query columns [col0, col0 + NL) of the tile.
+    const int sw = warp - 2;            // 0 .. 4 * H2 - 1
+    const int sq = sw & 3;              // quadrant warp within its column slice
+    const int col0 = (sw >> 2) * NL;    // first query column of this thread
     const int qd = warp & 3;            // TMEM lane quadrant this warp may access
-    const int stid = tid - 64;          // 0..127 within the softmax group
+    const int stid = tid - 64;          // 0 .. SMT - 1 within the softmax group
     const int my_row = qd * 32 + lane;  // key row of S^T, then head dim of O^T, this thread owns
     const uint32_t tq = tmem + ((uint32_t)(qd * 32) << 16);
     UnitIter itr{a, b, seg0};
@@ -472,8 +485,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int u, r_lo, r_hi;
     long long ustart;
     uint32_t it = 0, pv = 0, units = 0;
-    constexpr int PCHA = (NA + 7) / 8;  // 16-byte chunks of a P^T row holding active columns
-    for (int c = stid; c < C::P_BYTES / 16; c += 128) reinterpret_cast<uint4*>(ps)[c] = make_uint4(0, 0, 0, 0);
+    constexpr int PCHL = (NL + 7) / 8;  // 16-byte chunks of a P^T row this thread writes
+    for (int c = stid; c < C::P_BYTES / 16; c += SMT) reinterpret_cast<uint4*>(ps)[c] = make_uint4(0, 0, 0, 0);
     fence_async_smem();
     while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
       const int h = u % p.Hkv, qg = u / p.Hkv;
@@ -481,7 +494,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int nvh = S.q_len * p.G;                                   // query vectors per kv head
       const int nvec = (p.pair ? 2 * nvh : nvh) - qg * NQP;  // of this unit / group (may exceed NQP)
       // ---- Q^T operand: row n = query vector qg*NQP + n (pair: n < nvh head 2h, else 2h + 1)
-      for (int c = stid; c < NQP * (DH / 8); c += 128) {
+      for (int c = stid; c < NQP * (DH / 8); c += SMT) {
         const int n = c / (DH / 8), ch = c % (DH / 8);
         uint4 val = make_uint4(0, 0, 0, 0);
         if (n < nvec) {
@@ -503,17 +516,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         *reinterpret_cast<uint4*>(qs + off) = val;
       }
       fence_async_smem();
-      softmax_bar();
+      softmax_bar<SMT>();
       if (stid == 0) mbar_arrive(&bar_qready);
 
       // running column maxima live in shared memory (mst, log2-scaled), owned
-      // by lanes 0..NQP-1 of the first softmax warp
-      if (sw == 0 && lane < NQP) mst[lane] = NEG_INF;
-      float lp[NA], oacc[NA];
+      // by lanes 0..NL-1 of the first warp of each column slice
+      if (sq == 0 && lane < NL) mst[col0 + lane] = NEG_INF;
+      float lp[NL], oacc[NL];
 #pragma unroll
-      for (int n = 0; n < NA; ++n) {
-        lp[n] = 0.f;
-        oacc[n] = 0.f;
+      for (int j = 0; j < NL; ++j) {
+        lp[j] = 0.f;
+        oacc[j] = 0.f;
       }
       const float c2 = p.scale_log2;
       for (int t = 0; t < n_t; ++t) {
@@ -521,8 +534,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int sb = (int)(ti & 1u);
         tc_wait(&bar_sfull[sb], (ti >> 1) & 1u, &s_abort, p.err);
         tc_fence_after();
-        float s[NQP];
-        tmem_ld<NQP>(tq + (uint32_t)(sb * NQP), s);
+        float s[LW];
+        tmem_ld<LW>(tq + (uint32_t)(sb * NQP + col0), s);
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -535,45 +548,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int thr = p.causal ? (key - (S.k_len - S.q_len)) * p.G - qg * NQP : -(1 << 30);
         const int nlim = kvalid ? nvec : 0;
 #pragma unroll
-        for (int n = 0; n < NA; ++n) {
+        for (int j = 0; j < NL; ++j) {
+          const int n = col0 + j;
           const int vn = (p.pair && n >= nvh) ? n - nvh : n;  // vector index within its head
-          s[n] = (n < nlim && vn >= thr) ? s[n] : NEG_INF;    // raw (unscaled) scores
+          s[j] = (n < nlim && vn >= thr) ? s[j] : NEG_INF;    // raw (unscaled) scores
         }
         // column maxima over the tile's 128 keys
         float* rb = red + (ti & 1u) * (4 * NQP);
         {
-          float w[NA];
+          float w[NL];
 #pragma unroll
-          for (int n = 0; n < NA; ++n) w[n] = s[n];
-          const float r = warp_col_reduce<NA, true>(w, lane);
-          if (lane < NA) rb[sw * NA + reduced_col<NA>(lane)] = r;
+          for (int j = 0; j < NL; ++j) w[j] = s[j];
+          const float r = warp_col_reduce<NL, true>(w, lane);
+          if (lane < NL) rb[sq * NQP + col0 + reduced_col<NL>(lane)] = r;
         }
-        softmax_bar();
+        softmax_bar<SMT>();
         // column owner: new running max (moved only when the tile exceeds it by
         // more than 8 in log2 units; O and l share the stale max, so the result
         // is exact) and the rescale factor alpha
-        if (sw == 0) {
+        if (sq == 0) {
           float alpha = 1.f;
-          if (lane < NA) {
-            const float tmax = fmaxf(fmaxf(rb[lane], rb[NA + lane]), fmaxf(rb[2 * NA + lane], rb[3 * NA + lane]));
-            const float mo = mst[lane];
+          if (lane < NL) {
+            const int cl = col0 + lane;
+            const float tmax = fmaxf(fmaxf(rb[cl], rb[NQP + cl]), fmaxf(rb[2 * NQP + cl], rb[3 * NQP + cl]));
+            const float mo = mst[cl];
             if (tmax != NEG_INF) {
               const float ts = tmax * c2;
               if (mo == NEG_INF) {
-                mst[lane] = ts;
+                mst[cl] = ts;
               } else if (ts > mo + 8.f) {
                 alpha = fast_exp2(mo - ts);
-                mst[lane] = ts;
+                mst[cl] = ts;
               }
             }
-            ast[lane] = alpha;
+            ast[cl] = alpha;
           }
           const bool any = __any_sync(0xffffffffu, alpha != 1.f);
-          if (lane == 0) *rflag = any ? 1 : 0;
+          if (lane == 0) rflag[sw >> 2] = any ? 1 : 0;
         }
-        softmax_bar();
+        softmax_bar<SMT>();
         const int stage = (int)(ti % STAGES);
-        if (!kvalid) {
+        if (!kvalid && col0 == 0) {
           // rows past the unit may hold anything (even NaN): zero this key's V row
           unsigned char* vrow = kvs + stage * C::KV_STAGE + KB * C::BOX_BYTES + my_row * 128;
 #pragma unroll
@@ -587,22 +602,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (t >= 1) {
           tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err);
           tc_fence_after();
-          float o[NQP];
-          tmem_ld<NQP>(tq + (uint32_t)(2 * NQP), o);
+          float o[LW];
+          tmem_ld<LW>(tq + (uint32_t)(2 * NQP + col0), o);
           tc_wait_ld();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bar_ofree);
           ++pv;
 #pragma unroll
-          for (int n = 0; n < NA; ++n) oacc[n] += o[n];
+          for (int j = 0; j < NL; ++j) oacc[j] += o[j];
         }
         // rescale the running sums when some column's max moved
-        if (*rflag) {
-          if constexpr (NA >= 4) {
+        if (rflag[sw >> 2]) {
+          if constexpr (NL >= 4) {
 #pragma unroll
-            for (int n4 = 0; n4 < NA / 4; ++n4) {
-              const float4 a4 = reinterpret_cast<const float4*>(ast)[n4];
+            for (int n4 = 0; n4 < NL / 4; ++n4) {
+              const float4 a4 = reinterpret_cast<const float4*>(ast + col0)[n4];
               const float av[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
@@ -612,24 +627,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           } else {
 #pragma unroll
-            for (int n = 0; n < NA; ++n) {
-              lp[n] *= ast[n];
-              oacc[n] *= ast[n];
+            for (int j = 0; j < NL; ++j) {
+              lp[j] *= ast[col0 + j];
+              oacc[j] *= ast[col0 + j];
             }
           }
         }
-        // probabilities of this key; P^T row (bf16, swizzled MN-major), active chunks only
+        // probabilities of this key; P^T row (bf16, swizzled MN-major), this thread's chunks
 #pragma unroll
-        for (int c = 0; c < PCHA; ++c) {
+        for (int c = 0; c < PCHL; ++c) {
           float mv[8];
-          if constexpr (NA >= 8) {
-            const float4 m0 = reinterpret_cast<const float4*>(mst)[2 * c];
-            const float4 m1 = reinterpret_cast<const float4*>(mst)[2 * c + 1];
+          if constexpr (NL >= 8) {
+            const float4 m0 = reinterpret_cast<const float4*>(mst + col0)[2 * c];
+            const float4 m1 = reinterpret_cast<const float4*>(mst + col0)[2 * c + 1];
             mv[0] = m0.x; mv[1] = m0.y; mv[2] = m0.z; mv[3] = m0.w;
             mv[4] = m1.x; mv[5] = m1.y; mv[6] = m1.z; mv[7] = m1.w;
           } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) mv[e] = e < NA ? mst[e] : 0.f;
+            for (int e = 0; e < 8; ++e) mv[e] = e < NL ? mst[col0 + e] : 0.f;
           }
           uint32_t w4[4];
 #pragma unroll
@@ -637,10 +652,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             float pr2[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const int n = c * 8 + 2 * i + e;
-              if (n < NA) {
-                pr2[e] = (s[n] == NEG_INF) ? 0.f : fast_exp2(fmaf(s[n], c2, -mv[2 * i + e]));
-                lp[n] += pr2[e];
+              const int j = c * 8 + 2 * i + e;
+              if (j < NL) {
+                pr2[e] = (s[j] == NEG_INF) ? 0.f : fast_exp2(fmaf(s[j], c2, -mv[2 * i + e]));
+                lp[j] += pr2[e];
               } else {
                 pr2[e] = 0.f;
               }
@@ -648,40 +663,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             __nv_bfloat162 h2 = __floats2bfloat162_rn(pr2[0], pr2[1]);
             w4[i] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          uint32_t off = (uint32_t)(my_row * C::P_ROWB + c * 16);
+          uint32_t off = (uint32_t)(my_row * C::P_ROWB + (col0 / 8 + c) * 16);
           off ^= ((off >> 7) & ((1u << C::P_SWZ_BITS) - 1u)) << 4;
           *reinterpret_cast<uint4*>(ps + off) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
         fence_async_smem();
-        softmax_bar();
+        softmax_bar<SMT>();
         if (stid == 0) mbar_arrive(&bar_pfull);
       }
       {
         tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err);
         tc_fence_after();
-        float o[NQP];
-        tmem_ld<NQP>(tq + (uint32_t)(2 * NQP), o);
+        float o[LW];
+        tmem_ld<LW>(tq + (uint32_t)(2 * NQP + col0), o);
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_ofree);
         ++pv;
 #pragma unroll
-        for (int n = 0; n < NA; ++n) oacc[n] += o[n];
+        for (int j = 0; j < NL; ++j) oacc[j] += o[j];
       }
       it += n_t;
       ++units;
 
-      // ---- column sums of the unnormalised probabilities over the 128 threads
+      // ---- column sums of the unnormalised probabilities over the tile's 128 key rows
       float* lb = lred + (units & 1u) * (4 * NQP);
       {
-        float w[NA];
+        float w[NL];
 #pragma unroll
-        for (int n = 0; n < NA; ++n) w[n] = lp[n];
-        const float r = warp_col_reduce<NA, false>(w, lane);
-        if (lane < NA) lb[sw * NA + reduced_col<NA>(lane)] = r;
+        for (int j = 0; j < NL; ++j) w[j] = lp[j];
+        const float r = warp_col_reduce<NL, false>(w, lane);
+        if (lane < NL) lb[sq * NQP + col0 + reduced_col<NL>(lane)] = r;
       }
-      softmax_bar();
+      softmax_bar<SMT>();
+      auto lsum = [&](int n) { return lb[n] + lb[NQP + n] + lb[2 * NQP + n] + lb[3 * NQP + n]; };
 
       const int c_first = (int)(ustart / share);
       const int c_last = (int)((ustart + S.k_len - 1) / share);
@@ -703,11 +719,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       };
       if (n_contrib == 1) {
 #pragma unroll
-        for (int n = 0; n < NA; ++n) {
+        for (int j = 0; j < NL; ++j) {
+          const int n = col0 + j;
           if (n < nvec && dim_ok) {
-            const float L = lb[n] + lb[NA + n] + lb[2 * NA + n] + lb[3 * NA + n];
+            const float L = lsum(n);
             const long long oi = out_at(n);
-            if (oi >= 0) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(L > 0.f ? oacc[n] / L : 0.f);
+            if (oi >= 0) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(L > 0.f ? oacc[j] / L : 0.f);
           }
         }
       } else {
@@ -717,34 +734,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // O^T only for the unit's query columns (the merge reads no others)
         if (stid < NA) {
           pb[stid] = mst[stid];
-          pb[NQP + stid] = lb[stid] + lb[NA + stid] + lb[2 * NA + stid] + lb[3 * NA + stid];
+          pb[NQP + stid] = lsum(stid);
         }
 #pragma unroll
-        for (int n = 0; n < NA; ++n)
-          if (n < nvec && dim_ok) pb[2 * NQP + n * DH + dim] = oacc[n];
+        for (int j = 0; j < NL; ++j)
+          if (col0 + j < nvec && dim_ok) pb[2 * NQP + (col0 + j) * DH + dim] = oacc[j];
         __threadfence();
-        softmax_bar();
+        softmax_bar<SMT>();
         if (stid == 0) {
           const int prev = atomicAdd(p.ws_cnt + c_first, 1);
           s_flag = (prev == n_contrib - 1) ? 1 : 0;
         }
-        softmax_bar();
+        softmax_bar<SMT>();
         if (s_flag && dim_ok) {
           __threadfence();
-          // Online merge, columns in chunks of MCH: this CTA's own (m, l, O) come
-          // from shared memory and registers; for every other contributor all
-          // loads of a chunk are independent (one round trip per contributor).
-          constexpr int MCH = NA < 16 ? NA : 16;
+          // Online merge, this thread's columns in chunks of MCH: this CTA's own
+          // (m, l, O) come from shared memory and registers; for every other
+          // contributor all loads of a chunk are independent (one round trip each).
+          constexpr int MCH = NL < 16 ? NL : 16;
           const int k_own = (int)blockIdx.x - c_first;
 #pragma unroll
-          for (int c0 = 0; c0 < NA; c0 += MCH) {
+          for (int j0 = 0; j0 < NL; j0 += MCH) {
+            const int c0 = col0 + j0;
             if (c0 < nvec) {
               float M[MCH], Ls[MCH], acc[MCH];
 #pragma unroll
               for (int j = 0; j < MCH; ++j) {
                 M[j] = mst[c0 + j];
-                Ls[j] = lb[c0 + j] + lb[NA + c0 + j] + lb[2 * NA + c0 + j] + lb[3 * NA + c0 + j];
-                acc[j] = oacc[c0 + j];
+                Ls[j] = lsum(c0 + j);
+                acc[j] = oacc[j0 + j];
               }
               for (int k = 0; k < n_contrib; ++k) {
                 if (k == k_own) continue;
@@ -783,7 +801,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
         if (s_flag && stid == 0) p.ws_cnt[c_first] = 0;
-        softmax_bar();  // s_flag is re-written by the next unit
+        softmax_bar<SMT>();  // s_flag is re-written by the next unit
       }
     }
   }
