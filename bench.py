@@ -72,7 +72,7 @@ CFG5 = dict(B=64, R=16, H=32, Hkv=8, Dh=128, L0=32768, W=8, seed=5, alpha=0.8)
 # cfg3 was captured at batch 8 and scaled by the units processed (x4 at batch 32).
 NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
                      ("cfg2", "tc"): 543_091_968 + 6_767_104,
-                     ("cfg3", "tc"): (2_189_533_696 + 10_547_456) * 4,
+                     ("cfg3", "tc"): (2_189_340_160 + 8_944_640) * 4,
                      ("cfg4attn", "tc"): 3_631_410_688 + 8_572_672}
 
 
