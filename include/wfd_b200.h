@@ -241,6 +241,25 @@ int wfd_rope_split(const void* qkv, const float* cos_tab, const float* sin_tab, 
  * (dff % 8 == 0). */
 int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, int32_t dtype, void* stream);
 
+/* Row gather: out[i] = a[idx[i * idx_stride]] (+ b[same row] when b != NULL),
+ * rows of d elements (d % 8 == 0), n_src rows in a / b.  An index outside
+ * [0, n_src) sets the bad-rows bit of d_err and reads row 0. */
+int wfd_gather_rows(const void* a, const void* b, const int32_t* idx, int32_t idx_stride, void* out, int32_t n,
+                    int32_t d, int32_t n_src, int32_t dtype, int32_t* d_err, void* stream);
+
+/* Row scatter: dst[idx[i * idx_stride]] = src[i], and zero[that row] = 0 when
+ * zero != NULL; an index outside [0, n_dst) sets the bad-rows bit and is skipped. */
+int wfd_scatter_rows(const void* src, const int32_t* idx, int32_t idx_stride, void* dst, void* zero, int32_t n,
+                     int32_t d, int32_t n_dst, int32_t dtype, int32_t* d_err, void* stream);
+
+/* Wave item table from a union table of int32 rows of `cols` columns:
+ * items[i] = {tab[i][c_slot], tab[i][c_seq], tab[i][c_pos], tab[i][c_qlen], i}. */
+int wfd_items_from_table(const int32_t* tab, int32_t cols, int32_t c_slot, int32_t c_seq, int32_t c_pos,
+                         int32_t c_qlen, wfd_item* items, int32_t n, void* stream);
+
+/* Greedy ids: out[r] = the first index of the maximum of logits row r (n rows of V). */
+int wfd_argmax_rows(const void* x, int32_t* out, int32_t n, int32_t V, int32_t dtype, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Device-side wavefront scheduling (route / settle of scheduler_batch.py:268-360
  * as kernels, so one CUDA graph runs a whole tick; no counterpart in the

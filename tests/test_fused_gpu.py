@@ -89,3 +89,42 @@ def test_rope_bad_position_sets_error(cuda_dev):
     with pytest.raises(_abi.WfdError):
         rt.read_device_error(cuda_dev)           # reads and clears the word
     assert rt.read_device_error(cuda_dev) == 0
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_row_plumbing(cuda_dev, dt):
+    from wavefront_decoding_b200 import fused
+    g = gi.gen(34)
+    a = torch.randn((50, 256), generator=g).to(dt).to(cuda_dev)
+    b = torch.randn((50, 256), generator=g).to(dt).to(cuda_dev)
+    tab = torch.randint(0, 50, (17, 3), generator=g, dtype=torch.int32).to(cuda_dev)
+    idx = tab[:, 1]                                    # strided int32 column
+    il = idx.long()
+    assert torch.equal(fused.gather_rows(a, idx), a[il])
+    assert torch.equal(fused.gather_rows(a, idx, b=b), (a.float()[il] + b.float()[il]).to(dt))
+    uniq = torch.randperm(50, generator=g)[:17].to(torch.int32).to(cuda_dev)
+    dst, zero = a.clone(), b.clone()
+    src = torch.randn((17, 256), generator=g).to(dt).to(cuda_dev)
+    fused.scatter_rows(src, uniq, dst, zero=zero)
+    ref_d, ref_z = a.clone(), b.clone()
+    ref_d[uniq.long()] = src
+    ref_z[uniq.long()] = 0
+    assert torch.equal(dst, ref_d) and torch.equal(zero, ref_z)
+
+
+def test_items_from_table_and_argmax(cuda_dev):
+    from wavefront_decoding_b200 import fused
+    g = gi.gen(35)
+    tab = torch.randint(0, 1000, (33, 8), generator=g, dtype=torch.int32).to(cuda_dev)
+    items = torch.empty((33, 5), dtype=torch.int32, device=cuda_dev)
+    fused.items_from_table(tab, 4, 3, 1, 5, items)
+    ref = torch.stack([tab[:, 4], tab[:, 3], tab[:, 1], tab[:, 5],
+                       torch.arange(33, dtype=torch.int32, device=cuda_dev)], dim=1)
+    assert torch.equal(items, ref)
+    for dt in (torch.float32, torch.bfloat16):
+        x = torch.randn((9, 50304), generator=g).to(dt).to(cuda_dev)
+        x[3, 100] = x[3, 2000] = x[3].max() + 1        # a tie: the first index wins, as torch.argmax
+        out = torch.empty(9, dtype=torch.int32, device=cuda_dev)
+        fused.argmax_rows(x, out)
+        assert torch.equal(out.long(), x.float().argmax(dim=-1))
+        assert int(out[3]) == 100

@@ -23,7 +23,8 @@ EXPORTED = (
     "wfd_wave_attn", "wfd_wave_attn_static", "wfd_wave_attn_kernel", "wfd_attn_varlen", "wfd_attn_segments",
     "wfd_append",
     "wfd_write_prefill", "wfd_commit_drop", "wfd_commit_window", "wfd_gather_pack",
-    "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul",
+    "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul", "wfd_gather_rows", "wfd_scatter_rows",
+    "wfd_items_from_table", "wfd_argmax_rows",
     "wfd_sched_pre_tick", "wfd_sched_route", "wfd_sched_settle",
 )
 
@@ -88,6 +89,14 @@ _SIGS = {
     "wfd_rope_split": ([_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     # gu out n dff dtype stream
     "wfd_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
+    # a b idx stride out n d n_src dtype err stream
+    "wfd_gather_rows": ([_P, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P], _I),
+    # src idx stride dst zero n d n_dst dtype err stream
+    "wfd_scatter_rows": ([_P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _P], _I),
+    # tab cols c_slot c_seq c_pos c_qlen items n stream
+    "wfd_items_from_table": ([_P, _I, _I, _I, _I, _I, _P, _I, _P], _I),
+    # x out n V dtype stream
+    "wfd_argmax_rows": ([_P, _P, _I, _I, _I, _P], _I),
     # const wfd_sched_params*, stream
     "wfd_sched_pre_tick": ([_P, _P], _I),
     "wfd_sched_route": ([_P, _P], _I),

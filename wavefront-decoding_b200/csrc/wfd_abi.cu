@@ -802,6 +802,75 @@ extern "C" int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, i
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
+extern "C" int wfd_gather_rows(const void* a, const void* b, const int32_t* idx, int32_t idx_stride, void* out,
+                               int32_t n, int32_t d, int32_t n_src, int32_t dtype, int32_t* d_err, void* stream) {
+  if (n < 0 || d <= 0 || d % 8 != 0 || n_src <= 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!a || !idx || !out || !d_err) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(a) || (b && !aligned16(b)) || !aligned16(out)) return WFD_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = model_grid((long long)n * (d / 8));
+  if (dtype == WFD_DTYPE_BF16)
+    gather_rows_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b), idx, idx_stride,
+        static_cast<__nv_bfloat16*>(out), n, d, n_src, d_err);
+  else if (dtype == WFD_DTYPE_F32)
+    gather_rows_kernel<float><<<grid, kModelThreads, 0, st>>>(static_cast<const float*>(a),
+                                                             static_cast<const float*>(b), idx, idx_stride,
+                                                             static_cast<float*>(out), n, d, n_src, d_err);
+  else
+    return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+extern "C" int wfd_scatter_rows(const void* src, const int32_t* idx, int32_t idx_stride, void* dst, void* zero,
+                                int32_t n, int32_t d, int32_t n_dst, int32_t dtype, int32_t* d_err, void* stream) {
+  if (n < 0 || d <= 0 || d % 8 != 0 || n_dst <= 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!src || !idx || !dst || !d_err) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(src) || !aligned16(dst) || (zero && !aligned16(zero))) return WFD_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = model_grid((long long)n * (d / 8));
+  if (dtype == WFD_DTYPE_BF16)
+    scatter_rows_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(src), idx, idx_stride, static_cast<__nv_bfloat16*>(dst),
+        static_cast<__nv_bfloat16*>(zero), n, d, n_dst, d_err);
+  else if (dtype == WFD_DTYPE_F32)
+    scatter_rows_kernel<float><<<grid, kModelThreads, 0, st>>>(static_cast<const float*>(src), idx, idx_stride,
+                                                              static_cast<float*>(dst), static_cast<float*>(zero), n,
+                                                              d, n_dst, d_err);
+  else
+    return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+extern "C" int wfd_items_from_table(const int32_t* tab, int32_t cols, int32_t c_slot, int32_t c_seq, int32_t c_pos,
+                                    int32_t c_qlen, wfd_item* items, int32_t n, void* stream) {
+  if (n < 0 || cols <= 0) return WFD_ERR_INVALID_ARG;
+  if (c_slot < 0 || c_slot >= cols || c_seq < 0 || c_seq >= cols || c_pos < 0 || c_pos >= cols || c_qlen < 0 ||
+      c_qlen >= cols)
+    return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!tab || !items) return WFD_ERR_INVALID_ARG;
+  items_from_table_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      tab, cols, c_slot, c_seq, c_pos, c_qlen, reinterpret_cast<int32_t*>(items), n);
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+extern "C" int wfd_argmax_rows(const void* x, int32_t* out, int32_t n, int32_t V, int32_t dtype, void* stream) {
+  if (n < 0 || V <= 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!x || !out) return WFD_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == WFD_DTYPE_BF16)
+    argmax_rows_kernel<__nv_bfloat16><<<n, kModelThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), out, V);
+  else if (dtype == WFD_DTYPE_F32)
+    argmax_rows_kernel<float><<<n, kModelThreads, 0, st>>>(static_cast<const float*>(x), out, V);
+  else
+    return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
 // ---------------------------------------------------------------------------
 // device-side wavefront scheduling
 // ---------------------------------------------------------------------------

@@ -151,3 +151,121 @@ __global__ void __launch_bounds__(kModelThreads) silu_mul_kernel(const T* __rest
 }
 
 }  // namespace wfd
+
+namespace wfd {
+
+// ---------------------------------------------------------------------------
+// Engine row plumbing: gathers / scatters of state-pool rows by int32 indices
+// (a strided column of the union table), the wave item table built from the
+// union table, and the greedy id of each logits row.
+// ---------------------------------------------------------------------------
+
+// out[i] = a[idx[i * s]] (+ b[idx[i * s]] when b is given), rows of d elements
+template <typename T>
+__global__ void __launch_bounds__(kModelThreads)
+    gather_rows_kernel(const T* __restrict__ a, const T* __restrict__ b, const int32_t* __restrict__ idx, int stride,
+                       T* __restrict__ out, int n, int d, int n_src, int* err) {
+  const int vpr = d / 8;
+  const long long total = (long long)n * vpr;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int i = (int)(e / vpr), c = (int)(e - (long long)i * vpr) * 8;
+    int r = idx[(long long)i * stride];
+    if (r < 0 || r >= n_src) {
+      set_error(err, kErrBadRows);
+      r = 0;
+    }
+    float v[8];
+    Vec8<T>::load(a + (long long)r * d + c, v);
+    if (b != nullptr) {
+      float w[8];
+      Vec8<T>::load(b + (long long)r * d + c, w);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] += w[k];
+    }
+    Vec8<T>::store(out + (long long)i * d + c, v);
+  }
+}
+
+// dst[idx[i * s]] = src[i] (and zero[idx[i * s]] = 0 when zero is given)
+template <typename T>
+__global__ void __launch_bounds__(kModelThreads)
+    scatter_rows_kernel(const T* __restrict__ src, const int32_t* __restrict__ idx, int stride, T* __restrict__ dst,
+                        T* __restrict__ zero, int n, int d, int n_dst, int* err) {
+  const int vpr = d / 8;
+  const long long total = (long long)n * vpr;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int i = (int)(e / vpr), c = (int)(e - (long long)i * vpr) * 8;
+    const int r = idx[(long long)i * stride];
+    if (r < 0 || r >= n_dst) {
+      set_error(err, kErrBadRows);
+      continue;
+    }
+    float v[8];
+    Vec8<T>::load(src + (long long)i * d + c, v);
+    Vec8<T>::store(dst + (long long)r * d + c, v);
+    if (zero != nullptr) {
+      float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      Vec8<T>::store(zero + (long long)r * d + c, z);
+    }
+  }
+}
+
+// items[i] = {tab[i][c_slot], tab[i][c_seq], tab[i][c_pos], tab[i][c_qlen], i}
+__global__ void items_from_table_kernel(const int32_t* __restrict__ tab, int cols, int c_slot, int c_seq, int c_pos,
+                                        int c_qlen, int32_t* __restrict__ items, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int32_t* r = tab + (long long)i * cols;
+    int32_t* it = items + (long long)i * 5;
+    it[0] = r[c_slot];
+    it[1] = r[c_seq];
+    it[2] = r[c_pos];
+    it[3] = r[c_qlen];
+    it[4] = i;
+  }
+}
+
+// out[r] = argmax over the V logits of row r (the first index of the maximum,
+// as torch.argmax), one CTA per row
+template <typename T>
+__global__ void __launch_bounds__(kModelThreads) argmax_rows_kernel(const T* __restrict__ x, int32_t* __restrict__ out,
+                                                                     int V) {
+  const T* row = x + (long long)blockIdx.x * V;
+  float best = -__int_as_float(0x7f800000);
+  int bi = 0x7fffffff;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) {
+    const float v = to_f(row[j]);
+    if (v > best || (v == best && j < bi)) {
+      best = v;
+      bi = j;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  __shared__ float sb[kModelThreads / 32];
+  __shared__ int si[kModelThreads / 32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sb[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < kModelThreads / 32; ++k)
+      if (sb[k] > best || (sb[k] == best && si[k] < bi)) {
+        best = sb[k];
+        bi = si[k];
+      }
+    out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+}  // namespace wfd

@@ -748,9 +748,10 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         softmax_bar<SMT>();
         if (s_flag && dim_ok) {
           __threadfence();
-          // Online merge, this thread's columns in chunks of MCH: this CTA's own
-          // (m, l, O) come from shared memory and registers; for every other
-          // contributor all loads of a chunk are independent (one round trip each).
+          // Online merge, this thread's columns in chunks of MCH, contributors in
+          // key order (the result does not depend on which CTA arrives last): this
+          // CTA's own (m, l, O) come from shared memory and registers; for every
+          // other contributor all loads of a chunk are independent (one round trip).
           constexpr int MCH = NL < 16 ? NL : 16;
           const int k_own = (int)blockIdx.x - c_first;
 #pragma unroll
@@ -760,21 +761,29 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
               float M[MCH], Ls[MCH], acc[MCH];
 #pragma unroll
               for (int j = 0; j < MCH; ++j) {
-                M[j] = mst[c0 + j];
-                Ls[j] = lsum(c0 + j);
-                acc[j] = oacc[j0 + j];
+                M[j] = NEG_INF;
+                Ls[j] = 0.f;
+                acc[j] = 0.f;
               }
               for (int k = 0; k < n_contrib; ++k) {
-                if (k == k_own) continue;
-                const int cc = c_first + k;
-                const int sl = (k == 0) ? 2 * cc + 1 : 2 * cc;
-                const float* base = p.ws_part + (size_t)sl * C::PART_FLOATS;
                 float mk[MCH], lk[MCH], ok[MCH];
+                if (k == k_own) {
 #pragma unroll
-                for (int j = 0; j < MCH; ++j) {
-                  mk[j] = ld_cg_f32(base + c0 + j);
-                  lk[j] = ld_cg_f32(base + NQP + c0 + j);
-                  ok[j] = (c0 + j < nvec) ? ld_cg_f32(base + 2 * NQP + (c0 + j) * DH + dim) : 0.f;
+                  for (int j = 0; j < MCH; ++j) {
+                    mk[j] = mst[c0 + j];
+                    lk[j] = lsum(c0 + j);
+                    ok[j] = oacc[j0 + j];
+                  }
+                } else {
+                  const int cc = c_first + k;
+                  const int sl = (k == 0) ? 2 * cc + 1 : 2 * cc;
+                  const float* base = p.ws_part + (size_t)sl * C::PART_FLOATS;
+#pragma unroll
+                  for (int j = 0; j < MCH; ++j) {
+                    mk[j] = ld_cg_f32(base + c0 + j);
+                    lk[j] = ld_cg_f32(base + NQP + c0 + j);
+                    ok[j] = (c0 + j < nvec) ? ld_cg_f32(base + 2 * NQP + (c0 + j) * DH + dim) : 0.f;
+                  }
                 }
 #pragma unroll
                 for (int j = 0; j < MCH; ++j) {

@@ -31,6 +31,7 @@ import numpy as np
 import torch
 
 from . import attention as wa
+from . import fused
 from . import runtime as rt
 from .kv_cache import SlotKVCache
 from .looped_lm import LoopedLM
@@ -64,6 +65,15 @@ class _Tables:
         self.graph = None
         self.uploaded = torch.cuda.Event()   # the staging copy may be rewritten once this fired
         self.pending = False
+        self._consts: dict[int, torch.Tensor] = {}
+
+    def const(self, v: int) -> torch.Tensor:
+        """A (cap,) int32 column of v, made once (first use is an eager warm-up, before any capture)."""
+        c = self._consts.get(v)
+        if c is None:
+            c = self.ones * v
+            self._consts[v] = c
+        return c
 
 
 class WaveEngine:
@@ -184,7 +194,7 @@ class WaveEngine:
         m = self.model
         tab = t.dev
         q, k, v = m.qkv(blk, x, pos=tab[:, 1])
-        self.cache.write_tokens(t.ones * slot, tab[:, 3], tab[:, 1], k, v)
+        self.cache.write_tokens(t.const(slot), tab[:, 3], tab[:, 1], k, v)
         o = wa.attn_segments(q, self.Kflat, self.Vflat, t.row_ids, tab[:, 5], tab[:, 6 + j], tab[:, 1] + 1, 1,
                              causal=False)
         return m.finish_block(blk, x, o)
@@ -192,32 +202,26 @@ class WaveEngine:
     def _body(self, kind: str, t: _Tables) -> None:
         m, cfg = self.model, self.cfg
         tab = t.dev
-        rows = tab[:, 0].long()
+        rows = tab[:, 0]
         if kind == "P":
-            x = m.embed.index_select(0, tab[:, 2].long())
+            x = fused.gather_rows(m.embed, tab[:, 2])
             for j, blk in enumerate(m.prelude):
                 x = self._segment_block(blk, x, t, j, cfg.slot_prelude(j))
-            self.pool_e.index_copy_(0, rows, x)
-            self.pool_h.index_copy_(0, rows, torch.zeros_like(x))
+            fused.scatter_rows(x, rows, self.pool_e, zero=self.pool_h)
         elif kind == "R":
-            x = self.pool_h.index_select(0, rows) + self.pool_e.index_select(0, rows)
-            items = t.items
-            items[:, 0] = tab[:, 4]
-            items[:, 1] = tab[:, 3]
-            items[:, 2] = tab[:, 1]
-            items[:, 3] = tab[:, 5]
-            items[:, 4] = t.row_ids
+            x = fused.gather_rows(self.pool_h, rows, b=self.pool_e)
+            fused.items_from_table(tab, 4, 3, 1, 5, t.items)   # (slot base, seq, position, live, row)
             for l, blk in enumerate(m.core):
                 q, k, v = m.qkv(blk, x, pos=tab[:, 1])
-                o = wa.wave_attn(q, k, v, self.cache.K, self.cache.V, items, 1, lens=self.cache.lens,
+                o = wa.wave_attn(q, k, v, self.cache.K, self.cache.V, t.items, 1, lens=self.cache.lens,
                                  slot_offset=cfg.n_prelude + l)
                 x = m.finish_block(blk, x, o)
-            self.pool_h.index_copy_(0, rows, x)
+            fused.scatter_rows(x, rows, self.pool_h)
         else:
-            x = self.pool_h.index_select(0, rows)
+            x = fused.gather_rows(self.pool_h, rows)
             for j, blk in enumerate(m.coda):
                 x = self._segment_block(blk, x, t, j, cfg.slot_coda(j))
-            t.out.copy_(m.logits(x).argmax(dim=-1).to(torch.int32))
+            m.greedy_ids(x, t.out)
 
     def _run(self, kind: str, t: _Tables) -> None:
         self.n_launch_calls += 1

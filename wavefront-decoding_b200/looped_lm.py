@@ -163,6 +163,10 @@ class LoopedLM:
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         return (self.rmsnorm(x.contiguous(), self.final_norm) @ self.lm_head).float()
 
+    def greedy_ids(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """out (int32) = argmax of each row's logits (first maximum), without an fp32 copy."""
+        return fused.argmax_rows(self.rmsnorm(x.contiguous(), self.final_norm) @ self.lm_head, out)
+
     # ------------------------------------------------------------------
     @torch.no_grad()
     def prefill_dense(self, ids: torch.Tensor, cache) -> torch.Tensor:
