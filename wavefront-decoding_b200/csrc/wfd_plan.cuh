@@ -36,6 +36,10 @@ struct PlanParams {
   // outputs
   Seg* segs;
   long long* prefix;  // n + 1 entries, per-kv-head work units
+  // optional: the first segment of each CTA of a persistent grid of seg_grid
+  // CTAs that splits seg_units * prefix[n] into equal shares (tcgen05 kernel)
+  int* seg0;
+  int seg_grid, seg_units;
   // zero-fill of query rows that see no keys (k_len == 0)
   void* out;
   int Hq, Dh, elem_bytes;
@@ -157,6 +161,25 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) 
     __syncthreads();
   }
   if (threadIdx.x == 0) p.prefix[p.n] = carry;
+  if (p.seg0 != nullptr) {
+    __syncthreads();  // the prefix above is complete and visible to the block
+    const long long total = (long long)p.seg_units * carry;
+    const long long share = total > 0 ? (total + p.seg_grid - 1) / p.seg_grid : 1;
+    for (int c = threadIdx.x; c < p.seg_grid; c += blockDim.x) {
+      const long long a = (long long)c * share;
+      int lo = 0, hi = p.n - 1;  // largest i with seg_units * prefix[i] <= a
+      if (total <= 0 || a >= total) {
+        lo = 0;
+      } else {
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if ((long long)p.seg_units * p.prefix[mid] <= a) lo = mid;
+          else hi = mid - 1;
+        }
+      }
+      p.seg0[c] = lo;
+    }
+  }
 }
 
 }  // namespace wfd

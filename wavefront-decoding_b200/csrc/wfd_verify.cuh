@@ -58,6 +58,7 @@ struct VerifyParams {
   void* out;
   const Seg* segs;
   const long long* prefix;
+  const int* seg0;  // first segment of each CTA, from the plan kernel (null: search it here)
   int n_segs;
   int Hq, Hkv, G;
   float scale_log2;
@@ -349,7 +350,9 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   // threads probe 192 pivots of [lo, hi] at once, so up to 192 segments take
   // one round of loads instead of a chain of dependent ones.
   int seg0 = 0;
-  if (a < b) {
+  if (a < b && p.seg0 != nullptr) {
+    seg0 = p.seg0[blockIdx.x];
+  } else if (a < b) {
     int lo = 0, hi = p.n_segs - 1;
     while (lo < hi) {
       const int span = hi - lo;
