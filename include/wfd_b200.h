@@ -73,7 +73,10 @@ const char* wfd_status_string(int status);
 
 /* Copy the device error word to *h_err and reset it to 0 (synchronises
  * `stream`).  Returns WFD_OK, or WFD_ERR_DEVICE_TIMEOUT / _BOUNDS when the word
- * was non-zero. */
+ * was non-zero.  Bits: 1 bounded wait gave up, 2 slot / sequence out of range,
+ * 4 position or length past the slot capacity, 8 row index outside the given
+ * tensors, 16 bad cu_seqlens, 128 a device-scheduler invariant (token-slot
+ * overflow, two commit points of one sequence in a tick, R union over capacity). */
 int wfd_read_error(int32_t* d_err, int32_t* h_err, void* stream);
 
 /* Bytes of device workspace the attention entry points need for up to

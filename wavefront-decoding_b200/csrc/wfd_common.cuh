@@ -37,6 +37,7 @@ enum : int {
   kErrBadPos = 1 << 2,       // position or length outside the slot capacity
   kErrBadRows = 1 << 3,      // query / new-row index outside the given tensors
   kErrBadSegs = 1 << 4,      // cu_seqlens not monotone / out of range
+  kErrSched = 1 << 7,        // device-scheduler invariant (slot overflow, two commit points in a tick)
 };
 
 __device__ __forceinline__ void set_error(int* err, int bits) {

@@ -26,7 +26,6 @@ constexpr int kSchedThreads = 1024;
 constexpr int kSchedMaxW = 32;
 enum : int { kCtP = 0, kCtR = 1, kCtC = 2, kCtProp = 3, kCtAcc = 4, kCtRej = 5, kCtRoll = 6, kSeqCounters = 8 };
 enum : int { kBtTicks = 0, kBtP = 1, kBtC = 2, kBtRTotal = 3, kBtRMax = 4, kBatchCounters = 8 };
-enum : int { kErrSched = 1 << 7 };  // scheduler invariant broken (slot overflow, two verifies in one tick)
 
 struct SchedParams {
   // token slots (B * W)
