@@ -79,6 +79,17 @@ const char* wfd_status_string(int status);
  * overflow, two commit points of one sequence in a tick, R union over capacity). */
 int wfd_read_error(int32_t* d_err, int32_t* h_err, void* stream);
 
+/* Batch-invariant attention (process-wide, default off).  On: bf16 attention runs
+ * on the tensor-core kernel with every (item, kv head) unit processed whole by
+ * one CTA — no split, no merge — so a row's output depends on its own unit
+ * only, not on the other items of the launch (what bit-exact greedy equality of
+ * wavefront and sequential decoding needs, together with fixed GEMM shapes).
+ * Read when a launch is built: a captured CUDA graph keeps its mode.  fp32 stays
+ * on the CUDA-core kernel, which is not batch-invariant.  No counterpart in the
+ * reference. */
+int wfd_set_batch_invariant(int32_t on);
+int wfd_get_batch_invariant(void);
+
 /* Bytes of device workspace the attention entry points need for up to
  * `max_items` work items / segments.  The workspace must be zero-filled once
  * after allocation (wfd_workspace_init); the kernels leave it zeroed again. */

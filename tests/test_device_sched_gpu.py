@@ -101,3 +101,23 @@ def test_device_repeat_generation_reuses_graph(cuda_dev):
     a = _summary(dw.generate(prompts), eng, B)
     b = _summary(dw.generate(prompts), eng, B)
     assert a == b and len(dw._graphs) == 1
+
+
+@pytest.mark.parametrize("cfg_name", ["small", "config1"])
+def test_bf16_wavefront_bit_exact_with_batch_invariance(cuda_dev, cfg_name):
+    """bf16: with fixed union capacities and batch-invariant attention, greedy
+    wavefront decoding (T_draft 1, 2) commits exactly the tokens of sequential
+    decoding (T_draft = T_total) for every sequence."""
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import generate_wavefront_device
+    from wavefront_decoding_b200.looped_lm import CONFIG1
+    cfg = _small_cfg() if cfg_name == "small" else CONFIG1
+    B, L, N = (8, 16, 40) if cfg_name == "small" else (4, 128, 48)
+    prompts = _prompts(B, L, cfg.vocab, seed=31)
+    runs = {}
+    for d in (cfg.T_total, 1, 2):
+        _, eng = _engine(cfg, B, L + N + 2 * cfg.T_total + 8, dtype=torch.bfloat16)
+        bt = generate_wavefront_device(eng, prompts, N, sch.SsdPolicy(cfg.T_total, d), batch_invariant=True)
+        runs[d] = [t.tokens for t in bt.per_seq]
+    assert runs[1] == runs[cfg.T_total]
+    assert runs[2] == runs[cfg.T_total]

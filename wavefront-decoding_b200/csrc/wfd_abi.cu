@@ -4,6 +4,7 @@
 // and launches.  Every launch goes to the caller's stream; nothing here
 // allocates device memory or synchronises (except wfd_read_error, whose job is
 // to read the device error word).
+#include <atomic>
 #include <cmath>
 #include <cstddef>
 #include <cstdio>
@@ -24,6 +25,10 @@ using namespace wfd;
 namespace {
 
 constexpr int kMaxDevices = 64;
+
+// Batch-invariant attention (wfd_set_batch_invariant): read when a launch is
+// built, so a captured CUDA graph keeps the mode it was captured with.
+std::atomic<int> g_batch_invariant{0};
 constexpr int kGridPerSm = 4;  // upper bound on resident decode CTAs per SM used for sizing
 
 struct DevInfo {
@@ -281,7 +286,8 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   // on the CUDA cores (54 % vs 52 %), as does fp32 (tcgen05 would take it as tf32).
   const bool pair_ok = A.Dh == 64 && A.Hkv % 2 == 0 && 2ll * G * max_q <= kVerifyMaxRows;
   const bool odd_mha_d64_decode = A.Dh == 64 && !pair_ok && (long long)G * max_q == 1;
-  if (which < 0) which = (tc_ok && !odd_mha_d64_decode) ? 1 : 0;
+  const bool invariant = g_batch_invariant.load(std::memory_order_relaxed) != 0;
+  if (which < 0) which = (tc_ok && (invariant || !odd_mha_d64_decode)) ? 1 : 0;
   if (which == 1 && !tc_ok) return WFD_ERR_UNSUPPORTED;
   const bool pair = which == 1 && pair_ok;
   const int Gv = pair ? 2 * G : G;  // query vectors per unit and kv (pair) head
@@ -360,6 +366,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     vp.Hkv = pair ? A.Hkv / 2 : A.Hkv;
     vp.G = G;
     vp.pair = pair ? 1 : 0;
+    vp.invariant = invariant ? 1 : 0;
     vp.scale_log2 = scale * log2e;
     vp.causal = A.causal;
     vp.k_row_offset = k_row_offset;
@@ -540,6 +547,13 @@ const char* wfd_status_string(int status) {
     default: return "unknown status";
   }
 }
+
+int wfd_set_batch_invariant(int32_t on) {
+  g_batch_invariant.store(on ? 1 : 0);
+  return WFD_OK;
+}
+
+int wfd_get_batch_invariant(void) { return g_batch_invariant.load(); }
 
 int wfd_read_error(int32_t* d_err, int32_t* h_err, void* stream) {
   if (!d_err || !h_err) return WFD_ERR_INVALID_ARG;

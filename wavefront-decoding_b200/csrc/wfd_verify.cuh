@@ -65,6 +65,10 @@ struct VerifyParams {
   int causal;
   long long k_row_offset;
   int pair;  // 1: units are pairs of head_dim-64 kv heads (Hkv counts pairs, DH == 128)
+  // 1: batch-invariant split: every unit is processed whole by the CTA whose share
+  // contains its first key (no split, no merge), so a row's result depends on its
+  // own unit only, not on the other work items of the launch
+  int invariant;
   float* ws_part;
   int* ws_cnt;
   int* err;
@@ -249,18 +253,30 @@ struct UnitIter {
   int seg;
   __device__ __forceinline__ bool next(const VerifyParams& p, Seg& S, int& u, int& r_lo, int& r_hi,
                                        long long& unit_start) {
-    if (pos >= b) return false;
-    while (seg + 1 <= p.n_segs - 1 && (long long)p.Hkv * p.prefix[seg + 1] <= pos) ++seg;
-    S = p.segs[seg];
-    const long long seg_base = (long long)p.Hkv * p.prefix[seg];
-    const long long o = pos - seg_base;
-    u = (int)(o / S.k_len);
-    r_lo = (int)(o - (long long)u * S.k_len);
-    unit_start = seg_base + (long long)u * S.k_len;
-    const long long unit_end = unit_start + S.k_len;
-    r_hi = (int)(((unit_end < b) ? unit_end : b) - unit_start);
-    pos = unit_start + r_hi;
-    return true;
+    for (;;) {
+      if (pos >= b) return false;
+      while (seg + 1 <= p.n_segs - 1 && (long long)p.Hkv * p.prefix[seg + 1] <= pos) ++seg;
+      S = p.segs[seg];
+      const long long seg_base = (long long)p.Hkv * p.prefix[seg];
+      const long long o = pos - seg_base;
+      u = (int)(o / S.k_len);
+      unit_start = seg_base + (long long)u * S.k_len;
+      const long long unit_end = unit_start + S.k_len;
+      if (p.invariant) {
+        if (unit_start < pos) {  // began in the previous CTA's share: that CTA processes it
+          pos = unit_end;
+          continue;
+        }
+        r_lo = 0;
+        r_hi = S.k_len;  // whole unit, possibly past b
+        pos = unit_end;
+        return true;
+      }
+      r_lo = (int)(o - (long long)u * S.k_len);
+      r_hi = (int)(((unit_end < b) ? unit_end : b) - unit_start);
+      pos = unit_start + r_hi;
+      return true;
+    }
   }
 };
 
@@ -704,7 +720,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
 
       const int c_first = (int)(ustart / share);
       const int c_last = (int)((ustart + S.k_len - 1) / share);
-      const int n_contrib = c_last - c_first + 1;
+      const int n_contrib = p.invariant ? 1 : c_last - c_first + 1;
       const int dim = my_row;  // O^T TMEM lane == head dim (lanes >= DH hold nothing)
       const bool dim_ok = dim < DH;
       // output element of query column n held by this thread's O^T row, or -1

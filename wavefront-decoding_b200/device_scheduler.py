@@ -14,6 +14,12 @@ at most one token per sequence), so no tick runs after the last commit.
 
 Emulated acceptance draws (EmulatedAcceptance) are taken on the host in the
 same order the host scheduler consumes them and uploaded once.
+
+batch_invariant=True gives bit-exact greedy equality of wavefront and
+sequential decoding (T_draft = T_total) in bf16: every union runs at a fixed
+row capacity that does not depend on T_draft (so each GEMM sees the same shape
+in every run, and a row's result does not depend on its neighbours), and the
+attention runs in the library's batch-invariant mode (no split, no merge).
 """
 from __future__ import annotations
 
@@ -35,7 +41,7 @@ _CT = ("n_p_calls", "n_r_calls", "n_c_calls", "n_drafts_proposed", "n_drafts_acc
 class DeviceWave:
     """Device scheduling state and the tick graph for one engine / length budget."""
 
-    def __init__(self, engine: WaveEngine, max_new_tokens: int, policy: SsdPolicy):
+    def __init__(self, engine: WaveEngine, max_new_tokens: int, policy: SsdPolicy, batch_invariant: bool = False):
         eng = engine
         cfg = eng.cfg
         if policy.T_total != cfg.T_total:
@@ -43,6 +49,7 @@ class DeviceWave:
         self.eng = eng
         self.policy = policy
         self.max_new = max_new_tokens
+        self.batch_invariant = batch_invariant
         B = eng.B
         self.B = B
         self.W = cfg.T_total + 2
@@ -69,8 +76,9 @@ class DeviceWave:
         self.batch_ct = torch.zeros(8, **i32)
         self.keys = torch.zeros(3, dtype=torch.int64, device=dev)
         self.c_slot = torch.full((2 * B,), -1, **i32)
-        # union tables: P one row per sequence, C two, R the live tokens
-        self.r_cap = B * (cfg.T_total // policy.T_draft + 2)
+        # union tables: P one row per sequence, C two, R the live tokens (a
+        # capacity independent of T_draft in batch-invariant mode)
+        self.r_cap = B * ((cfg.T_total if batch_invariant else cfg.T_total // policy.T_draft) + 2)
         self.tp = _Tables("P", B, 6 + cfg.n_prelude, dev)
         self.tr = _Tables("R", self.r_cap, 6, dev)
         self.tc = _Tables("C", 2 * B, 6 + cfg.n_coda, dev)
@@ -121,6 +129,10 @@ class DeviceWave:
     def _capture(self, p) -> torch.cuda.CUDAGraph:
         # warm up on an all-finished state (every row padding, nothing changes),
         # then capture; the real state is loaded afterwards (pointers are fixed)
+        with rt.batch_invariant(self.batch_invariant):
+            return self._capture_graph(p)
+
+    def _capture_graph(self, p) -> torch.cuda.CUDAGraph:
         self.done.fill_(1)
         cur = torch.cuda.current_stream(self.device)
         side = torch.cuda.Stream(self.device)
@@ -194,11 +206,12 @@ class DeviceWave:
             k = max(1, min(max(remaining), guard - ticks))
             if ticks >= guard:
                 raise RuntimeError(f"device wavefront exceeded the tick guard ({guard})")
-            for _ in range(k):
-                if graph is not None:
-                    graph.replay()
-                else:
-                    self._tick(p)
+            with rt.batch_invariant(self.batch_invariant):
+                for _ in range(k):
+                    if graph is not None:
+                        graph.replay()
+                    else:
+                        self._tick(p)
             ticks += k
         torch.cuda.synchronize(self.device)
         rt.read_device_error(self.device)
@@ -227,7 +240,7 @@ class DeviceWave:
 
 
 def generate_wavefront_device(engine: WaveEngine, prompt_ids: torch.Tensor, max_new_tokens: int, policy: SsdPolicy,
-                              emus=None, *, use_graph: bool = True) -> BatchTrace:
+                              emus=None, *, use_graph: bool = True, batch_invariant: bool = False) -> BatchTrace:
     """scheduler.generate_wavefront_batch with route / settle on the device."""
-    return DeviceWave(engine, max_new_tokens, policy).generate(prompt_ids, emus, use_graph=use_graph)
+    return DeviceWave(engine, max_new_tokens, policy, batch_invariant).generate(prompt_ids, emus, use_graph=use_graph)
 

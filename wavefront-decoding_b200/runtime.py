@@ -104,3 +104,27 @@ def read_device_error(device: torch.device | None = None) -> int:
     if status not in (_abi.WFD_OK,):
         raise _abi.WfdError("device error word", status, f"{_abi.status_string(status)}; bits=0x{h.value:x}")
     return h.value
+
+
+def set_batch_invariant(on: bool) -> bool:
+    """Turn the library's batch-invariant attention on or off; returns the old mode."""
+    lib = _abi.load()
+    old = bool(lib.wfd_get_batch_invariant())
+    _abi.check(lib.wfd_set_batch_invariant(1 if on else 0), "wfd_set_batch_invariant")
+    return old
+
+
+class batch_invariant:
+    """Context manager: batch-invariant attention inside the block."""
+
+    def __init__(self, on: bool = True):
+        self.on = on
+        self.old = False
+
+    def __enter__(self):
+        self.old = set_batch_invariant(self.on)
+        return self
+
+    def __exit__(self, *exc):
+        set_batch_invariant(self.old)
+
