@@ -119,6 +119,9 @@ def parse():
                          "cfg5: Bernoulli draft acceptance (default 0.8)")
     ap.add_argument("--scheduler", choices=["device", "host"], default="device",
                     help="cfg4: route / settle on the GPU (one graph per tick) or on the host")
+    ap.add_argument("--batch-invariant", action="store_true",
+                    help="cfg4 (device scheduler): fixed union capacities + batch-invariant attention "
+                         "(bit-exact greedy equality with sequential decoding)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", type=int, default=-1, choices=[-1, 0, 1],
@@ -610,7 +613,7 @@ def run_cfg4(args):
     model = LoopedLM(cfg, seed=CFG4["model_seed"], dtype=torch.bfloat16, device=dev)
     eng = WaveEngine(model, Bl, L + new + 2 * cfg.T_total + 8)
     policy = sch.SsdPolicy(cfg.T_total, args.t_draft)
-    dwave = DeviceWave(eng, new, policy) if args.scheduler == "device" else None
+    dwave = DeviceWave(eng, new, policy, args.batch_invariant) if args.scheduler == "device" else None
 
     ev_all0, ev_dec0, ev_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
 
@@ -691,7 +694,7 @@ def run_cfg4(args):
                             f"prelude {cfg.n_prelude} / core {cfg.n_core} x R={cfg.T_total} / coda {cfg.n_coda}",
                    "global_batch": Bg, "batch_per_gpu": Bl if Bg % world == 0 else f"{Bg // world}-{-(-Bg // world)}",
                    "prompt_len": L, "new_tokens": new,
-                   "T_draft": args.t_draft, "scheduler": args.scheduler,
+                   "T_draft": args.t_draft, "scheduler": args.scheduler, "batch_invariant": args.batch_invariant,
                    "acceptance": "greedy gold == draft" if args.alpha is None else f"emulated Bernoulli({args.alpha})",
                    "parallelism": f"sequences sharded, {world} rank(s), no collective on the hot path",
                    "timing": "decode region per generation, CUDA events, max over ranks; "
