@@ -128,3 +128,17 @@ def test_items_from_table_and_argmax(cuda_dev):
         fused.argmax_rows(x, out)
         assert torch.equal(out.long(), x.float().argmax(dim=-1))
         assert int(out[3]) == 100
+    # vector path (V % 8 == 0, aligned), scalar path (odd V, or a row base off
+    # the 16-byte boundary), ties inside one 8-element vector and across the
+    # unrolled loads, and the maximum at the last element
+    for dt in (torch.float32, torch.bfloat16):
+        for V in (8, 7, 4104, 40000, 50303):
+            base = torch.randn(5 * V + 1, generator=g).to(dt).to(cuda_dev)
+            for x in (base[:5 * V].view(5, V), base[1:].view(5, V)):
+                x[0, V - 1] = x[0].max() + 1
+                m = x[1].max() + 1
+                x[1, min(3, V - 1)] = x[1, min(5, V - 1)] = x[1, V // 2] = m
+                x[2, V // 3] = x[2, V - 1] = x[2].max() + 1
+                out = torch.empty(5, dtype=torch.int32, device=cuda_dev)
+                fused.argmax_rows(x, out)
+                assert torch.equal(out.long(), x.float().argmax(dim=-1)), (dt, V, x.data_ptr() % 16)

@@ -884,10 +884,11 @@ extern "C" int wfd_argmax_rows(const void* x, int32_t* out, int32_t n, int32_t V
   if (n == 0) return WFD_OK;
   if (!x || !out) return WFD_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vec = (V % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
   if (dtype == WFD_DTYPE_BF16)
-    argmax_rows_kernel<__nv_bfloat16><<<n, kModelThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), out, V);
+    argmax_rows_kernel<__nv_bfloat16><<<n, kArgmaxThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), out, V, vec);
   else if (dtype == WFD_DTYPE_F32)
-    argmax_rows_kernel<float><<<n, kModelThreads, 0, st>>>(static_cast<const float*>(x), out, V);
+    argmax_rows_kernel<float><<<n, kArgmaxThreads, 0, st>>>(static_cast<const float*>(x), out, V, vec);
   else
     return WFD_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;

@@ -227,19 +227,47 @@ __global__ void items_from_table_kernel(const int32_t* __restrict__ tab, int col
 }
 
 // out[r] = argmax over the V logits of row r (the first index of the maximum,
-// as torch.argmax), one CTA per row
+// as torch.argmax), one CTA of kArgmaxThreads per row.  A row of the lm_head
+// output is ~100 KB and the launch has only a few rows, so each CTA keeps
+// several 16-byte loads in flight per thread (`vec` != 0: V % 8 == 0 and x
+// 16-byte aligned) instead of one scalar load at a time.  The comparison is a
+// total order on (value, -index), so the result does not depend on which
+// thread sees which element.
+constexpr int kArgmaxThreads = 512;
+
 template <typename T>
-__global__ void __launch_bounds__(kModelThreads) argmax_rows_kernel(const T* __restrict__ x, int32_t* __restrict__ out,
-                                                                     int V) {
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const T* __restrict__ x, int32_t* __restrict__ out,
+                                                                      int V, int vec) {
   const T* row = x + (long long)blockIdx.x * V;
   float best = -__int_as_float(0x7f800000);
   int bi = 0x7fffffff;
-  for (int j = threadIdx.x; j < V; j += blockDim.x) {
-    const float v = to_f(row[j]);
+  auto take = [&](float v, int j) {
     if (v > best || (v == best && j < bi)) {
       best = v;
       bi = j;
     }
+  };
+  if (vec) {
+    constexpr int U = 4;  // 16-byte loads in flight per thread
+    const int nv = V >> 3;
+    int c = threadIdx.x;
+    for (; c + (U - 1) * kArgmaxThreads < nv; c += U * kArgmaxThreads) {
+      float a[U][8];
+#pragma unroll
+      for (int u = 0; u < U; ++u) Vec8<T>::load(row + 8 * (c + u * kArgmaxThreads), a[u]);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) take(a[u][i], 8 * (c + u * kArgmaxThreads) + i);
+    }
+    for (; c < nv; c += kArgmaxThreads) {
+      float a[8];
+      Vec8<T>::load(row + 8 * c, a);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) take(a[i], 8 * c + i);
+    }
+  } else {
+    for (int j = threadIdx.x; j < V; j += kArgmaxThreads) take(to_f(row[j]), j);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -250,8 +278,8 @@ __global__ void __launch_bounds__(kModelThreads) argmax_rows_kernel(const T* __r
       bi = oi;
     }
   }
-  __shared__ float sb[kModelThreads / 32];
-  __shared__ int si[kModelThreads / 32];
+  __shared__ float sb[kArgmaxThreads / 32];
+  __shared__ int si[kArgmaxThreads / 32];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) {
     sb[w] = best;
@@ -259,7 +287,7 @@ __global__ void __launch_bounds__(kModelThreads) argmax_rows_kernel(const T* __r
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int k = 1; k < kModelThreads / 32; ++k)
+    for (int k = 1; k < kArgmaxThreads / 32; ++k)
       if (sb[k] > best || (sb[k] == best && si[k] < bi)) {
         best = sb[k];
         bi = si[k];

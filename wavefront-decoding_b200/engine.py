@@ -189,24 +189,28 @@ class WaveEngine:
 
     # ------------------------------------------------------------------
     # device-side bodies (captured into graphs)
-    def _segment_block(self, blk, x, t: _Tables, j: int, slot: int):
-        """Prelude / coda layer: append every row, then attend with segments."""
+    def _segment_block(self, blk, x, t: _Tables, j: int, slot: int, cols: torch.Tensor, k_len: torch.Tensor):
+        """Prelude / coda layer: append every row, then attend with segments.
+        cols: the table transposed (n_cols, cap), so each column is contiguous;
+        k_len = position + 1."""
         m = self.model
-        tab = t.dev
-        q, k, v = m.qkv(blk, x, pos=tab[:, 1])
-        self.cache.write_tokens(t.const(slot), tab[:, 3], tab[:, 1], k, v)
-        o = wa.attn_segments(q, self.Kflat, self.Vflat, t.row_ids, tab[:, 5], tab[:, 6 + j], tab[:, 1] + 1, 1,
-                             causal=False)
+        q, k, v = m.qkv(blk, x, pos=t.dev[:, 1])
+        self.cache.write_tokens(t.const(slot), cols[3], cols[1], k, v)
+        o = wa.attn_segments(q, self.Kflat, self.Vflat, t.row_ids, cols[5], cols[6 + j], k_len, 1, causal=False)
         return m.finish_block(blk, x, o)
 
     def _body(self, kind: str, t: _Tables) -> None:
         m, cfg = self.model, self.cfg
         tab = t.dev
         rows = tab[:, 0]
+        if kind != "R":
+            # one transpose (and one add) per body instead of a copy per strided column per layer
+            cols = tab.t().contiguous()
+            k_len = cols[1] + 1
         if kind == "P":
             x = fused.gather_rows(m.embed, tab[:, 2])
             for j, blk in enumerate(m.prelude):
-                x = self._segment_block(blk, x, t, j, cfg.slot_prelude(j))
+                x = self._segment_block(blk, x, t, j, cfg.slot_prelude(j), cols, k_len)
             fused.scatter_rows(x, rows, self.pool_e, zero=self.pool_h)
         elif kind == "R":
             x = fused.gather_rows(self.pool_h, rows, b=self.pool_e)
@@ -220,7 +224,7 @@ class WaveEngine:
         else:
             x = fused.gather_rows(self.pool_h, rows)
             for j, blk in enumerate(m.coda):
-                x = self._segment_block(blk, x, t, j, cfg.slot_coda(j))
+                x = self._segment_block(blk, x, t, j, cfg.slot_coda(j), cols, k_len)
             m.greedy_ids(x, t.out)
 
     def _run(self, kind: str, t: _Tables) -> None:

@@ -153,12 +153,15 @@ class LoopedLM:
                 v.view(*lead, cfg.n_kv_heads, cfg.head_dim))
 
     def finish_block(self, blk: Block, x: torch.Tensor, attn: torch.Tensor) -> torch.Tensor:
-        """x + o_proj(attn), then x + SwiGLU(norm(x)); residual adds ride on the GEMMs."""
+        """x + o_proj(attn), then x + SwiGLU(norm(x)); the residual adds ride on the
+        GEMMs (beta = 1), which update the residual stream x IN PLACE (x must be
+        contiguous and owned by the caller) and return it."""
         cfg = self.cfg
         shp = x.shape
-        x2 = torch.addmm(x.reshape(-1, cfg.d_model), attn.reshape(-1, cfg.n_heads * cfg.head_dim), blk.wo)
+        x2 = x.view(-1, cfg.d_model)
+        x2.addmm_(attn.reshape(-1, cfg.n_heads * cfg.head_dim), blk.wo)
         a = fused.silu_mul(self.rmsnorm(x2, blk.norm2) @ blk.wgu)
-        return torch.addmm(x2, a, blk.wd).view(shp)
+        return x2.addmm_(a, blk.wd).view(shp)
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         return (self.rmsnorm(x.contiguous(), self.final_norm) @ self.lm_head).float()
