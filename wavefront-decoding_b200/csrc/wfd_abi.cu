@@ -70,7 +70,7 @@ inline int nq_cap(int dtype, int dh) { return dtype == WFD_DTYPE_BF16 ? 8 : 16; 
 // zero between launches, so every call has to find them at the same place
 // whatever its item count or head_dim.
 struct WsLayout {
-  size_t cnt, part, segs, prefix, seg0, total;
+  size_t cnt, part, segs, prefix, start, total;
 };
 
 constexpr size_t ws_part_floats(bool tc_only, int head_dim, size_t sms) {
@@ -89,8 +89,8 @@ WsLayout ws_layout(int max_items, int head_dim, int sms, bool tc_only = false) {
   w.part = align256(w.cnt + n_ctas * sizeof(int));
   w.segs = align256(w.part + ws_part_floats(tc_only, head_dim, (size_t)sms) * sizeof(float));
   w.prefix = align256(w.segs + (size_t)max_items * sizeof(Seg));
-  w.seg0 = align256(w.prefix + (size_t)(max_items + 1) * sizeof(long long));
-  w.total = align256(w.seg0 + (size_t)sms * sizeof(int));
+  w.start = align256(w.prefix + (size_t)(max_items + 1) * sizeof(long long));
+  w.total = align256(w.start + (size_t)sms * sizeof(CtaStart));
   return w;
 }
 
@@ -328,7 +328,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   pp.segs = reinterpret_cast<Seg*>(ws + L.segs);
   pp.prefix = reinterpret_cast<long long*>(ws + L.prefix);
   if (which == 1) {  // the tcgen05 grid: one CTA per SM over (pair) kv-head units
-    pp.seg0 = reinterpret_cast<int*>(ws + L.seg0);
+    pp.start = reinterpret_cast<CtaStart*>(ws + L.start);
     pp.seg_grid = sms;
     pp.seg_units = pair ? A.Hkv / 2 : A.Hkv;
   }
@@ -360,7 +360,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     vp.out = A.out;
     vp.segs = pp.segs;
     vp.prefix = pp.prefix;
-    vp.seg0 = pp.seg0;
+    vp.start = pp.start;
     vp.n_segs = A.n;
     vp.Hq = A.Hq;
     vp.Hkv = pair ? A.Hkv / 2 : A.Hkv;
@@ -476,7 +476,7 @@ constexpr size_t static_ws_bytes() {
                                              ws_part_floats(true, 128, kStaticMaxSms) * sizeof(float)) +
                                     (size_t)kStaticMaxItems * sizeof(Seg)) +
                            (size_t)(kStaticMaxItems + 1) * sizeof(long long)) +
-                  (size_t)kStaticMaxSms * sizeof(int));
+                  (size_t)kStaticMaxSms * sizeof(CtaStart));
 }
 constexpr size_t kStaticWsBytes = static_ws_bytes();
 

@@ -29,6 +29,18 @@ struct Seg {
 };
 static_assert(sizeof(Seg) == 32, "Seg must stay 32 bytes");
 
+// Where one CTA of the persistent tensor-core grid starts (written by the plan
+// kernel): its first segment, that segment's first work index and the next
+// segment's (in unit-keys), and the segment itself.  One 64-byte load replaces
+// the dependent prefix / segment loads a CTA would otherwise make at start.
+struct CtaStart {
+  Seg S;
+  long long base, nbase;  // nbase: LLONG_MAX for the last segment
+  int seg;
+  int pad[3];
+};
+static_assert(sizeof(CtaStart) == 64, "CtaStart must stay 64 bytes");
+
 // Error bits written into the caller's device error word (atomicOr).  The host
 // turns them into WFD_ERR_* status codes; no kernel ever traps.
 enum : int {

@@ -36,9 +36,10 @@ struct PlanParams {
   // outputs
   Seg* segs;
   long long* prefix;  // n + 1 entries, per-kv-head work units
-  // optional: the first segment of each CTA of a persistent grid of seg_grid
-  // CTAs that splits seg_units * prefix[n] into equal shares (tcgen05 kernel)
-  int* seg0;
+  // optional: the start record (first segment and its bounds) of each CTA of a
+  // persistent grid of seg_grid CTAs that splits seg_units * prefix[n] into
+  // equal shares (tcgen05 kernel)
+  CtaStart* start;
   int seg_grid, seg_units;
   // zero-fill of query rows that see no keys (k_len == 0)
   void* out;
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) 
     __syncthreads();
   }
   if (threadIdx.x == 0) p.prefix[p.n] = carry;
-  if (p.seg0 != nullptr) {
+  if (p.start != nullptr) {
     __syncthreads();  // the prefix above is complete and visible to the block
     const long long total = (long long)p.seg_units * carry;
     const long long share = total > 0 ? (total + p.seg_grid - 1) / p.seg_grid : 1;
@@ -177,7 +178,13 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) 
           else hi = mid - 1;
         }
       }
-      p.seg0[c] = lo;
+      CtaStart cs;
+      cs.S = p.segs[lo];
+      cs.base = (long long)p.seg_units * p.prefix[lo];
+      cs.nbase = lo + 1 <= p.n - 1 ? (long long)p.seg_units * p.prefix[lo + 1] : 0x7fffffffffffffffll;
+      cs.seg = lo;
+      cs.pad[0] = cs.pad[1] = cs.pad[2] = 0;
+      p.start[c] = cs;
     }
   }
 }

@@ -17,7 +17,9 @@
 //
 // Warp roles (one CTA per SM; 192 threads, 320 for 32 query columns):
 //   warp 0      TMA producer: K and V tiles (2 boxes of 64 dims each, 128B
-//               swizzle) into a STAGES-deep ring, mbarrier complete_tx
+//               swizzle) into a STAGES-deep ring, mbarrier complete_tx; and
+//               each unit's Q^T operand into one of two buffers ahead of the
+//               MMA warp (a unit boundary then waits on no global load)
 //   warp 1      TMEM allocator + tcgen05.mma issuer (one lane issues)
 //   warps 2..   softmax / correction, 4 warps per slice of 16 query columns
 //               (warp w reads TMEM lane quadrant w % 4): S^T from TMEM, column
@@ -58,7 +60,7 @@ struct VerifyParams {
   void* out;
   const Seg* segs;
   const long long* prefix;
-  const int* seg0;  // first segment of each CTA, from the plan kernel (null: search it here)
+  const CtaStart* start;  // start record of each CTA, from the plan kernel (null: search here)
   int n_segs;
   int Hq, Hkv, G;
   float scale_log2;
@@ -77,11 +79,11 @@ struct VerifyParams {
 template <int NQP, int DH>
 struct TcCfg {
   static constexpr int KB = DH / 64;                       // 64-dim boxes per K (and per V) tile
-  static constexpr int STAGES = DH == 128 ? 3 : 6;
+  static constexpr int STAGES = DH == 128 ? 3 : (NQP == 32 ? 5 : 6);
   static constexpr int BOX_BYTES = kTcTile * 128;          // 128 rows x 64 bf16
   static constexpr int KV_STAGE = 2 * KB * BOX_BYTES;      // K boxes, then V boxes
   static constexpr int GUARD = DH == 128 ? 0 : BOX_BYTES;  // read by the M = 128 P.V MMA of the last stage
-  static constexpr int Q_BYTES = NQP * DH * 2;             // KB boxes of NQP rows x 128 B
+  static constexpr int Q_BYTES = NQP * DH * 2;             // KB boxes of NQP rows x 128 B (one of two buffers)
   static constexpr int P_ROWB = NQP * 2;                   // one key row of P^T
   static constexpr int P_BYTES = kTcTile * P_ROWB;
   static constexpr int P_SWZ_BITS = NQP == 16 ? 1 : 2;     // Swizzle<1,4,3> (32B) / <2,4,3> (64B)
@@ -89,7 +91,7 @@ struct TcCfg {
   static constexpr int P_ATOM = 8 * P_ROWB;                // 8 key rows
   static constexpr int RED_FLOATS = 2 * 4 * NQP;           // double-buffered per-warp column values
   static constexpr int SMEM =
-      STAGES * KV_STAGE + GUARD + Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + (2 * NQP + 4) * 4 + 1024;
+      STAGES * KV_STAGE + GUARD + 2 * Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + (2 * NQP + 4) * 4 + 1024;
   static constexpr int TMEM_COLS = NQP == 16 ? 64 : 128;   // S (x2) and O accumulators
   static constexpr int PART_FLOATS = NQP * (DH + 2);
   static_assert(NQP == 16 || NQP == 32, "N of the swap-AB MMA");
@@ -247,20 +249,39 @@ __device__ __forceinline__ int reduced_col(int lane) {
 }
 
 // The (segment, unit, key range) pieces of one CTA's share, in order; every
-// role walks the same sequence.
+// role walks the same sequence.  The current segment (its Seg, its first and
+// the next segment's first work index) stays in registers, so moving to the
+// next unit of the same segment reads no global memory.
 struct UnitIter {
   long long pos, b;
   int seg;
-  __device__ __forceinline__ bool next(const VerifyParams& p, Seg& S, int& u, int& r_lo, int& r_hi,
+  bool have = false;
+  Seg S{};
+  long long base = 0, nbase = 0;
+  __device__ __forceinline__ long long seg_base(const VerifyParams& p, int i) const {
+    return i <= p.n_segs - 1 ? (long long)p.Hkv * p.prefix[i] : 0x7fffffffffffffffll;
+  }
+  __device__ __forceinline__ bool next(const VerifyParams& p, Seg& Sout, int& u, int& r_lo, int& r_hi,
                                        long long& unit_start) {
     for (;;) {
       if (pos >= b) return false;
-      while (seg + 1 <= p.n_segs - 1 && (long long)p.Hkv * p.prefix[seg + 1] <= pos) ++seg;
-      S = p.segs[seg];
-      const long long seg_base = (long long)p.Hkv * p.prefix[seg];
-      const long long o = pos - seg_base;
+      if (!have || pos >= nbase) {
+        if (!have) {
+          base = seg_base(p, seg);
+          nbase = seg_base(p, seg + 1);
+        }
+        while (pos >= nbase) {  // largest seg with Hkv * prefix[seg] <= pos
+          ++seg;
+          base = nbase;
+          nbase = seg_base(p, seg + 1);
+        }
+        S = p.segs[seg];
+        have = true;
+      }
+      Sout = S;
+      const long long o = pos - base;
       u = (int)(o / S.k_len);
-      unit_start = seg_base + (long long)u * S.k_len;
+      unit_start = base + (long long)u * S.k_len;
       const long long unit_end = unit_start + S.k_len;
       if (p.invariant) {
         if (unit_start < pos) {  // began in the previous CTA's share: that CTA processes it
@@ -304,8 +325,8 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* kvs = smem;                               // STAGES x (K0 K1 V0 V1)
-  unsigned char* qs = kvs + STAGES * C::KV_STAGE + C::GUARD;  // Q^T operand (K-major, SW128)
-  unsigned char* ps = qs + C::Q_BYTES;                     // P^T operand (MN-major)
+  unsigned char* qs = kvs + STAGES * C::KV_STAGE + C::GUARD;  // 2 x Q^T operand (K-major, SW128)
+  unsigned char* ps = qs + 2 * C::Q_BYTES;                 // P^T operand (MN-major)
   float* red = reinterpret_cast<float*>(ps + C::P_BYTES);  // [2][4][NQP] column maxima
   float* lred = red + C::RED_FLOATS;                       // [2][4][NQP] column sums
   float* mst = lred + C::RED_FLOATS;                       // [NQP] running column max (log2-scaled)
@@ -319,7 +340,8 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   __shared__ __align__(8) uint64_t bar_pfull;
   __shared__ __align__(8) uint64_t bar_ofull;
   __shared__ __align__(8) uint64_t bar_ofree;
-  __shared__ __align__(8) uint64_t bar_qready;
+  __shared__ __align__(8) uint64_t bar_qready[2];  // unit's Q^T written (producer)
+  __shared__ __align__(8) uint64_t bar_qfree[2];   // unit's S MMAs done with its Q^T (MMA commit)
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
   __shared__ int s_flag;
@@ -338,7 +360,10 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
     mbar_init(&bar_pfull, 1);
     mbar_init(&bar_ofull, 1);
     mbar_init(&bar_ofree, 4 * H2);
-    mbar_init(&bar_qready, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar_qready[s], 1);
+      mbar_init(&bar_qfree[s], 1);
+    }
     fence_mbar_init();
     s_abort = 0;
   }
@@ -354,6 +379,10 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
+  // independent loads in flight together: this CTA's start record (from the
+  // plan kernel) and the total work
+  CtaStart cs{};
+  if (p.start != nullptr) cs = p.start[blockIdx.x];
   const long long total = (long long)p.Hkv * p.prefix[p.n_segs];
   long long share = 1, a = 0, b = 0;
   if (total > 0) {
@@ -366,8 +395,8 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   // threads probe 192 pivots of [lo, hi] at once, so up to 192 segments take
   // one round of loads instead of a chain of dependent ones.
   int seg0 = 0;
-  if (a < b && p.seg0 != nullptr) {
-    seg0 = p.seg0[blockIdx.x];
+  if (a < b && p.start != nullptr) {
+    seg0 = cs.seg;
   } else if (a < b) {
     int lo = 0, hi = p.n_segs - 1;
     while (lo < hi) {
@@ -390,18 +419,31 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
     }
     seg0 = lo;
   }
+  // every role walks the same units; with a start record the first segment is
+  // already in registers
+  auto make_iter = [&]() {
+    UnitIter r{a, b, seg0};
+    if (a < b && p.start != nullptr) {
+      r.have = true;
+      r.S = cs.S;
+      r.base = cs.base;
+      r.nbase = cs.nbase;
+    }
+    return r;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    UnitIter itr{a, b, seg0};
+    UnitIter itr = make_iter();
     Seg S;
     int u, r_lo, r_hi;
     long long ustart;
-    uint32_t it = 0;
+    uint32_t it = 0, units = 0;
     while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
-      const int h = u % p.Hkv;
+      const int h = u % p.Hkv, qg = u / p.Hkv;
       const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
       const long long row0 = S.k_row0 + p.k_row_offset + r_lo;
+
       for (int t = 0; t < n_t; ++t, ++it) {
         const int stage = (int)(it % STAGES);
         const bool go = (it >= (uint32_t)STAGES) ? tc_wait(&bar_empty[stage], ((it / STAGES) - 1) & 1u, &s_abort, p.err)
@@ -419,16 +461,60 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
           }
         }
         __syncwarp();
+        if (t == 0) {
+          // ---- once the unit's first K / V tile is on its way: its Q^T operand
+          // into buffer units & 1, after the S MMAs of unit units - 2 are done
+          // with it.  Row n = query vector qg*NQP + n (pair: n < nvh head 2h,
+          // else 2h + 1); rows past the unit's vectors are zero.  This warp runs
+          // ahead of the MMA warp, so the load is off its path.
+          {
+            const int qb = (int)(units & 1u);
+            const bool qgo =
+                units >= 2 ? tc_wait(&bar_qfree[qb], ((units >> 1) - 1) & 1u, &s_abort, p.err) : !s_abort;
+            if (qgo) {
+              const int nvh = S.q_len * p.G;
+              const int nvec = (p.pair ? 2 * nvh : nvh) - qg * NQP;
+              unsigned char* qd = qs + qb * C::Q_BYTES;
+              for (int c = lane; c < NQP * (DH / 8); c += 32) {
+                const int n = c / (DH / 8), ch = c % (DH / 8);
+                uint4 val = make_uint4(0, 0, 0, 0);
+                if (n < nvec) {
+                  if (p.pair) {
+                    const int e = n >= nvh ? 1 : 0, v = n - e * nvh;
+                    const int row = v / p.G, g = v % p.G;
+                    if ((ch >> 3) == e)
+                      val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
+                                     ((long long)(S.q_row0 + row) * p.Hq + (2 * h + e) * p.G + g) * 64 + (ch & 7) * 8);
+                  } else {
+                    const int v = qg * NQP + n;
+                    const int row = v / p.G, g = v % p.G;
+                    val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
+                                   ((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + ch * 8);
+                  }
+                }
+                const int box = ch >> 3, cc = ch & 7;
+                const uint32_t off = (uint32_t)(box * NQP * 128 + n * 128 + ((cc ^ (n & 7)) << 4));
+                *reinterpret_cast<uint4*>(qd + off) = val;
+              }
+              fence_async_smem();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_qready[qb]);
+            ++units;
+          }
+        }
       }
     }
     // the MMA warp's last commits arrive on these barriers: see them land
     // before this CTA may exit
+    for (uint32_t k = (units > 2 ? units - 2 : 0); k < units; ++k)
+      tc_wait(&bar_qfree[k & 1u], (k >> 1) & 1u, &s_abort, p.err);
     const uint32_t n_used = it;
     for (uint32_t j = (n_used > (uint32_t)STAGES ? n_used - STAGES : 0); j < n_used; ++j)
       tc_wait(&bar_empty[j % STAGES], (j / STAGES) & 1u, &s_abort, p.err);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    UnitIter itr{a, b, seg0};
+    UnitIter itr = make_iter();
     Seg S;
     int u, r_lo, r_hi;
     long long ustart;
@@ -439,7 +525,9 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
     const uint32_t p_addr = smem_u32(ps);
     while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
       const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
-      tc_wait(&bar_qready, units & 1u, &s_abort, p.err);
+      const int qb = (int)(units & 1u);
+      const uint32_t qa = q_addr + (uint32_t)(qb * C::Q_BYTES);
+      tc_wait(&bar_qready[qb], (units >> 1) & 1u, &s_abort, p.err);
       tc_fence_after();
       for (int t = 0; t <= n_t; ++t) {
         if (t < n_t) {
@@ -457,9 +545,10 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
               const uint32_t koff = (uint32_t)((j >> 2) * C::BOX_BYTES + (j & 3) * 32);
               const uint32_t qoff = (uint32_t)((j >> 2) * (NQP * 128) + (j & 3) * 32);
               umma_f16(tmem + (uint32_t)(sb * NQP), umma_desc(k_addr + koff, 16, 1024, 2),
-                       umma_desc(q_addr + qoff, 16, 1024, 2), IDESC_S, j > 0 ? 1u : 0u);
+                       umma_desc(qa + qoff, 16, 1024, 2), IDESC_S, j > 0 ? 1u : 0u);
             }
             umma_commit(&bar_sfull[sb]);
+            if (t == n_t - 1) umma_commit(&bar_qfree[qb]);  // the unit's Q^T buffer may be rewritten
           }
           __syncwarp();
         }
@@ -499,7 +588,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
     const int stid = tid - 64;          // 0 .. SMT - 1 within the softmax group
     const int my_row = qd * 32 + lane;  // key row of S^T, then head dim of O^T, this thread owns
     const uint32_t tq = tmem + ((uint32_t)(qd * 32) << 16);
-    UnitIter itr{a, b, seg0};
+    UnitIter itr = make_iter();
     Seg S;
     int u, r_lo, r_hi;
     long long ustart;
@@ -512,31 +601,6 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
       const int nvh = S.q_len * p.G;                                   // query vectors per kv head
       const int nvec = (p.pair ? 2 * nvh : nvh) - qg * NQP;  // of this unit / group (may exceed NQP)
-      // ---- Q^T operand: row n = query vector qg*NQP + n (pair: n < nvh head 2h, else 2h + 1)
-      for (int c = stid; c < NQP * (DH / 8); c += SMT) {
-        const int n = c / (DH / 8), ch = c % (DH / 8);
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (n < nvec) {
-          if (p.pair) {
-            const int e = n >= nvh ? 1 : 0, v = n - e * nvh;
-            const int row = v / p.G, g = v % p.G;
-            if ((ch >> 3) == e)
-              val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
-                             ((long long)(S.q_row0 + row) * p.Hq + (2 * h + e) * p.G + g) * 64 + (ch & 7) * 8);
-          } else {
-            const int v = qg * NQP + n;
-            const int row = v / p.G, g = v % p.G;
-            val = ld_nc_v4(static_cast<const __nv_bfloat16*>(p.q) +
-                           ((long long)(S.q_row0 + row) * p.Hq + h * p.G + g) * DH + ch * 8);
-          }
-        }
-        const int box = ch >> 3, cc = ch & 7;
-        const uint32_t off = (uint32_t)(box * NQP * 128 + n * 128 + ((cc ^ (n & 7)) << 4));
-        *reinterpret_cast<uint4*>(qs + off) = val;
-      }
-      fence_async_smem();
-      softmax_bar<SMT>();
-      if (stid == 0) mbar_arrive(&bar_qready);
 
       // running column maxima live in shared memory (mst, log2-scaled), owned
       // by lanes 0..NL-1 of the first warp of each column slice
