@@ -337,7 +337,8 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   pp.Dh = A.Dh;
   pp.elem_bytes = elem_bytes(A.dtype);
   pp.err = A.err;
-  plan_kernel<<<1, kPlanThreads, 0, st>>>(pp);
+  if (launch_pdl(plan_kernel, dim3(1), dim3(kPlanThreads), 0, st, pp) != cudaSuccess)
+    return WFD_ERR_CUDA;
   if (cudaGetLastError() != cudaSuccess) return WFD_ERR_CUDA;
 
   const float scale = A.scale > 0.f ? A.scale : 1.0f / std::sqrt((float)A.Dh);
@@ -680,10 +681,11 @@ int wfd_append(const void* k_new, const void* v_new, void* k_cache, void* v_cach
   if (!aligned16(k_new) || !aligned16(v_new) || !aligned16(k_cache) || !aligned16(v_cache)) return WFD_ERR_ALIGNMENT;
   const int threads = 256;
   const int blocks = (int)(((long long)n * 32 + threads - 1) / threads);
-  append_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const char*>(k_new), static_cast<const char*>(v_new), static_cast<char*>(k_cache),
-      static_cast<char*>(v_cache), lens, slots, seqs, positions, n, slot_offset,
-      geom(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype), d_err);
+  if (launch_pdl(append_kernel, dim3(blocks), dim3(threads), 0, static_cast<cudaStream_t>(stream),
+                 static_cast<const char*>(k_new), static_cast<const char*>(v_new), static_cast<char*>(k_cache),
+                 static_cast<char*>(v_cache), lens, slots, seqs, positions, n, slot_offset,
+                 geom(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype), d_err) != cudaSuccess)
+    return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
@@ -767,14 +769,16 @@ extern "C" int wfd_rmsnorm(const void* x, const void* w, void* y, int32_t n, int
   if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return WFD_ERR_ALIGNMENT;
   const int grid = (n + kModelThreads / 32 - 1) / (kModelThreads / 32);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == WFD_DTYPE_BF16)
-    rmsnorm_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
-                                                                   static_cast<const __nv_bfloat16*>(w),
-                                                                   static_cast<__nv_bfloat16*>(y), n, d, eps);
-  else if (dtype == WFD_DTYPE_F32)
-    rmsnorm_kernel<float><<<grid, kModelThreads, 0, st>>>(static_cast<const float*>(x), static_cast<const float*>(w),
-                                                         static_cast<float*>(y), n, d, eps);
-  else
+  if (dtype == WFD_DTYPE_BF16) {
+    if (launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(grid), dim3(kModelThreads), 0, st,
+                   static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+                   static_cast<__nv_bfloat16*>(y), n, d, eps) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else if (dtype == WFD_DTYPE_F32) {
+    if (launch_pdl(rmsnorm_kernel<float>, dim3(grid), dim3(kModelThreads), 0, st, static_cast<const float*>(x),
+                   static_cast<const float*>(w), static_cast<float*>(y), n, d, eps) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else
     return WFD_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
@@ -792,16 +796,18 @@ extern "C" int wfd_rope_split(const void* qkv, const float* cos_tab, const float
   const long long work = (long long)n * (n_heads + 2 * n_kv_heads) * (head_dim / 2);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = model_grid(work);
-  if (dtype == WFD_DTYPE_BF16)
-    rope_split_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(qkv), cos_tab, sin_tab, pos, pos_stride, pos_period,
-        static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v), n, n_heads,
-        n_kv_heads, head_dim, style, max_pos, d_err);
-  else if (dtype == WFD_DTYPE_F32)
-    rope_split_kernel<float><<<grid, kModelThreads, 0, st>>>(
-        static_cast<const float*>(qkv), cos_tab, sin_tab, pos, pos_stride, pos_period, static_cast<float*>(q),
-        static_cast<float*>(k), static_cast<float*>(v), n, n_heads, n_kv_heads, head_dim, style, max_pos, d_err);
-  else
+  if (dtype == WFD_DTYPE_BF16) {
+    if (launch_pdl(rope_split_kernel<__nv_bfloat16>, dim3(grid), dim3(kModelThreads), 0, st,
+                   static_cast<const __nv_bfloat16*>(qkv), cos_tab, sin_tab, pos, pos_stride, pos_period,
+                   static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(v),
+                   n, n_heads, n_kv_heads, head_dim, style, max_pos, d_err) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else if (dtype == WFD_DTYPE_F32) {
+    if (launch_pdl(rope_split_kernel<float>, dim3(grid), dim3(kModelThreads), 0, st, static_cast<const float*>(qkv),
+                   cos_tab, sin_tab, pos, pos_stride, pos_period, static_cast<float*>(q), static_cast<float*>(k),
+                   static_cast<float*>(v), n, n_heads, n_kv_heads, head_dim, style, max_pos, d_err) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else
     return WFD_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
@@ -813,13 +819,15 @@ extern "C" int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, i
   if (!aligned16(gu) || !aligned16(out)) return WFD_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = model_grid((long long)n * (dff / 8));
-  if (dtype == WFD_DTYPE_BF16)
-    silu_mul_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(gu),
-                                                                    static_cast<__nv_bfloat16*>(out), n, dff);
-  else if (dtype == WFD_DTYPE_F32)
-    silu_mul_kernel<float><<<grid, kModelThreads, 0, st>>>(static_cast<const float*>(gu), static_cast<float*>(out),
-                                                          n, dff);
-  else
+  if (dtype == WFD_DTYPE_BF16) {
+    if (launch_pdl(silu_mul_kernel<__nv_bfloat16>, dim3(grid), dim3(kModelThreads), 0, st,
+                   static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(out), n, dff) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else if (dtype == WFD_DTYPE_F32) {
+    if (launch_pdl(silu_mul_kernel<float>, dim3(grid), dim3(kModelThreads), 0, st, static_cast<const float*>(gu),
+                   static_cast<float*>(out), n, dff) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else
     return WFD_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
@@ -832,15 +840,17 @@ extern "C" int wfd_gather_rows(const void* a, const void* b, const int32_t* idx,
   if (!aligned16(a) || (b && !aligned16(b)) || !aligned16(out)) return WFD_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = model_grid((long long)n * (d / 8));
-  if (dtype == WFD_DTYPE_BF16)
-    gather_rows_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b), idx, idx_stride,
-        static_cast<__nv_bfloat16*>(out), n, d, n_src, d_err);
-  else if (dtype == WFD_DTYPE_F32)
-    gather_rows_kernel<float><<<grid, kModelThreads, 0, st>>>(static_cast<const float*>(a),
-                                                             static_cast<const float*>(b), idx, idx_stride,
-                                                             static_cast<float*>(out), n, d, n_src, d_err);
-  else
+  if (dtype == WFD_DTYPE_BF16) {
+    if (launch_pdl(gather_rows_kernel<__nv_bfloat16>, dim3(grid), dim3(kModelThreads), 0, st,
+                   static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b), idx, idx_stride,
+                   static_cast<__nv_bfloat16*>(out), n, d, n_src, d_err) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else if (dtype == WFD_DTYPE_F32) {
+    if (launch_pdl(gather_rows_kernel<float>, dim3(grid), dim3(kModelThreads), 0, st, static_cast<const float*>(a),
+                   static_cast<const float*>(b), idx, idx_stride, static_cast<float*>(out), n, d, n_src,
+                   d_err) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else
     return WFD_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
@@ -853,15 +863,17 @@ extern "C" int wfd_scatter_rows(const void* src, const int32_t* idx, int32_t idx
   if (!aligned16(src) || !aligned16(dst) || (zero && !aligned16(zero))) return WFD_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = model_grid((long long)n * (d / 8));
-  if (dtype == WFD_DTYPE_BF16)
-    scatter_rows_kernel<__nv_bfloat16><<<grid, kModelThreads, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(src), idx, idx_stride, static_cast<__nv_bfloat16*>(dst),
-        static_cast<__nv_bfloat16*>(zero), n, d, n_dst, d_err);
-  else if (dtype == WFD_DTYPE_F32)
-    scatter_rows_kernel<float><<<grid, kModelThreads, 0, st>>>(static_cast<const float*>(src), idx, idx_stride,
-                                                              static_cast<float*>(dst), static_cast<float*>(zero), n,
-                                                              d, n_dst, d_err);
-  else
+  if (dtype == WFD_DTYPE_BF16) {
+    if (launch_pdl(scatter_rows_kernel<__nv_bfloat16>, dim3(grid), dim3(kModelThreads), 0, st,
+                   static_cast<const __nv_bfloat16*>(src), idx, idx_stride, static_cast<__nv_bfloat16*>(dst),
+                   static_cast<__nv_bfloat16*>(zero), n, d, n_dst, d_err) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else if (dtype == WFD_DTYPE_F32) {
+    if (launch_pdl(scatter_rows_kernel<float>, dim3(grid), dim3(kModelThreads), 0, st,
+                   static_cast<const float*>(src), idx, idx_stride, static_cast<float*>(dst),
+                   static_cast<float*>(zero), n, d, n_dst, d_err) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else
     return WFD_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
@@ -874,8 +886,9 @@ extern "C" int wfd_items_from_table(const int32_t* tab, int32_t cols, int32_t c_
     return WFD_ERR_INVALID_ARG;
   if (n == 0) return WFD_OK;
   if (!tab || !items) return WFD_ERR_INVALID_ARG;
-  items_from_table_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      tab, cols, c_slot, c_seq, c_pos, c_qlen, reinterpret_cast<int32_t*>(items), n);
+  if (launch_pdl(items_from_table_kernel, dim3((n + 255) / 256), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                 tab, cols, c_slot, c_seq, c_pos, c_qlen, reinterpret_cast<int32_t*>(items), n) != cudaSuccess)
+    return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
@@ -885,11 +898,15 @@ extern "C" int wfd_argmax_rows(const void* x, int32_t* out, int32_t n, int32_t V
   if (!x || !out) return WFD_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int vec = (V % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
-  if (dtype == WFD_DTYPE_BF16)
-    argmax_rows_kernel<__nv_bfloat16><<<n, kArgmaxThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), out, V, vec);
-  else if (dtype == WFD_DTYPE_F32)
-    argmax_rows_kernel<float><<<n, kArgmaxThreads, 0, st>>>(static_cast<const float*>(x), out, V, vec);
-  else
+  if (dtype == WFD_DTYPE_BF16) {
+    if (launch_pdl(argmax_rows_kernel<__nv_bfloat16>, dim3(n), dim3(kArgmaxThreads), 0, st,
+                   static_cast<const __nv_bfloat16*>(x), out, V, vec) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else if (dtype == WFD_DTYPE_F32) {
+    if (launch_pdl(argmax_rows_kernel<float>, dim3(n), dim3(kArgmaxThreads), 0, st, static_cast<const float*>(x),
+                   out, V, vec) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else
     return WFD_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
@@ -918,24 +935,27 @@ int sched_check(const wfd_sched_params* p) {
 extern "C" int wfd_sched_pre_tick(const wfd_sched_params* p, void* stream) {
   const int rc = sched_check(p);
   if (rc != WFD_OK) return rc;
-  sched_pre_tick_kernel<<<1, kSchedThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      *reinterpret_cast<const SchedParams*>(p));
+  if (launch_pdl(sched_pre_tick_kernel, dim3(1), dim3(kSchedThreads), 0, static_cast<cudaStream_t>(stream),
+                 *reinterpret_cast<const SchedParams*>(p)) != cudaSuccess)
+    return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
 extern "C" int wfd_sched_route(const wfd_sched_params* p, void* stream) {
   const int rc = sched_check(p);
   if (rc != WFD_OK) return rc;
-  sched_route_kernel<<<1, kSchedThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      *reinterpret_cast<const SchedParams*>(p));
+  if (launch_pdl(sched_route_kernel, dim3(1), dim3(kSchedThreads), 0, static_cast<cudaStream_t>(stream),
+                 *reinterpret_cast<const SchedParams*>(p)) != cudaSuccess)
+    return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
 extern "C" int wfd_sched_settle(const wfd_sched_params* p, void* stream) {
   const int rc = sched_check(p);
   if (rc != WFD_OK) return rc;
-  sched_settle_kernel<<<(p->B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      *reinterpret_cast<const SchedParams*>(p));
+  if (launch_pdl(sched_settle_kernel, dim3((p->B + 127) / 128), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                 *reinterpret_cast<const SchedParams*>(p)) != cudaSuccess)
+    return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 

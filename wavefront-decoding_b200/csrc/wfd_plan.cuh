@@ -77,6 +77,7 @@ __device__ __forceinline__ long long block_excl_scan(long long x, long long* war
 }
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) {
+  griddep_wait();  // launched with programmatic stream serialization (items come from the predecessor)
   griddep_launch_dependents();  // the attention kernel may run its prologue meanwhile
   __shared__ long long warp_tot[32];
   __shared__ long long s_total;
