@@ -25,8 +25,7 @@ __device__ __forceinline__ void copy_row(char* dst, const char* src, long long b
 __global__ void append_kernel(const char* k_new, const char* v_new, char* kc, char* vc, int32_t* lens,
                               const int32_t* slots, const int32_t* seqs, const int32_t* positions, int n,
                               int slot_offset, CacheGeom g, int* err) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n) return;

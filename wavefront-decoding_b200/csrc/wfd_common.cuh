@@ -68,6 +68,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // execute griddep_wait() before it touches anything the predecessor writes (or
 // reads and this kernel overwrites).  griddep_launch_dependents() lets the next
 // such kernel start early.  Both are no-ops without a programmatic dependency.
+// Every kernel of this library is launched that way and waits first; only the
+// plan -> append -> attention chain inside one call triggers early, because a
+// kernel's successor outside the call may be a library kernel that reads our
+// output before it waits (seen on B200 as run-to-run differences when an early
+// trigger preceded a cuBLAS GEMM).
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -66,8 +66,7 @@ __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return
 template <typename T>
 __global__ void __launch_bounds__(kModelThreads) rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                  T* __restrict__ y, int n, int d, float eps) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const int row = blockIdx.x * (kModelThreads / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
@@ -104,8 +103,7 @@ __global__ void __launch_bounds__(kModelThreads)
                       const int32_t* __restrict__ pos, int pos_stride, int pos_period, T* __restrict__ q,
                       T* __restrict__ k, T* __restrict__ v, int n, int H, int Hkv, int Dh, int style, int max_pos,
                       int* err) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const int half = Dh >> 1;
   const int heads = H + 2 * Hkv;
   const long long per_row = (long long)heads * half;  // element pairs per row
@@ -140,8 +138,7 @@ __global__ void __launch_bounds__(kModelThreads)
 template <typename T>
 __global__ void __launch_bounds__(kModelThreads) silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out,
                                                                   int n, int dff) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const int vpr = dff / 8;
   const long long total = (long long)n * vpr;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
@@ -171,8 +168,7 @@ template <typename T>
 __global__ void __launch_bounds__(kModelThreads)
     gather_rows_kernel(const T* __restrict__ a, const T* __restrict__ b, const int32_t* __restrict__ idx, int stride,
                        T* __restrict__ out, int n, int d, int n_src, int* err) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const int vpr = d / 8;
   const long long total = (long long)n * vpr;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
@@ -200,8 +196,7 @@ template <typename T>
 __global__ void __launch_bounds__(kModelThreads)
     scatter_rows_kernel(const T* __restrict__ src, const int32_t* __restrict__ idx, int stride, T* __restrict__ dst,
                         T* __restrict__ zero, int n, int d, int n_dst, int* err) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const int vpr = d / 8;
   const long long total = (long long)n * vpr;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
@@ -225,8 +220,7 @@ __global__ void __launch_bounds__(kModelThreads)
 // items[i] = {tab[i][c_slot], tab[i][c_seq], tab[i][c_pos], tab[i][c_qlen], i}
 __global__ void items_from_table_kernel(const int32_t* __restrict__ tab, int cols, int c_slot, int c_seq, int c_pos,
                                         int c_qlen, int32_t* __restrict__ items, int n) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int32_t* r = tab + (long long)i * cols;
     int32_t* it = items + (long long)i * 5;
@@ -250,8 +244,7 @@ constexpr int kArgmaxThreads = 512;
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const T* __restrict__ x, int32_t* __restrict__ out,
                                                                       int V, int vec) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const T* row = x + (long long)blockIdx.x * V;
   float best = -__int_as_float(0x7f800000);
   int bi = 0x7fffffff;

@@ -82,8 +82,7 @@ __device__ __forceinline__ void sched_fill_row(int32_t* row, int cols, const Sch
 // P table (one row per sequence: its queued token, now entering the wave at
 // step 0) and the compacted R table of every live token.  One block.
 __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const SchedParams p) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   __shared__ int s_cnt[kSchedThreads];
   __shared__ int s_any_p;
   __shared__ unsigned long long s_keys[2];
@@ -160,8 +159,7 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
 // After the R union: every live token advanced one step.  Route commit points
 // (step == T_total, C row 2b) and draft points (step == T_draft, C row 2b + 1).
 __global__ void __launch_bounds__(kSchedThreads) sched_route_kernel(const SchedParams p) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   __shared__ int s_any_c;
   __shared__ unsigned long long s_keys;
   const int b = threadIdx.x;
@@ -234,8 +232,7 @@ __device__ __forceinline__ void sched_commit(const SchedParams& p, int b, int to
 // Settle: accept / reject the commit point's successor, cascade rollback, queue
 // the next token and the new leading-edge draft.  One thread per sequence.
 __global__ void __launch_bounds__(kSchedThreads) sched_settle_kernel(const SchedParams p) {
-  griddep_wait();  // launched with programmatic stream serialization
-  griddep_launch_dependents();
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= p.B || p.done[b]) return;
   const int vs = p.c_slot[2 * b], ds = p.c_slot[2 * b + 1];
