@@ -71,9 +71,9 @@ CFG5 = dict(B=64, R=16, H=32, Hkv=8, Dh=128, L0=32768, W=8, seed=5, alpha=0.8)
 # wave_tc_cfg4attn.md for tcgen05).
 # cfg3 was captured at batch 8 and scaled by the units processed (x4 at batch 32).
 NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
-                     ("cfg2", "tc"): 543_091_968 + 6_767_104,
+                     ("cfg2", "tc"): 543_152_128 + 4_816_384,
                      ("cfg3", "tc"): (2_189_340_160 + 8_944_640) * 4,
-                     ("cfg4attn", "tc"): 3_631_410_688 + 8_572_672}
+                     ("cfg4attn", "tc"): 3_631_393_536 + 6_166_272}
 
 
 def ncu_traffic(workload: str, tc: bool, c: dict):
