@@ -526,14 +526,14 @@ def run_wfd(args):
     value_e2e = total_bytes / (ms_e2e * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     achieved = nbytes / (ms * 1e-3) / 1e9    # per GPU, per launch of the step
-    # bf16 / Dh=128 defaults to the tensor-core kernel: plan + window append +
-    # wave_tc_kernel per step; the CUDA-core kernel is plan + wave_decode_kernel
+    # bf16 / Dh=128 defaults to the tensor-core kernel: plan (with the window
+    # append) + wave_tc_kernel per step; the CUDA-core kernel is plan + wave_decode_kernel
     tc = args.kernel != 0
     nqp = 16 if c["H"] // c["Hkv"] * max_q <= 16 else 32
-    kernel_name = (f"wave_tc_kernel<{nqp}> (+ plan_kernel, append_segs_kernel" if tc else
+    kernel_name = (f"wave_tc_kernel<{nqp}> (+ plan_kernel with the window append" if tc else
                    "wave_decode_kernel<bf16,128,4> (+ plan_kernel")
     kernel_name += (", commit_window_kernel" if acc is not None else "") + ", timed together)"
-    launches_per_step = (3 if tc else 2) + (1 if acc is not None else 0)
+    launches_per_step = 2 + (1 if acc is not None else 0)
     line = None
     if rank == 0:
         line = {

@@ -337,24 +337,30 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   pp.Dh = A.Dh;
   pp.elem_bytes = elem_bytes(A.dtype);
   pp.err = A.err;
-  if (launch_pdl(plan_kernel, dim3(1), dim3(kPlanThreads), 0, st, pp) != cudaSuccess)
+  // The tensor-core kernel reads every key through TMA, so the window rows are
+  // appended to the cache before it starts: by extra blocks of the plan kernel
+  // (the CUDA-core kernel appends them itself).
+  int plan_blocks = 1;
+  if (which == 1 && A.k_new != nullptr && A.k_app != nullptr) {
+    if (A.mode != kPlanSlots) return WFD_ERR_INVALID_ARG;
+    pp.k_new = static_cast<const char*>(A.k_new);
+    pp.v_new = static_cast<const char*>(A.v_new);
+    pp.k_app = static_cast<char*>(A.k_app);
+    pp.v_app = static_cast<char*>(A.v_app);
+    pp.row_bytes = (long long)A.Hkv * A.Dh * 2;
+    pp.k_row_offset = (long long)A.slot_offset * A.n_seqs * (long long)A.max_seq;
+    pp.lens = A.lens;
+    pp.lens_offset = A.slot_offset * A.n_seqs;
+    plan_blocks = 1 + (A.n < 4 * sms ? A.n : 4 * sms);
+  }
+  if (launch_pdl(plan_kernel, dim3(plan_blocks), dim3(kPlanThreads), 0, st, pp) != cudaSuccess)
     return WFD_ERR_CUDA;
-  if (cudaGetLastError() != cudaSuccess) return WFD_ERR_CUDA;
 
   const float scale = A.scale > 0.f ? A.scale : 1.0f / std::sqrt((float)A.Dh);
   const float log2e = 1.4426950408889634f;
 
   if (which == 1) {
     const long long k_row_offset = (long long)A.slot_offset * A.n_seqs * (long long)A.max_seq;
-    if (A.k_new != nullptr && A.k_app != nullptr) {
-      // the tensor-core kernel reads every key through TMA: append the window
-      // rows to the cache first (same stream, so the attention sees them)
-      if (launch_pdl(append_segs_kernel, dim3(A.n), dim3(256), 0, st, (const Seg*)pp.segs, A.n,
-                     static_cast<const char*>(A.k_new), static_cast<const char*>(A.v_new),
-                     static_cast<char*>(A.k_app), static_cast<char*>(A.v_app), (long long)A.Hkv * A.Dh * 2,
-                     k_row_offset, A.lens, A.slot_offset * A.n_seqs) != cudaSuccess)
-        return WFD_ERR_CUDA;
-    }
     VerifyParams vp;
     memset(&vp, 0, sizeof(vp));
     vp.q = A.q;

@@ -45,29 +45,6 @@ __global__ void append_kernel(const char* k_new, const char* v_new, char* kc, ch
   if (lane == 0 && lens != nullptr) atomicMax(lens + slot * g.n_seqs + seq, pos + 1);
 }
 
-// Window append from a planned segment table (slot mode): segment i's rows
-// k_new[new_row0 + j] go to key row k_row0 + k_row_offset + (k_len - q_len) + j,
-// all kv heads; the slot length is raised to k_len.  One CTA per segment.  Used
-// ahead of the tensor-core kernel, which reads every key through TMA.
-__global__ void append_segs_kernel(const Seg* segs, int n, const char* k_new, const char* v_new, char* kc, char* vc,
-                                   long long row_bytes, long long k_row_offset, int32_t* lens, int lens_offset) {
-  griddep_launch_dependents();
-  griddep_wait();  // segs come from the plan kernel
-  const int i = blockIdx.x;
-  if (i >= n) return;
-  const Seg S = segs[i];
-  if (S.new_row0 < 0 || S.q_len <= 0) return;
-  const long long nvec = row_bytes / 16;
-  for (long long e = threadIdx.x; e < (long long)S.q_len * nvec; e += blockDim.x) {
-    const long long j = e / nvec, c = e % nvec;
-    const long long src = (S.new_row0 + j) * row_bytes + c * 16;
-    const long long dst = (S.k_row0 + k_row_offset + S.k_len - S.q_len + j) * row_bytes + c * 16;
-    *reinterpret_cast<uint4*>(kc + dst) = ld_nc_v4(k_new + src);
-    *reinterpret_cast<uint4*>(vc + dst) = ld_nc_v4(v_new + src);
-  }
-  if (threadIdx.x == 0 && lens != nullptr && S.lens_idx >= 0) atomicMax(lens + S.lens_idx + lens_offset, S.k_len);
-}
-
 // write_prefill: k, v (n_seqs, L, Hkv, Dh) -> positions [0, L) of `slot`.
 __global__ void prefill_kernel(const char* k, const char* v, char* kc, char* vc, int32_t* lens, int slot, int L,
                                CacheGeom g) {

@@ -45,9 +45,24 @@ struct PlanParams {
   void* out;
   int Hq, Dh, elem_bytes;
   int* err;
+  // optional window append (slot mode, blocks 1..gridDim.x-1): rows
+  // k_new[q_row0 + j] of every valid item go to key row
+  // (slot * n_seqs + seq) * max_seq + k_row_offset + pos0 + j of k_app / v_app,
+  // and the slot length lens[slot * n_seqs + seq + lens_offset] rises to pos0 + q_len
+  const char* k_new;
+  const char* v_new;
+  char* k_app;
+  char* v_app;
+  long long row_bytes, k_row_offset;
+  int32_t* lens;
+  int lens_offset;
 };
 
 constexpr int kPlanThreads = 1024;
+// Up to this many segments the prefix sums are also kept in shared memory, so
+// the per-CTA start-record searches run on shared memory instead of making a
+// chain of dependent global loads each.
+constexpr int kPlanStaged = 4095;
 
 __device__ __forceinline__ long long block_excl_scan(long long x, long long* warp_tot, long long* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -79,8 +94,33 @@ __device__ __forceinline__ long long block_excl_scan(long long x, long long* war
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) {
   griddep_wait();  // launched with programmatic stream serialization (items come from the predecessor)
   griddep_launch_dependents();  // the attention kernel may run its prologue meanwhile
+  if (blockIdx.x > 0) {
+    // ---- window append: the tensor-core kernel reads every key through TMA, so
+    // the window rows go to the cache before it starts (it waits for this grid).
+    // Items are checked as below; invalid ones are skipped (block 0 reports them).
+    const long long nvec = p.row_bytes / 16;
+    for (int i = blockIdx.x - 1; i < p.n; i += gridDim.x - 1) {
+      const wfd_item it = p.items[i];
+      if (it.slot < 0 || it.slot >= p.n_slots || it.seq < 0 || it.seq >= p.n_seqs || it.pos0 < 0 || it.q_len <= 0 ||
+          (long long)it.pos0 + it.q_len > p.max_seq || it.q_row0 < 0 || (long long)it.q_row0 + it.q_len > p.n_rows)
+        continue;
+      const long long row0 = ((long long)it.slot * p.n_seqs + it.seq) * p.max_seq + p.k_row_offset + it.pos0;
+      for (long long e = threadIdx.x; e < (long long)it.q_len * nvec; e += blockDim.x) {
+        const long long j = e / nvec, c = e % nvec;
+        const long long src = (it.q_row0 + j) * p.row_bytes + c * 16;
+        const long long dst = (row0 + j) * p.row_bytes + c * 16;
+        *reinterpret_cast<uint4*>(p.k_app + dst) = ld_nc_v4(p.k_new + src);
+        *reinterpret_cast<uint4*>(p.v_app + dst) = ld_nc_v4(p.v_new + src);
+      }
+      if (threadIdx.x == 0 && p.lens != nullptr)
+        atomicMax(p.lens + it.slot * p.n_seqs + it.seq + p.lens_offset, it.pos0 + it.q_len);
+    }
+    return;
+  }
   __shared__ long long warp_tot[32];
   __shared__ long long s_total;
+  __shared__ long long s_prefix[kPlanStaged + 1];
+  const bool staged = p.n <= kPlanStaged;
   long long carry = 0;
   for (int base = 0; base < p.n; base += kPlanThreads) {
     const int i = base + threadIdx.x;
@@ -158,15 +198,22 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) 
       }
     }
     const long long excl = block_excl_scan(work, warp_tot, &s_total);
-    if (i < p.n) p.prefix[i] = carry + excl;
+    if (i < p.n) {
+      p.prefix[i] = carry + excl;
+      if (staged) s_prefix[i] = carry + excl;
+    }
     carry += s_total;
     __syncthreads();
   }
-  if (threadIdx.x == 0) p.prefix[p.n] = carry;
+  if (threadIdx.x == 0) {
+    p.prefix[p.n] = carry;
+    if (staged) s_prefix[p.n] = carry;
+  }
   if (p.start != nullptr) {
     __syncthreads();  // the prefix above is complete and visible to the block
     const long long total = (long long)p.seg_units * carry;
     const long long share = total > 0 ? (total + p.seg_grid - 1) / p.seg_grid : 1;
+    const long long* pf = staged ? s_prefix : p.prefix;
     for (int c = threadIdx.x; c < p.seg_grid; c += blockDim.x) {
       const long long a = (long long)c * share;
       int lo = 0, hi = p.n - 1;  // largest i with seg_units * prefix[i] <= a
@@ -175,14 +222,14 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) 
       } else {
         while (lo < hi) {
           const int mid = (lo + hi + 1) >> 1;
-          if ((long long)p.seg_units * p.prefix[mid] <= a) lo = mid;
+          if ((long long)p.seg_units * pf[mid] <= a) lo = mid;
           else hi = mid - 1;
         }
       }
       CtaStart cs;
       cs.S = p.segs[lo];
-      cs.base = (long long)p.seg_units * p.prefix[lo];
-      cs.nbase = lo + 1 <= p.n - 1 ? (long long)p.seg_units * p.prefix[lo + 1] : 0x7fffffffffffffffll;
+      cs.base = (long long)p.seg_units * pf[lo];
+      cs.nbase = lo + 1 <= p.n - 1 ? (long long)p.seg_units * pf[lo + 1] : 0x7fffffffffffffffll;
       cs.seg = lo;
       cs.pad[0] = cs.pad[1] = cs.pad[2] = 0;
       p.start[c] = cs;

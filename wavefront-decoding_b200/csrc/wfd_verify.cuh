@@ -38,8 +38,8 @@
 // (the other half is discarded).  The MMA count per byte is then that of
 // head_dim 128: the tensor-core issue rate, not the HBM, bounds a 64-dim tile.
 //
-// Window keys are read from the KV cache: the caller appends the window rows
-// (append_segs_kernel) in a launch before this one.  Launched with programmatic
+// Window keys are read from the KV cache: the window rows are appended by the
+// plan kernel's extra blocks in the launch before this one.  Launched with programmatic
 // stream serialization: barrier set-up and the TMEM allocation overlap the
 // previous kernel; griddep_wait() precedes every read of its outputs.
 #pragma once

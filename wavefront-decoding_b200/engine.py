@@ -109,13 +109,12 @@ class WaveEngine:
         # accounting (host side, exact): K/V bytes the attention of live rows
         # reads, libwfd kernel launches, bytes read back per C union
         self._row_bytes = cfg.n_kv_heads * cfg.head_dim * torch.finfo(model.dtype).bits // 8
-        # the library's kernel choice for single-row waves: tcgen05 for bf16 except
-        # MHA at head_dim 64 with an odd kv-head count
-        tc = model.dtype == torch.bfloat16 and not (cfg.head_dim == 64 and cfg.n_heads == cfg.n_kv_heads
-                                                     and cfg.n_kv_heads % 2 == 1)
-        # wave_attn: plan + (window append + tcgen05 kernel | fused decode kernel);
-        # prelude / coda layers: append + plan + segment attention
-        self._launches = {"P": 3 * cfg.n_prelude, "R": (3 if tc else 2) * cfg.n_core, "C": 3 * cfg.n_coda}
+        # every libwfd kernel a body launches.  Per prelude / coda layer: 2 RMSNorm,
+        # RoPE split, append, plan, segment attention, SwiGLU gate; per core layer:
+        # 2 RMSNorm, RoPE split, plan (with the window append), attention (tcgen05 or
+        # the fused CUDA-core decode), SwiGLU gate.  Per body: P gather + scatter,
+        # R gather + item table + scatter, C gather + final RMSNorm + greedy argmax.
+        self._launches = {"P": 2 + 7 * cfg.n_prelude, "R": 3 + 6 * cfg.n_core, "C": 3 + 7 * cfg.n_coda}
         self._layers = {"P": cfg.n_prelude, "R": cfg.n_core, "C": cfg.n_coda}
         self.kv_read_bytes = 0
         self.wfd_launches = 0
