@@ -370,3 +370,35 @@ def test_tc_varlen_packed_causal(cuda_dev):
                          max(k_lens), causal=True)
     no_device_error(cuda_dev)
     assert maxdiff(out, ref) < TOL_BF16
+
+
+def test_tc_more_items_than_staged_and_append_blocks(cuda_dev):
+    """4200 items: more than the plan kernel keeps in shared memory (its start
+    records then search the global prefix) and many more than its window-append
+    blocks (grid-stride); two out-of-range items are skipped and reported while
+    every valid item is still exact and appended."""
+    from wavefront_decoding_b200 import runtime as rt
+    from wavefront_decoding_b200._abi import WfdError
+    rng = np.random.default_rng(11)
+    n_slots, B, S, H, Hkv, Dh = 2, 2100, 48, 4, 2, 128
+    items = [[r, b, int(rng.integers(0, S - 1)), 1, r * B + b] for r in range(n_slots) for b in range(B)]
+    K, V, q, kn, vn = _wave_case(41, n_slots, B, S, H, Hkv, Dh, items, torch.bfloat16)
+    ref, o = _oracle_wave(K, V, q, kn, vn, items)
+    bad = [list(items[7]), list(items[3001])]
+    bad[0][0] = n_slots          # slot out of range
+    bad[1][2] = S                # window past the slot
+    run_items = [bad[0] if i == 7 else bad[1] if i == 3001 else it for i, it in enumerate(items)]
+    out, Kd, Vd, lens = _run_wave(cuda_dev, K, V, q, kn, vn, run_items, 1, kernel=1)
+    with pytest.raises(WfdError):
+        rt.read_device_error(cuda_dev)
+    keep = torch.ones(len(items), dtype=torch.bool)
+    keep[7] = keep[3001] = False
+    assert maxdiff(out.cpu()[keep], ref[keep.numpy()]) < TOL_BF16
+    # appended rows: every valid item's window row is in place; the skipped items wrote nothing
+    Kh = Kd.cpu()
+    for i, (slot, seq, p0, ql, row) in enumerate(items):
+        if keep[i]:
+            assert torch.equal(Kh[slot, seq, p0], kn[row]), i
+            assert int(lens[slot, seq]) == p0 + ql
+    assert torch.equal(Kh[0, 7], K[0, 7])
+    assert int(lens[0, 7]) == 0
