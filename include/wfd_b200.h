@@ -297,6 +297,7 @@ typedef struct {
   int32_t p_cols, c_cols, r_cap;
   int32_t scratch_row, scratch_seq;
   int32_t p_slot0, n_prelude, c_slot0, n_coda;
+  int32_t depth_slots; /* core depth slots: T_total, or the KV-sharing budget s (depth r -> slot r % s) */
 } wfd_sched_params;
 
 /* Before the P union: queue -> wave for each sequence's queued token (P table

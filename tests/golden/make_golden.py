@@ -166,9 +166,12 @@ def gen_scheduler() -> dict:
     return out
 
 
-def gen_config1(n_new: int = 64, T_total: int = 4, drafts=(1, 2, 4)) -> dict:
+def gen_config1(n_new: int = 64, T_total: int = 4, drafts=(1, 2, 4), budgets=(2,), budget_drafts=(1, 2)) -> dict:
     """Config 1: the reference's ParcaeBlocks on the fixture model, greedy, fp32,
-    SDPA backend; AR (ar_baseline.py:132-193) and WFD (scheduler.py:89-225)."""
+    SDPA backend; AR (ar_baseline.py:132-193) and WFD (scheduler.py:89-225).
+    With KV sharing (`kv_budget_s` = s < T_total, parcae_blocks.py:77-81,114-120:
+    core depth r uses recurrence slot r % s, last write wins) for AR and WFD at
+    the given draft depths; keys ar_s{s} / wfd_d{d}_s{s}."""
     import parcae_fixture as pf
     from src.decoding.ar_baseline import ar_generate_parcae_blocks
     from src.decoding.parcae_blocks import ParcaeBlocks
@@ -178,9 +181,10 @@ def gen_config1(n_new: int = 64, T_total: int = 4, drafts=(1, 2, 4)) -> dict:
     model = pf.ParcaeFixture(seed=0).eval()
     prompt = pf.config1_prompt()
 
-    def blocks():
+    def blocks(budget=None):
         b = ParcaeBlocks(model, T_total, max_seq_len=pf.MAX_SEQ)
         b.state_init = "zero"
+        b.kv_budget_s = budget
         caches = []
         orig = b.prefill
 
@@ -209,6 +213,21 @@ def gen_config1(n_new: int = 64, T_total: int = 4, drafts=(1, 2, 4)) -> dict:
                                                            "n_rollback_events")}}
         print(f"config1 T_draft={d}: {out[f'wfd_d{d}']['n_drafts_accepted']}/"
               f"{out[f'wfd_d{d}']['n_drafts_proposed']} drafts accepted")
+    counters = ("n_r_calls", "n_p_calls", "n_c_calls", "n_drafts_proposed", "n_drafts_accepted",
+                "n_drafts_rejected", "n_rollback_events")
+    for sb in budgets:
+        b, caches = blocks(sb)
+        toks, _ = ar_generate_parcae_blocks(b, prompt[None], n_new)
+        out[f"ar_s{sb}"] = {"tokens": [int(t) for t in toks], "seqlen": lens(caches[-1])}
+        for d in budget_drafts:
+            b, caches = blocks(sb)
+            toks, tr = generate_wavefront_dynamic(b, prompt, n_new, SsdPolicy(T_total=T_total, T_draft=d))
+            key = f"wfd_d{d}_s{sb}"
+            out[key] = {"tokens": [int(t) for t in toks], "seqlen": lens(caches[-1]),
+                        **{k: getattr(tr, k) for k in counters}}
+            print(f"config1 kv_budget_s={sb} T_draft={d}: {out[key]['n_drafts_accepted']}/"
+                  f"{out[key]['n_drafts_proposed']} drafts accepted, "
+                  f"{sum(a != c for a, c in zip(out[key]['tokens'], out[f'ar_s{sb}']['tokens']))} tokens differ from AR")
     return out
 
 

@@ -178,15 +178,16 @@ def to_looped_weights(m: ParcaeFixture) -> dict:
             "core": [blk(b) for b in tr.core_block], "coda": [blk(b) for b in tr.coda]}
 
 
-def looped_config(m: ParcaeFixture, T_total: int):
-    """The product model config matching the fixture."""
+def looped_config(m: ParcaeFixture, T_total: int, kv_budget_s: int = 0):
+    """The product model config matching the fixture (kv_budget_s: the
+    reference blocks' KV-sharing budget, 0 = off)."""
     from wavefront_decoding_b200.looped_lm import LoopedLMConfig
     c = m.config
     tr = m.transformer
     return LoopedLMConfig(vocab=tr.wte.num_embeddings, d_model=c.n_embd, n_heads=c.num_attention_heads,
                           n_kv_heads=c.num_key_value_heads, head_dim=c.n_embd // c.num_attention_heads,
                           d_ff=c.d_ff, n_prelude=len(tr.prelude), n_core=len(tr.core_block), n_coda=len(tr.coda),
-                          T_total=T_total, rope_style="interleaved", norm_eps=1e-6)
+                          T_total=T_total, rope_style="interleaved", norm_eps=1e-6, kv_budget_s=kv_budget_s)
 
 
 def weight_sums(m: ParcaeFixture) -> list[float]:

@@ -46,3 +46,26 @@ def test_oracle_matches_reference_tokens():
     W, cfg = olm.weights_from(model)
     n = 8      # full recompute per token in float64: keep the CPU suite short
     assert olm.greedy_generate(W, cfg, pf.config1_prompt().tolist(), n) == GOLD["ar"]["tokens"][:n]
+
+
+def test_kv_sharing_slot_map():
+    """KV-sharing budget s: core depth r -> depth slot r % s, s depth slots allocated."""
+    from wavefront_decoding_b200.looped_lm import LoopedLMConfig
+    c = LoopedLMConfig(n_prelude=1, n_core=2, n_coda=1, T_total=4, kv_budget_s=2)
+    assert c.n_depth_slots == 2 and c.n_slots == 6
+    assert [c.slot_core(r, l) for r in range(4) for l in range(2)] == [1, 2, 3, 4, 1, 2, 3, 4]
+    assert c.slot_coda(0) == 5
+    for s in (0, 4, 9):        # off: one slot per depth
+        c = LoopedLMConfig(n_prelude=1, n_core=2, n_coda=1, T_total=4, kv_budget_s=s)
+        assert c.n_depth_slots == 4 and c.slot_core(3, 1) == 8 and c.slot_coda(0) == 9
+
+
+def test_reference_kv_sharing_golden():
+    """The reference's own results with kv_budget_s = 2: WFD commits AR's tokens
+    on this fixture, the shared slots change the drafts (counters differ from the
+    unshared run), and only the used slots exist (coda kept at its unshared index)."""
+    for d in (1, 2):
+        assert GOLD[f"wfd_d{d}_s2"]["tokens"] == GOLD["ar_s2"]["tokens"]
+    assert (GOLD["wfd_d1_s2"]["n_drafts_accepted"], GOLD["wfd_d2_s2"]["n_drafts_accepted"]) != \
+        (GOLD["wfd_d1"]["n_drafts_accepted"], GOLD["wfd_d2"]["n_drafts_accepted"])
+    assert set(GOLD["ar_s2"]["seqlen"]) == {"0", "1", "2", "3", "4", "9"}

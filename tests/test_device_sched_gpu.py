@@ -8,7 +8,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from test_engine_gpu import _check_cache_vs_oracle, _config1_engine, _engine, _prompts, _small_cfg
+from test_engine_gpu import _check_cache_vs_oracle, _config1_engine, _engine, _prompts, _seqlen_as_reference, _small_cfg
 
 pytestmark = pytest.mark.gpu
 
@@ -87,6 +87,22 @@ def test_device_config1_matches_reference(cuda_dev, T_draft):
         assert getattr(t, k) == g[k], k
     lens = eng.cache.seqlen
     assert {str(s): lens[s][0] for s in range(len(lens))} == g["seqlen"]
+
+
+@pytest.mark.parametrize("T_draft", [1, 2])
+def test_device_config1_kv_sharing_matches_reference(cuda_dev, T_draft):
+    """KV sharing (s = 2) with route / settle on the device: the reference's
+    tokens, counters and slot lengths."""
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import generate_wavefront_device
+    eng, prompt, gold = _config1_engine(kv_budget_s=2)
+    g = gold[f"wfd_d{T_draft}_s2"]
+    bt = generate_wavefront_device(eng, prompt, gold["n_new"], sch.SsdPolicy(gold["T_total"], T_draft))
+    t = bt.per_seq[0]
+    assert t.tokens == g["tokens"]
+    for k in ("n_drafts_proposed", "n_drafts_accepted", "n_drafts_rejected", "n_rollback_events"):
+        assert getattr(t, k) == g[k], k
+    assert _seqlen_as_reference(eng) == g["seqlen"]
 
 
 def test_device_repeat_generation_reuses_graph(cuda_dev):

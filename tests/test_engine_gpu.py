@@ -119,14 +119,14 @@ def test_engine_emulated_acceptance(cuda_dev):
 # ---------------------------------------------------------------------------
 # config 1: the reference's ParcaeBlocks tokens / counters / KV lengths
 # ---------------------------------------------------------------------------
-def _config1_engine():
+def _config1_engine(kv_budget_s: int = 0):
     import parcae_fixture as pf
     from wavefront_decoding_b200.engine import WaveEngine
     from wavefront_decoding_b200.looped_lm import LoopedLM
     from test_config1 import GOLD
     torch.backends.cuda.matmul.allow_tf32 = False
     m = pf.ParcaeFixture(seed=0)
-    model = LoopedLM(pf.looped_config(m, GOLD["T_total"]), dtype=torch.float32, device="cuda")
+    model = LoopedLM(pf.looped_config(m, GOLD["T_total"], kv_budget_s), dtype=torch.float32, device="cuda")
     model.load_weights(pf.to_looped_weights(m))
     return WaveEngine(model, 1, 256), pf.config1_prompt()[None], GOLD
 
@@ -152,6 +152,42 @@ def test_config1_wfd_matches_reference(cuda_dev, T_draft):
         assert getattr(t, k) == g[k], k
     lens = eng.cache.seqlen
     assert {str(s): lens[s][0] for s in range(len(lens))} == g["seqlen"]
+
+
+def _seqlen_as_reference(eng):
+    """The engine's slot lengths keyed like the reference's cache: with KV sharing
+    ParcaeBlocks keeps its coda slots at n_prelude + T_total * n_core
+    (parcae_blocks.py:76), while the engine allocates only the depth slots in use."""
+    cfg = eng.cfg
+    shift = (cfg.T_total - cfg.n_depth_slots) * cfg.n_core
+    lens = eng.cache.seqlen
+    return {str(s if s < cfg.slot_coda(0) else s + shift): lens[s][0] for s in range(len(lens))}
+
+
+def test_config1_ar_kv_sharing_matches_reference(cuda_dev):
+    """KV-sharing budget s = 2 (core depth r keeps its K/V in slot r % 2): the
+    reference's AR tokens and slot lengths."""
+    from wavefront_decoding_b200 import scheduler as sch
+    eng, prompt, gold = _config1_engine(kv_budget_s=2)
+    assert eng.cfg.n_slots == 6
+    bt = sch.ar_generate_batch(eng, prompt, gold["n_new"])
+    assert bt.per_seq[0].tokens == gold["ar_s2"]["tokens"]
+    assert _seqlen_as_reference(eng) == gold["ar_s2"]["seqlen"]
+
+
+@pytest.mark.parametrize("T_draft", [1, 2])
+def test_config1_wfd_kv_sharing_matches_reference(cuda_dev, T_draft):
+    """KV sharing with the host scheduler: tokens, draft counters (they differ
+    from the unshared run's) and slot lengths of the reference."""
+    from wavefront_decoding_b200 import scheduler as sch
+    eng, prompt, gold = _config1_engine(kv_budget_s=2)
+    g = gold[f"wfd_d{T_draft}_s2"]
+    bt = sch.generate_wavefront_batch(eng, prompt, gold["n_new"], sch.SsdPolicy(gold["T_total"], T_draft), None)
+    t = bt.per_seq[0]
+    assert t.tokens == g["tokens"]
+    for k in ("n_drafts_proposed", "n_drafts_accepted", "n_drafts_rejected", "n_rollback_events"):
+        assert getattr(t, k) == g[k], k
+    assert _seqlen_as_reference(eng) == g["seqlen"]
 
 
 def _check_cache_vs_oracle(eng, model, prompts, per_seq, tol):

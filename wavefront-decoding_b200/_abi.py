@@ -51,7 +51,7 @@ class wfd_sched_params(ctypes.Structure):
         [(n, ctypes.c_int32) for n in (
             "B", "W", "T_total", "T_draft", "max_new", "emu_len", "n_core", "n_kv_slots", "lens_stride",
             "max_seq", "p_cols", "c_cols", "r_cap", "scratch_row", "scratch_seq", "p_slot0", "n_prelude",
-            "c_slot0", "n_coda")]
+            "c_slot0", "n_coda", "depth_slots")]
 
 
 _P = ctypes.c_void_p

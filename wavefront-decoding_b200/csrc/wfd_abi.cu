@@ -337,17 +337,18 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   pp.Dh = A.Dh;
   pp.elem_bytes = elem_bytes(A.dtype);
   pp.err = A.err;
-  // The tensor-core kernel reads every key through TMA, so the window rows are
-  // appended to the cache before it starts: by extra blocks of the plan kernel
-  // (the CUDA-core kernel appends them itself).
+  // The window rows are appended to the cache before the attention starts, by
+  // extra blocks of the plan kernel: the tensor-core kernel reads every key
+  // through TMA, and with KV sharing (several items of one launch on the same
+  // slot and sequence) an item reads rows another item appends.
   int plan_blocks = 1;
-  if (which == 1 && A.k_new != nullptr && A.k_app != nullptr) {
+  if (A.k_new != nullptr && A.k_app != nullptr) {
     if (A.mode != kPlanSlots) return WFD_ERR_INVALID_ARG;
     pp.k_new = static_cast<const char*>(A.k_new);
     pp.v_new = static_cast<const char*>(A.v_new);
     pp.k_app = static_cast<char*>(A.k_app);
     pp.v_app = static_cast<char*>(A.v_app);
-    pp.row_bytes = (long long)A.Hkv * A.Dh * 2;
+    pp.row_bytes = (long long)A.Hkv * A.Dh * elem_bytes(A.dtype);
     pp.k_row_offset = (long long)A.slot_offset * A.n_seqs * (long long)A.max_seq;
     pp.lens = A.lens;
     pp.lens_offset = A.slot_offset * A.n_seqs;
@@ -391,10 +392,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   dp.v = A.v;
   dp.k_new = A.k_new;
   dp.v_new = A.v_new;
-  dp.k_app = A.k_app;
-  dp.v_app = A.v_app;
   dp.out = A.out;
-  dp.lens = A.lens;
   dp.segs = pp.segs;
   dp.prefix = pp.prefix;
   dp.n_segs = A.n;
@@ -404,7 +402,6 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   dp.scale_log2 = scale * log2e;
   dp.causal = A.causal;
   dp.k_row_offset = (long long)A.slot_offset * A.n_seqs * (long long)A.max_seq;
-  dp.lens_offset = A.slot_offset * A.n_seqs;
   dp.ws_part = reinterpret_cast<float*>(ws + L.part);
   dp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
   dp.err = A.err;
@@ -923,6 +920,8 @@ extern "C" int wfd_argmax_rows(const void* x, int32_t* out, int32_t n, int32_t V
 static_assert(sizeof(wfd_sched_params) == sizeof(wfd::SchedParams), "wfd_sched_params layout");
 static_assert(offsetof(wfd_sched_params, c_out) == offsetof(wfd::SchedParams, c_out), "wfd_sched_params layout");
 static_assert(offsetof(wfd_sched_params, n_coda) == offsetof(wfd::SchedParams, n_coda), "wfd_sched_params layout");
+static_assert(offsetof(wfd_sched_params, depth_slots) == offsetof(wfd::SchedParams, depth_slots),
+              "wfd_sched_params layout");
 
 namespace {
 int sched_check(const wfd_sched_params* p) {

@@ -28,12 +28,9 @@ struct DecodeParams {
   const void* q;
   const void* k;      // key buffer rows (cache or packed)
   const void* v;
-  const void* k_new;  // window rows (slot mode) or null
+  const void* k_new;  // window rows (slot mode) or null; already appended to k / v by the plan kernel
   const void* v_new;
-  void* k_app;        // append destination (== k as writable) or null
-  void* v_app;
   void* out;
-  int32_t* lens;      // slot lengths raised after append, or null
   const Seg* segs;
   const long long* prefix;
   int n_segs;
@@ -41,7 +38,6 @@ struct DecodeParams {
   float scale_log2;   // softmax scale * log2(e)
   int causal;
   long long k_row_offset;  // added to every segment's k_row0 (layer offset in slot mode)
-  int lens_offset;         // added to every segment's lens_idx
   float* ws_part;          // 2 * gridDim.x partial slots
   int* ws_cnt;             // gridDim.x arrival counters (zero between launches)
   int* err;
@@ -243,30 +239,6 @@ __global__ void __launch_bounds__(128) wave_decode_kernel(const DecodeParams p) 
       for (int d = 0; d < VEC / 2; ++d) qv[nq][d] = make_float2(f[2 * d] * p.scale_log2, f[2 * d + 1] * p.scale_log2);
       const int lim = !valid ? -1 : (p.causal ? S.k_len - S.q_len + row : S.k_len - 1);
       if (nq == nq_j) lim_j = lim;
-    }
-
-    // ---- fused append of the window rows this CTA covers (first query group only) ----
-    if (S.new_row0 >= 0 && qg == 0 && p.k_app != nullptr) {
-      const int win0 = S.k_len - S.q_len;
-      const int a0 = (r_lo > win0) ? r_lo : win0;
-      const int n_app = r_hi - a0;
-      if (n_app > 0) {
-        constexpr int VPR = DH / VEC;  // vectors per row
-        for (int e = tid; e < n_app * VPR * 2; e += C::THREADS) {
-          const int kv = e / (n_app * VPR);
-          const int rem = e - kv * n_app * VPR;
-          const int rr = rem / VPR, c = rem % VPR;
-          const int r = a0 + rr;
-          const long long src_row = (long long)S.new_row0 + (r - win0);
-          const long long dst_row = S.k_row0 + p.k_row_offset + r;
-          const T* src = static_cast<const T*>(kv ? p.v_new : p.k_new) + (src_row * p.Hkv + h) * DH + c * VEC;
-          T* dst = static_cast<T*>(kv ? p.v_app : p.k_app) + (dst_row * p.Hkv + h) * DH + c * VEC;
-          *reinterpret_cast<uint4*>(dst) = ld_nc_v4(src);
-        }
-      }
-      if (h == 0 && r_hi == S.k_len && p.lens != nullptr && S.lens_idx >= 0 && tid == 0) {
-        atomicMax(p.lens + S.lens_idx + p.lens_offset, S.k_len);
-      }
     }
 
     // ---- online softmax state ----

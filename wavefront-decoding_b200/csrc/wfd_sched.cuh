@@ -56,6 +56,7 @@ struct SchedParams {
   int p_cols, c_cols, r_cap;
   int scratch_row, scratch_seq;
   int p_slot0, n_prelude, c_slot0, n_coda;  // first KV slot and count of the prelude / coda layers
+  int depth_slots;                           // core depth slots (KV sharing: depth r -> slot r % depth_slots)
 };
 
 __device__ __forceinline__ void sched_pad_row(int32_t* row, int cols, const SchedParams& p, int seg_slot0) {
@@ -134,7 +135,9 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
     for (int j = 0; j < p.W; ++j) {
       const int s = b * p.W + j;
       if (p.alive[s] && p.state[s] == 2) {
-        if (r < p.r_cap) sched_fill_row(p.r_tab + (long long)r * 6, 6, p, 0, b, s, p.step[s] * p.n_core);
+        if (r < p.r_cap)
+          sched_fill_row(p.r_tab + (long long)r * 6, 6, p, 0, b, s,
+                         (p.depth_slots > 0 ? p.step[s] % p.depth_slots : p.step[s]) * p.n_core);
         kk += (unsigned long long)(p.pos[s] + 1);
         ++r;
       }

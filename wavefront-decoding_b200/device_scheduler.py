@@ -110,6 +110,7 @@ class DeviceWave:
         p.scratch_row, p.scratch_seq = e.scratch_row, e.scratch_seq
         p.p_slot0, p.n_prelude = cfg.slot_prelude(0), cfg.n_prelude
         p.c_slot0, p.n_coda = cfg.slot_coda(0), cfg.n_coda
+        p.depth_slots = cfg.n_depth_slots
         self._params[key] = p
         return p
 

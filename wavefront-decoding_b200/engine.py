@@ -9,7 +9,7 @@ ouro_blocks_batch.py:123-248, huginn_blocks_batch.py:207-346), B200-first:
   `hidden` is its pool row, so a union call gathers rows instead of stacking
   per-token tensors, and writes them back in place.
 * One R tick is one attention launch per core layer for the whole union
-  (`wfd_wave_attn`: append + attention fused, one item table shared by all
+  (`wfd_wave_attn`: window append + attention in one call, one item table shared by all
   layers through `slot_offset`), replacing the reference's per-layer
   write_tokens + gather_pack + attn_varlen (ouro_blocks_batch.py:207-231) and the
   graph engine's per-row `_fa_varlen` loop (graph_blocks.py:187-194).
@@ -49,7 +49,7 @@ def _bucket(n: int) -> int:
 class _Tables:
     """Device tables of one (kind, bucket) and their pinned staging copy.
     int32 columns: 0 pool row, 1 position, 2 token id, 3 cache sequence,
-    4 R: slot base (depth * n_core), 5 live (q_len 1) / padding (0),
+    4 R: slot base (depth slot * n_core), 5 live (q_len 1) / padding (0),
     6.. prelude / coda layers: first cache row of the row's (slot, sequence)."""
 
     def __init__(self, kind: str, cap: int, n_cols: int, device):
@@ -160,7 +160,7 @@ class WaveEngine:
         a[:n, 2] = [tk.token_id for tk in toks]
         a[:n, 3] = seq_ids
         if kind == "R":
-            a[:n, 4] = [tk.step * cfg.n_core for tk in toks]
+            a[:n, 4] = [cfg.core_slot_base(tk.step) for tk in toks]
         a[:n, 5] = 1
         for j, slot in enumerate(seg_slots):
             a[:, 6 + j] = (slot * (self.B + 1) + a[:, 3].astype(np.int64)) * self.S

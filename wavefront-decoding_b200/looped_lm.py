@@ -46,19 +46,34 @@ class LoopedLMConfig:
     rope_style: str = "half"  # "half": dims i, i + Dh/2 rotate together; "interleaved": dims 2i, 2i+1
     norm_eps: float = 1e-6
     init_std: float = 0.02
+    # KV sharing across loop depths (parcae_blocks.py:77-81,114-120,
+    # ouro_blocks_batch.py:15-18,66-78): with a budget 0 < s < T_total, core
+    # depth r keeps its K/V in depth slot r % s (the last depth to write a
+    # position wins) and the cache holds s depth slots instead of T_total.
+    # 0 = off (one slot per depth, lossless).
+    kv_budget_s: int = 0
+
+    @property
+    def n_depth_slots(self) -> int:
+        s = self.kv_budget_s
+        return s if 0 < s < self.T_total else self.T_total
 
     @property
     def n_slots(self) -> int:
-        return self.n_prelude + self.T_total * self.n_core + self.n_coda
+        return self.n_prelude + self.n_depth_slots * self.n_core + self.n_coda
 
     def slot_prelude(self, i: int) -> int:
         return i
 
+    def core_slot_base(self, r: int) -> int:
+        """First core slot of loop depth r, relative to the prelude slots (r % s * n_core)."""
+        return (r % self.n_depth_slots) * self.n_core
+
     def slot_core(self, r: int, l: int) -> int:
-        return self.n_prelude + r * self.n_core + l
+        return self.n_prelude + self.core_slot_base(r) + l
 
     def slot_coda(self, i: int) -> int:
-        return self.n_prelude + self.T_total * self.n_core + i
+        return self.n_prelude + self.n_depth_slots * self.n_core + i
 
     def n_params(self) -> int:
         d, Dh = self.d_model, self.head_dim
