@@ -39,6 +39,7 @@ varlen loop, restated in oracle/cpu_path.py) on the host cores, rank 0 only.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import datetime
 import json
 import os
@@ -119,6 +120,8 @@ def parse():
                          "cfg5: Bernoulli draft acceptance (default 0.8)")
     ap.add_argument("--scheduler", choices=["device", "host"], default="device",
                     help="cfg4: route / settle on the GPU (one graph per tick) or on the host")
+    ap.add_argument("--kv-budget", type=int, default=0,
+                    help="cfg4: KV-sharing budget s (core depth r keeps its K/V in slot r %% s); 0 = off")
     ap.add_argument("--batch-invariant", action="store_true",
                     help="cfg4 (device scheduler): fixed union capacities + batch-invariant attention "
                          "(bit-exact greedy equality with sequential decoding)")
@@ -601,7 +604,7 @@ def run_cfg4(args):
     from wavefront_decoding_b200.looped_lm import CONFIG4, LoopedLM
 
     from wavefront_decoding_b200.parallel import reduce_over_ranks, shard_range
-    cfg = CONFIG4
+    cfg = dataclasses.replace(CONFIG4, kv_budget_s=args.kv_budget)
     Bg = args.batch or CFG4["B"]
     s0, s1 = shard_range(Bg, world, rank)
     Bl = s1 - s0
@@ -695,6 +698,7 @@ def run_cfg4(args):
                    "global_batch": Bg, "batch_per_gpu": Bl if Bg % world == 0 else f"{Bg // world}-{-(-Bg // world)}",
                    "prompt_len": L, "new_tokens": new,
                    "T_draft": args.t_draft, "scheduler": args.scheduler, "batch_invariant": args.batch_invariant,
+                   "kv_budget_s": args.kv_budget,
                    "acceptance": "greedy gold == draft" if args.alpha is None else f"emulated Bernoulli({args.alpha})",
                    "parallelism": f"sequences sharded, {world} rank(s), no collective on the hot path",
                    "timing": "decode region per generation, CUDA events, max over ranks; "
