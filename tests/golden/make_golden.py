@@ -166,7 +166,7 @@ def gen_scheduler() -> dict:
     return out
 
 
-def gen_config1(n_new: int = 64, T_total: int = 4, drafts=(1, 2, 4), budgets=(2,), budget_drafts=(1, 2)) -> dict:
+def gen_config1(n_new: int = 64, T_total: int = 4, drafts=(1, 2, 4), budgets=(2, 1), budget_drafts=(1, 2)) -> dict:
     """Config 1: the reference's ParcaeBlocks on the fixture model, greedy, fp32,
     SDPA backend; AR (ar_baseline.py:132-193) and WFD (scheduler.py:89-225).
     With KV sharing (`kv_budget_s` = s < T_total, parcae_blocks.py:77-81,114-120:

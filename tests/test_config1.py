@@ -61,11 +61,13 @@ def test_kv_sharing_slot_map():
 
 
 def test_reference_kv_sharing_golden():
-    """The reference's own results with kv_budget_s = 2: WFD commits AR's tokens
+    """The reference's own results with kv_budget_s = 2 and 1: WFD commits AR's tokens
     on this fixture, the shared slots change the drafts (counters differ from the
     unshared run), and only the used slots exist (coda kept at its unshared index)."""
-    for d in (1, 2):
-        assert GOLD[f"wfd_d{d}_s2"]["tokens"] == GOLD["ar_s2"]["tokens"]
-    assert (GOLD["wfd_d1_s2"]["n_drafts_accepted"], GOLD["wfd_d2_s2"]["n_drafts_accepted"]) != \
-        (GOLD["wfd_d1"]["n_drafts_accepted"], GOLD["wfd_d2"]["n_drafts_accepted"])
+    for sb in (1, 2):
+        for d in (1, 2):
+            assert GOLD[f"wfd_d{d}_s{sb}"]["tokens"] == GOLD[f"ar_s{sb}"]["tokens"]
+        assert (GOLD[f"wfd_d1_s{sb}"]["n_drafts_accepted"], GOLD[f"wfd_d2_s{sb}"]["n_drafts_accepted"]) != \
+            (GOLD["wfd_d1"]["n_drafts_accepted"], GOLD["wfd_d2"]["n_drafts_accepted"])
     assert set(GOLD["ar_s2"]["seqlen"]) == {"0", "1", "2", "3", "4", "9"}
+    assert set(GOLD["ar_s1"]["seqlen"]) == {"0", "1", "2", "9"}

@@ -89,14 +89,16 @@ def test_device_config1_matches_reference(cuda_dev, T_draft):
     assert {str(s): lens[s][0] for s in range(len(lens))} == g["seqlen"]
 
 
+@pytest.mark.parametrize("s", [1, 2])
 @pytest.mark.parametrize("T_draft", [1, 2])
-def test_device_config1_kv_sharing_matches_reference(cuda_dev, T_draft):
-    """KV sharing (s = 2) with route / settle on the device: the reference's
+def test_device_config1_kv_sharing_matches_reference(cuda_dev, T_draft, s):
+    """KV sharing with route / settle on the device (the pre-tick kernel orders
+    each sequence's rows and forms the shared-slot windows): the reference's
     tokens, counters and slot lengths."""
     from wavefront_decoding_b200 import scheduler as sch
     from wavefront_decoding_b200.device_scheduler import generate_wavefront_device
-    eng, prompt, gold = _config1_engine(kv_budget_s=2)
-    g = gold[f"wfd_d{T_draft}_s2"]
+    eng, prompt, gold = _config1_engine(kv_budget_s=s)
+    g = gold[f"wfd_d{T_draft}_s{s}"]
     bt = generate_wavefront_device(eng, prompt, gold["n_new"], sch.SsdPolicy(gold["T_total"], T_draft))
     t = bt.per_seq[0]
     assert t.tokens == g["tokens"]

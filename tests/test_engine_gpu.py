@@ -164,24 +164,28 @@ def _seqlen_as_reference(eng):
     return {str(s if s < cfg.slot_coda(0) else s + shift): lens[s][0] for s in range(len(lens))}
 
 
-def test_config1_ar_kv_sharing_matches_reference(cuda_dev):
-    """KV-sharing budget s = 2 (core depth r keeps its K/V in slot r % 2): the
+@pytest.mark.parametrize("s", [1, 2])
+def test_config1_ar_kv_sharing_matches_reference(cuda_dev, s):
+    """KV-sharing budget s (core depth r keeps its K/V in slot r % s): the
     reference's AR tokens and slot lengths."""
     from wavefront_decoding_b200 import scheduler as sch
-    eng, prompt, gold = _config1_engine(kv_budget_s=2)
-    assert eng.cfg.n_slots == 6
+    eng, prompt, gold = _config1_engine(kv_budget_s=s)
+    assert eng.cfg.n_slots == 1 + 2 * s + 1
     bt = sch.ar_generate_batch(eng, prompt, gold["n_new"])
-    assert bt.per_seq[0].tokens == gold["ar_s2"]["tokens"]
-    assert _seqlen_as_reference(eng) == gold["ar_s2"]["seqlen"]
+    assert bt.per_seq[0].tokens == gold[f"ar_s{s}"]["tokens"]
+    assert _seqlen_as_reference(eng) == gold[f"ar_s{s}"]["seqlen"]
 
 
+@pytest.mark.parametrize("s", [1, 2])
 @pytest.mark.parametrize("T_draft", [1, 2])
-def test_config1_wfd_kv_sharing_matches_reference(cuda_dev, T_draft):
+def test_config1_wfd_kv_sharing_matches_reference(cuda_dev, T_draft, s):
     """KV sharing with the host scheduler: tokens, draft counters (they differ
-    from the unshared run's) and slot lengths of the reference."""
+    from the unshared run's) and slot lengths of the reference.  With s = 1 the
+    tokens of a sequence share one depth slot and each run of them is one
+    attention window."""
     from wavefront_decoding_b200 import scheduler as sch
-    eng, prompt, gold = _config1_engine(kv_budget_s=2)
-    g = gold[f"wfd_d{T_draft}_s2"]
+    eng, prompt, gold = _config1_engine(kv_budget_s=s)
+    g = gold[f"wfd_d{T_draft}_s{s}"]
     bt = sch.generate_wavefront_batch(eng, prompt, gold["n_new"], sch.SsdPolicy(gold["T_total"], T_draft), None)
     t = bt.per_seq[0]
     assert t.tokens == g["tokens"]

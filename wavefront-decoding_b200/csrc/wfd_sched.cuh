@@ -130,17 +130,40 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
   }
   const int total = s_cnt[kSchedThreads - 1];
   if (b < p.B && cnt > 0) {
-    int r = s_cnt[b] - cnt;
-    unsigned long long kk = 0;
-    for (int j = 0; j < p.W; ++j) {
+    // This sequence's live tokens in (depth slot, position) order.  A run of
+    // consecutive positions on one depth slot (KV sharing) becomes one window:
+    // its first row carries the run length in column 5 (the item's q_len), the
+    // other rows 0, so the shared slot prefix is read once per run
+    // (ouro_blocks_batch.py:184-205).  Without sharing every run is one token.
+    auto dslot = [&](int s) { return p.depth_slots > 0 ? p.step[s] % p.depth_slots : p.step[s]; };
+    int ord[kSchedMaxW];
+    int m = 0;
+    for (int j = 0; j < p.W && m < kSchedMaxW; ++j) {
       const int s = b * p.W + j;
       if (p.alive[s] && p.state[s] == 2) {
-        if (r < p.r_cap)
-          sched_fill_row(p.r_tab + (long long)r * 6, 6, p, 0, b, s,
-                         (p.depth_slots > 0 ? p.step[s] % p.depth_slots : p.step[s]) * p.n_core);
-        kk += (unsigned long long)(p.pos[s] + 1);
-        ++r;
+        int k = m++;
+        while (k > 0 && (dslot(ord[k - 1]) > dslot(s) ||
+                         (dslot(ord[k - 1]) == dslot(s) && p.pos[ord[k - 1]] > p.pos[s]))) {
+          ord[k] = ord[k - 1];
+          --k;
+        }
+        ord[k] = s;
       }
+    }
+    int r = s_cnt[b] - cnt;
+    unsigned long long kk = 0;
+    for (int i = 0; i < m;) {
+      int e = i + 1;
+      while (e < m && dslot(ord[e]) == dslot(ord[i]) && p.pos[ord[e]] == p.pos[ord[e - 1]] + 1) ++e;
+      for (int k = i; k < e; ++k, ++r) {
+        if (r < p.r_cap) {
+          int32_t* row = p.r_tab + (long long)r * 6;
+          sched_fill_row(row, 6, p, 0, b, ord[k], dslot(ord[k]) * p.n_core);
+          row[5] = k == i ? e - i : 0;
+        }
+      }
+      kk += (unsigned long long)(p.pos[ord[e - 1]] + 1);  // the run's window reads its slot prefix once
+      i = e;
     }
     atomicAdd(&s_keys[1], kk);
   }

@@ -116,6 +116,9 @@ class WaveEngine:
         # R gather + item table + scatter, C gather + final RMSNorm + greedy argmax.
         self._launches = {"P": 2 + 7 * cfg.n_prelude, "R": 3 + 6 * cfg.n_core, "C": 3 + 7 * cfg.n_coda}
         self._layers = {"P": cfg.n_prelude, "R": cfg.n_core, "C": cfg.n_coda}
+        # rows per R attention window: 1 without KV sharing; with sharing a run of
+        # one sequence's tokens on one depth slot (at most T_total + 2 tokens live)
+        self.r_max_q = 1 if cfg.n_depth_slots == cfg.T_total else cfg.T_total + 2
         self.kv_read_bytes = 0
         self.wfd_launches = 0
         self.d2h_bytes = 0
@@ -143,6 +146,30 @@ class WaveEngine:
     def _fill(self, kind: str, toks, seq_ids, rows) -> _Tables:
         cfg = self.cfg
         n = len(toks)
+        runs = None
+        if kind == "R":
+            # rows in (sequence, depth slot, position) order; a run of consecutive
+            # positions of one sequence on one depth slot (KV sharing) is one
+            # attention window: column 5 holds the run length on its first row and
+            # 0 on the others (ouro_blocks_batch.py:184-205).  Without sharing every
+            # run is a single token.
+            order = sorted(range(n), key=lambda i: (int(seq_ids[i]), cfg.core_slot_base(toks[i].step),
+                                                    toks[i].position))
+            toks = [toks[i] for i in order]
+            seq_ids = [seq_ids[i] for i in order]
+            rows = [rows[i] for i in order]
+            runs = [0] * n
+            i = 0
+            while i < n:
+                e = i + 1
+                while (e < n and seq_ids[e] == seq_ids[i]
+                       and cfg.core_slot_base(toks[e].step) == cfg.core_slot_base(toks[i].step)
+                       and toks[e].position == toks[e - 1].position + 1):
+                    e += 1
+                runs[i] = e - i
+                i = e
+            if max(runs, default=0) > self.r_max_q:
+                raise ValueError(f"R window of {max(runs)} rows exceeds {self.r_max_q}")
         cap = _bucket(n)
         t = self._tables.get((kind, cap))
         seg_slots = self._seg_layers(kind)
@@ -161,13 +188,19 @@ class WaveEngine:
         a[:n, 3] = seq_ids
         if kind == "R":
             a[:n, 4] = [cfg.core_slot_base(tk.step) for tk in toks]
-        a[:n, 5] = 1
+            a[:n, 5] = runs
+        else:
+            a[:n, 5] = 1
         for j, slot in enumerate(seg_slots):
             a[:, 6 + j] = (slot * (self.B + 1) + a[:, 3].astype(np.int64)) * self.S
         t.dev.copy_(t.host, non_blocking=True)
         t.uploaded.record()
         t.pending = True
-        keys = int(a[:n, 1].sum()) + n                      # k_len = position + 1 per live row
+        # K/V read: k_len = position + 1 of each window's last row (once per run)
+        if runs is None:
+            keys = int(a[:n, 1].sum()) + n
+        else:
+            keys = sum(int(a[i + runs[i] - 1, 1]) + 1 for i in range(n) if runs[i] > 0)
         self.kv_read_bytes += keys * self._layers[kind] * 2 * self._row_bytes
         self.wfd_launches += self._launches[kind]
         return t
@@ -216,7 +249,7 @@ class WaveEngine:
             fused.items_from_table(tab, 4, 3, 1, 5, t.items)   # (slot base, seq, position, live, row)
             for l, blk in enumerate(m.core):
                 q, k, v = m.qkv(blk, x, pos=tab[:, 1])
-                o = wa.wave_attn(q, k, v, self.cache.K, self.cache.V, t.items, 1, lens=self.cache.lens,
+                o = wa.wave_attn(q, k, v, self.cache.K, self.cache.V, t.items, self.r_max_q, lens=self.cache.lens,
                                  slot_offset=cfg.n_prelude + l)
                 x = m.finish_block(blk, x, o)
             fused.scatter_rows(x, rows, self.pool_h)
