@@ -163,6 +163,15 @@ def gen_scheduler() -> dict:
     prompts = gi.sched_prompts(gi.SCHED_CASES[0])
     bt = sb.ar_generate_batch(blocks, prompts, 12)
     out["ar_T4"] = gi.trace_summary(bt, blocks.last_cache)
+    for case in gi.DTV_CASES:
+        blocks = gi.FakeBlocks(case["T_total"])
+        prompts = gi.sched_prompts(case)
+        emus = None
+        if case["alpha"] is not None:
+            emus = [EmulatedAcceptance(case["alpha"], seed=200 + b) for b in range(case["B"])]
+        bt = sb.generate_dtv_batch(blocks, prompts, case["new"],
+                                   SsdPolicy(T_total=case["T_total"], T_draft=case["T_draft"]), case["K"], emus)
+        out[case["name"]] = gi.trace_summary(bt, blocks.last_cache)
     return out
 
 
@@ -234,12 +243,15 @@ def gen_config1(n_new: int = 64, T_total: int = 4, drafts=(1, 2, 4), budgets=(2,
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
-    ap.add_argument("--only", choices=["all", "config1"], default="all")
+    ap.add_argument("--only", choices=["all", "config1", "scheduler"], default="all")
     args = ap.parse_args()
     fa, BSK = import_reference(args.reference)
     if args.only in ("all", "config1"):
         (HERE / "reference_config1.json").write_text(json.dumps(gen_config1(), indent=0) + "\n")
     if args.only == "config1":
+        return
+    if args.only == "scheduler":
+        (HERE / "reference_scheduler.json").write_text(json.dumps(gen_scheduler(), indent=0) + "\n")
         return
     data = {}
     data.update(gen_attention(fa))

@@ -200,6 +200,14 @@ SCHED_CASES = [
 ]
 
 
+# draft-then-verify (scheduler_batch.py:378-501): K = draft_length drafts per round
+DTV_CASES = [
+    dict(name="dtv_T4_D1_K3_greedy", T_total=4, T_draft=1, K=3, B=3, L=7, new=24, alpha=None),
+    dict(name="dtv_T4_D2_K4_emu08", T_total=4, T_draft=2, K=4, B=3, L=5, new=20, alpha=0.8),
+    dict(name="dtv_T8_D2_K8_emu05", T_total=8, T_draft=2, K=8, B=4, L=6, new=20, alpha=0.5),
+]
+
+
 def sched_prompts(case) -> torch.Tensor:
     return torch.randint(0, 50, (case["B"], case["L"]), generator=gen(97))
 

@@ -154,6 +154,22 @@ def test_config1_wfd_matches_reference(cuda_dev, T_draft):
     assert {str(s): lens[s][0] for s in range(len(lens))} == g["seqlen"]
 
 
+@pytest.mark.parametrize("T_draft,K", [(1, 3), (2, 4), (2, 1)])
+def test_config1_dtv_is_lossless(cuda_dev, T_draft, K):
+    """Draft-then-verify on the engine (the verify union attends each sequence's
+    K + 1 sources as one window on their depth slot): greedy DtV commits the
+    reference's AR tokens, and the cache holds every depth's K / V of the
+    committed positions as sequential decoding would."""
+    from wavefront_decoding_b200 import scheduler as sch
+    eng, prompt, gold = _config1_engine()
+    bt = sch.generate_dtv_batch(eng, prompt, gold["n_new"], sch.SsdPolicy(gold["T_total"], T_draft), K)
+    t = bt.per_seq[0]
+    assert t.tokens == gold["ar"]["tokens"]
+    assert t.n_drafts_proposed > 0 and bt.r_union_max >= min(K + 1, 2)
+    if K == 3:
+        _check_cache_vs_oracle(eng, eng.model, prompt, bt.per_seq, 2e-4)
+
+
 def _seqlen_as_reference(eng):
     """The engine's slot lengths keyed like the reference's cache: with KV sharing
     ParcaeBlocks keeps its coda slots at n_prelude + T_total * n_core

@@ -1,7 +1,7 @@
 """Host-side scheduler logic vs the reference's own batch schedulers.
 
-The reference's `generate_wavefront_batch` / `ar_generate_batch`
-(scheduler_batch.py:185-362) were run on a deterministic stand-in for the model
+The reference's `generate_wavefront_batch` / `ar_generate_batch` /
+`generate_dtv_batch` (scheduler_batch.py:185-501) were run on a deterministic stand-in for the model
 blocks (golden_inputs.FakeBlocks); tests/golden/reference_scheduler.json holds
 their committed tokens, every per-sequence and batch counter and the rollback
 calls.  The restated scheduler must reproduce all of it exactly, and the
@@ -35,6 +35,30 @@ def test_wfd_matches_reference_trace(case):
     bt = sch.generate_wavefront_batch(blocks, gi.sched_prompts(case), case["new"],
                                       sch.SsdPolicy(T_total=case["T_total"], T_draft=case["T_draft"]), emus)
     assert gi.trace_summary(bt, blocks.last_cache) == GOLD[case["name"]]
+
+
+@pytest.mark.parametrize("case", gi.DTV_CASES, ids=[c["name"] for c in gi.DTV_CASES])
+def test_dtv_matches_reference_trace(case):
+    """Draft-then-verify (scheduler_batch.py:378-501): tokens, counters, union
+    sizes and rollback calls of the reference's own run."""
+    sch = _sched()
+    blocks = gi.FakeBlocks(case["T_total"])
+    emus = None
+    if case["alpha"] is not None:
+        emus = [sch.EmulatedAcceptance(case["alpha"], seed=200 + b) for b in range(case["B"])]
+    bt = sch.generate_dtv_batch(blocks, gi.sched_prompts(case), case["new"],
+                                sch.SsdPolicy(T_total=case["T_total"], T_draft=case["T_draft"]), case["K"], emus)
+    assert gi.trace_summary(bt, blocks.last_cache) == GOLD[case["name"]]
+
+
+def test_dtv_greedy_is_lossless():
+    """Greedy DtV commits the AR tokens (every committed token is a full-depth id)."""
+    sch = _sched()
+    prompts = gi.sched_prompts(gi.SCHED_CASES[0])
+    ar = sch.ar_generate_batch(gi.FakeBlocks(4), prompts, 20)
+    for K in (1, 3, 6):
+        bt = sch.generate_dtv_batch(gi.FakeBlocks(4), prompts, 20, sch.SsdPolicy(4, 2), K)
+        assert [t.tokens for t in bt.per_seq] == [t.tokens for t in ar.per_seq]
 
 
 def test_ar_matches_reference_trace():

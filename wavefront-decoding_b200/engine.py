@@ -127,6 +127,16 @@ class WaveEngine:
     def synchronize(self) -> None:
         torch.cuda.synchronize(self.device)
 
+    def ensure_window_rows(self, n: int) -> None:
+        """Let an R window (a run of one sequence's tokens on one depth slot)
+        hold up to n rows, e.g. the K + 1 sources of a draft-then-verify round.
+        Captured R graphs bake the bound in and are dropped when it grows."""
+        if n > self.r_max_q:
+            self.r_max_q = n
+            for (kind, _), t in self._tables.items():
+                if kind == "R":
+                    t.graph = None
+
     def drop_positions_at_and_after(self, b: int, position: int) -> None:
         self.cache.drop_positions_at_and_after(b, position)
 

@@ -12,6 +12,10 @@ Per tick: P union (tokens queued for the prelude) -> R union (one loop step for
 every live wave token) -> route (commit point: step == T_total -> verify; draft
 point: step == T_draft -> copy for a draft C) -> C union (greedy ids) -> settle
 (accept / reject cascade / rollback per sequence, new leading-edge draft).
+
+`generate_dtv_batch` is the reference's draft-then-verify scheduler
+(scheduler_batch.py:365-501): per sequence, rounds of K drafts at depth T_draft
+followed by one verify of all K + 1 sources at full depth.
 """
 from __future__ import annotations
 
@@ -113,6 +117,18 @@ class SeqState:
     active_p: list = field(default_factory=list)
     active_r: list = field(default_factory=list)
     active_c: list = field(default_factory=list)
+    # DtV round state (batch_state.py:38-49): phase "need_p" (the next source needs
+    # its prelude), "draft" (the current source runs steps 0..T_draft), "verify"
+    # (all K + 1 sources run T_draft..T_total), "idle" once done
+    phase: str = "need_p"
+    K: int = 0                 # drafts this round
+    j: int = 0                 # index of the current source (0..K)
+    sources: list = field(default_factory=list)
+    drafts: list = field(default_factory=list)
+    cur_tok: int = 0           # token forwarded as source j, and its position
+    cur_pos: int = 0
+    last_token: int = 0        # last committed token (the round's seed), and its position
+    p: int = 0
 
     def commit(self, token_id: int) -> None:
         self.committed.append(token_id)
@@ -133,6 +149,8 @@ class SeqState:
 
     def clear_working_state(self) -> None:
         self.active_p, self.active_r, self.active_c = [], [], []
+        self.sources, self.drafts = [], []
+        self.phase = "idle"
 
 
 @dataclass
@@ -364,3 +382,137 @@ def generate_wavefront_batch(blocks, prompt_ids, max_new_tokens: int, policy: Ss
             s.active_c = []
 
     return _finalize(bt, seqs, t0, blocks)
+
+
+# ---------------------------------------------------------------------------
+# draft-then-verify (scheduler_batch.py:365-501)
+# ---------------------------------------------------------------------------
+def _dtv_new_round(s: SeqState, max_new_tokens: int, draft_length: int) -> None:
+    """scheduler_batch.py:368-376: K = min(draft_length, tokens still to commit)
+    drafts, seeded by the last committed token."""
+    s.K = min(draft_length, max_new_tokens - len(s.committed))
+    s.j = 0
+    s.sources, s.drafts = [], []
+    s.cur_tok, s.cur_pos = s.last_token, s.p
+    s.phase = "need_p"
+
+
+def generate_dtv_batch(blocks, prompt_ids, max_new_tokens: int, policy: SsdPolicy, draft_length: int,
+                       emus: list | None = None) -> BatchTrace:
+    """Draft-then-verify over union P / R / C calls (scheduler_batch.py:378-501).
+
+    Each sequence runs rounds: source 0 is the last committed token; each source
+    goes through the prelude and T_draft loop steps, and its draft-depth greedy id
+    is the next source (draft d_{j+1}), K drafts per round.  Then all K + 1
+    sources advance together from T_draft to T_total (one window per sequence:
+    consecutive positions on one depth slot) and the full-depth ids verify the
+    drafts: accept while equal (emus[b] replaces the comparison), commit the
+    first gold on a reject and drop the cache from there, or commit the bonus
+    token when all K are accepted."""
+    bt = BatchTrace()
+    t0 = time.perf_counter()
+    cache, seqs = _prefill_and_first(blocks, prompt_ids, emus, max_new_tokens, bt, t0)
+    T_total, T_draft = policy.T_total, policy.T_draft
+    rows = getattr(blocks, "ensure_window_rows", None)
+    if rows is not None:
+        rows(draft_length + 1)   # the verify union attends K + 1 sources of a sequence as one window
+    for s in seqs:
+        if not s.done:
+            s.last_token, s.p = s.committed[-1], s.prefix_len
+            _dtv_new_round(s, max_new_tokens, draft_length)
+
+    ticks, max_ticks = 0, max_new_tokens * ((draft_length + 1) * max(T_draft, 1) + T_total + 4) + 100
+    while True:
+        alive = [s for s in seqs if not s.done]
+        if not alive:
+            break
+        ticks += 1
+        if ticks > max_ticks:
+            raise RuntimeError(f"dtv batch exceeded the tick guard ({max_ticks})")
+
+        # P: sequences whose next source needs its prelude
+        need = [s for s in alive if s.phase == "need_p"]
+        if need:
+            toks = []
+            for s in need:
+                t = ActiveToken(token_id=s.cur_tok, position=s.cur_pos, role="verify")
+                s.sources.append(t)
+                s.trace.n_p_calls += 1
+                s.phase = "draft"
+                toks.append(t)
+            blocks.prelude_union([s.idx for s in need], toks, cache)
+            bt.n_p_calls += 1
+
+        # R: a drafting sequence advances its current source, a verifying one all
+        # of its sources (until they reach full depth)
+        pairs, took = [], []
+        for s in alive:
+            if s.phase == "draft":
+                pairs.append((s, s.sources[-1]))
+                took.append(s)
+            elif s.phase == "verify" and s.sources[0].step < T_total:
+                pairs += [(s, t) for t in s.sources]
+                took.append(s)
+        if pairs:
+            blocks.advance_union([s.idx for s, _ in pairs], [t for _, t in pairs], cache)
+            _record_r(bt, len(pairs))
+            for s in took:
+                s.trace.n_r_calls += 1
+
+        # C: a draft (the current source reached T_draft) or the verify (all
+        # sources reached T_total)
+        entries = []
+        for s in alive:
+            if s.phase == "draft" and s.sources[-1].step == T_draft:
+                entries.append((s, "draft", [s.sources[-1]]))
+            elif s.phase == "verify" and s.sources[0].step == T_total:
+                entries.append((s, "verify", list(s.sources)))
+        if not entries:
+            continue
+        flat = [t for _, _, ts in entries for t in ts]
+        ids = blocks.coda_argmax_union([s.idx for s, _, ts in entries for _ in ts], flat, cache)
+        bt.n_c_calls += 1
+        k = 0
+        for s, kind, ts in entries:
+            out = [int(x) for x in ids[k:k + len(ts)]]
+            k += len(ts)
+            s.trace.n_c_calls += 1
+            if kind == "draft":
+                if s.j < s.K:
+                    s.drafts.append(out[0])          # d_{j+1}, at cur_pos + 1
+                s.cur_tok, s.cur_pos = out[0], s.cur_pos + 1
+                s.j += 1
+                s.phase = "need_p" if s.j <= s.K else "verify"
+                continue
+            # verify: source p + i predicts position p + i + 1
+            rejected = False
+            for i in range(s.K):
+                s.trace.n_drafts_proposed += 1
+                accept = s.emu.draw() if s.emu is not None else out[i] == s.drafts[i]
+                if accept:
+                    s.trace.n_drafts_accepted += 1
+                    s.commit(s.drafts[i])
+                    if len(s.committed) >= max_new_tokens:
+                        s.done = True
+                        break
+                else:
+                    s.trace.n_drafts_rejected += 1
+                    s.trace.n_rollback_events += 1
+                    rejected = True
+                    s.commit(out[i])
+                    cache.drop_positions_at_and_after(s.idx, s.p + i + 1)
+                    s.last_token, s.p = out[i], s.p + i + 1
+                    if len(s.committed) >= max_new_tokens:
+                        s.done = True
+                    break
+            if not rejected and not s.done:
+                s.commit(out[s.K])                   # every draft accepted: the bonus token
+                s.last_token, s.p = out[s.K], s.p + s.K + 1
+                if len(s.committed) >= max_new_tokens:
+                    s.done = True
+            if s.done:
+                s.clear_working_state()
+            else:
+                _dtv_new_round(s, max_new_tokens, draft_length)
+    return _finalize(bt, seqs, t0, blocks)
+
