@@ -118,8 +118,10 @@ def parse():
     ap.add_argument("--alpha", type=float, default=None,
                     help="cfg4: emulated draft acceptance rate (default: greedy gold == draft); "
                          "cfg5: Bernoulli draft acceptance (default 0.8)")
-    ap.add_argument("--scheduler", choices=["device", "host"], default="device",
-                    help="cfg4: route / settle on the GPU (one graph per tick) or on the host")
+    ap.add_argument("--scheduler", choices=["device", "host", "dtv"], default="device",
+                    help="cfg4: wavefront with route / settle on the GPU (one graph per tick) or on the host, "
+                         "or draft-then-verify (host)")
+    ap.add_argument("--draft-length", type=int, default=8, help="cfg4 with --scheduler dtv: drafts per round")
     ap.add_argument("--kv-budget", type=int, default=0,
                     help="cfg4: KV-sharing budget s (core depth r keeps its K/V in slot r %% s); 0 = off")
     ap.add_argument("--batch-invariant", action="store_true",
@@ -637,6 +639,8 @@ def run_cfg4(args):
             ev_all0.record()
             if dwave is not None:
                 bt = dwave.generate(prompts, emus)
+            elif args.scheduler == "dtv":
+                bt = sch.generate_dtv_batch(eng, prompts, new, policy, args.draft_length, emus)
             else:
                 bt = sch.generate_wavefront_batch(eng, prompts, new, policy, emus)
             ev_end.record()
@@ -698,6 +702,7 @@ def run_cfg4(args):
                    "global_batch": Bg, "batch_per_gpu": Bl if Bg % world == 0 else f"{Bg // world}-{-(-Bg // world)}",
                    "prompt_len": L, "new_tokens": new,
                    "T_draft": args.t_draft, "scheduler": args.scheduler, "batch_invariant": args.batch_invariant,
+                   "draft_length": args.draft_length if args.scheduler == "dtv" else None,
                    "kv_budget_s": args.kv_budget,
                    "acceptance": "greedy gold == draft" if args.alpha is None else f"emulated Bernoulli({args.alpha})",
                    "parallelism": f"sequences sharded, {world} rank(s), no collective on the hot path",
