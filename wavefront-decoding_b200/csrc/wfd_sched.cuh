@@ -135,15 +135,18 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
     // its first row carries the run length in column 5 (the item's q_len), the
     // other rows 0, so the shared slot prefix is read once per run
     // (ouro_blocks_batch.py:184-205).  Without sharing every run is one token.
-    auto dslot = [&](int s) { return p.depth_slots > 0 ? p.step[s] % p.depth_slots : p.step[s]; };
+    // Without sharing the live tokens of a sequence have distinct steps, so every
+    // run is one token and the rows keep token-slot order.
+    const bool shared = p.depth_slots > 0 && p.depth_slots < p.T_total;
+    auto dslot = [&](int s) { return shared ? p.step[s] % p.depth_slots : p.step[s]; };
     int ord[kSchedMaxW];
     int m = 0;
     for (int j = 0; j < p.W && m < kSchedMaxW; ++j) {
       const int s = b * p.W + j;
       if (p.alive[s] && p.state[s] == 2) {
         int k = m++;
-        while (k > 0 && (dslot(ord[k - 1]) > dslot(s) ||
-                         (dslot(ord[k - 1]) == dslot(s) && p.pos[ord[k - 1]] > p.pos[s]))) {
+        while (shared && k > 0 && (dslot(ord[k - 1]) > dslot(s) ||
+                                   (dslot(ord[k - 1]) == dslot(s) && p.pos[ord[k - 1]] > p.pos[s]))) {
           ord[k] = ord[k - 1];
           --k;
         }
@@ -154,7 +157,7 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
     unsigned long long kk = 0;
     for (int i = 0; i < m;) {
       int e = i + 1;
-      while (e < m && dslot(ord[e]) == dslot(ord[i]) && p.pos[ord[e]] == p.pos[ord[e - 1]] + 1) ++e;
+      while (shared && e < m && dslot(ord[e]) == dslot(ord[i]) && p.pos[ord[e]] == p.pos[ord[e - 1]] + 1) ++e;
       for (int k = i; k < e; ++k, ++r) {
         if (r < p.r_cap) {
           int32_t* row = p.r_tab + (long long)r * 6;

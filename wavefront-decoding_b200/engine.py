@@ -163,11 +163,12 @@ class WaveEngine:
             # attention window: column 5 holds the run length on its first row and
             # 0 on the others (ouro_blocks_batch.py:184-205).  Without sharing every
             # run is a single token.
-            order = sorted(range(n), key=lambda i: (int(seq_ids[i]), cfg.core_slot_base(toks[i].step),
-                                                    toks[i].position))
-            toks = [toks[i] for i in order]
-            seq_ids = [seq_ids[i] for i in order]
-            rows = [rows[i] for i in order]
+            slot_of = [(int(seq_ids[i]), cfg.core_slot_base(toks[i].step)) for i in range(n)]
+            if len(set(slot_of)) < n:   # some sequence has several tokens on one depth slot
+                order = sorted(range(n), key=lambda i: (slot_of[i], toks[i].position))
+                toks = [toks[i] for i in order]
+                seq_ids = [seq_ids[i] for i in order]
+                rows = [rows[i] for i in order]
             runs = [0] * n
             i = 0
             while i < n:
