@@ -49,8 +49,10 @@ def _bucket(n: int) -> int:
 class _Tables:
     """Device tables of one (kind, bucket) and their pinned staging copy.
     int32 columns: 0 pool row, 1 position, 2 token id, 3 cache sequence,
-    4 R: slot base (depth slot * n_core), 5 live (q_len 1) / padding (0),
-    6.. prelude / coda layers: first cache row of the row's (slot, sequence)."""
+    4 R: slot base (depth slot * n_core), P / C: 0, 5 live (q_len 1; R: the
+    window's row count on its first row, 0 on the others) / padding (0),
+    6.. prelude / coda layers: first cache row of the row's (slot, sequence) (the
+    device scheduler's table layout; the bodies address slots by item tables)."""
 
     def __init__(self, kind: str, cap: int, n_cols: int, device):
         self.kind = kind
@@ -59,21 +61,10 @@ class _Tables:
         self.host = torch.zeros((cap, n_cols), dtype=torch.int32).pin_memory()
         self.dev = torch.zeros((cap, n_cols), dtype=torch.int32, device=device)
         self.items = torch.zeros((cap, 5), dtype=torch.int32, device=device)
-        self.row_ids = torch.arange(cap, dtype=torch.int32, device=device)
-        self.ones = torch.ones(cap, dtype=torch.int32, device=device)
         self.out = torch.zeros(cap, dtype=torch.int32, device=device)
         self.graph = None
         self.uploaded = torch.cuda.Event()   # the staging copy may be rewritten once this fired
         self.pending = False
-        self._consts: dict[int, torch.Tensor] = {}
-
-    def const(self, v: int) -> torch.Tensor:
-        """A (cap,) int32 column of v, made once (first use is an eager warm-up, before any capture)."""
-        c = self._consts.get(v)
-        if c is None:
-            c = self.ones * v
-            self._consts[v] = c
-        return c
 
 
 class WaveEngine:
@@ -90,8 +81,6 @@ class WaveEngine:
         self.cache = SlotKVCache(cfg.n_slots, batch_size + 1, cfg.n_kv_heads, cfg.head_dim, max_seq_len, model.dtype,
                                  model.device)
         self.scratch_seq = batch_size
-        self.Kflat = self.cache.K.view(-1, cfg.n_kv_heads, cfg.head_dim)
-        self.Vflat = self.cache.V.view(-1, cfg.n_kv_heads, cfg.head_dim)
         # state pool: live tokens are at most B * (T_total / T_draft + 2) per tick;
         # round-robin reuse over this many rows never recycles a live row
         self.pool_cap = batch_size * 2 * (cfg.T_total + 8)
@@ -109,12 +98,11 @@ class WaveEngine:
         # accounting (host side, exact): K/V bytes the attention of live rows
         # reads, libwfd kernel launches, bytes read back per C union
         self._row_bytes = cfg.n_kv_heads * cfg.head_dim * torch.finfo(model.dtype).bits // 8
-        # every libwfd kernel a body launches.  Per prelude / coda layer: 2 RMSNorm,
-        # RoPE split, append, plan, segment attention, SwiGLU gate; per core layer:
-        # 2 RMSNorm, RoPE split, plan (with the window append), attention (tcgen05 or
-        # the fused CUDA-core decode), SwiGLU gate.  Per body: P gather + scatter,
-        # R gather + item table + scatter, C gather + final RMSNorm + greedy argmax.
-        self._launches = {"P": 2 + 7 * cfg.n_prelude, "R": 3 + 6 * cfg.n_core, "C": 3 + 7 * cfg.n_coda}
+        # every libwfd kernel a body launches.  Per layer: 2 RMSNorm, RoPE split,
+        # plan (with the window append), attention (tcgen05 or CUDA-core), SwiGLU
+        # gate.  Per body: P gather + item table + scatter, R gather + item table +
+        # scatter, C gather + item table + final RMSNorm + greedy argmax.
+        self._launches = {"P": 3 + 6 * cfg.n_prelude, "R": 3 + 6 * cfg.n_core, "C": 4 + 6 * cfg.n_coda}
         self._layers = {"P": cfg.n_prelude, "R": cfg.n_core, "C": cfg.n_coda}
         # rows per R attention window: 1 without KV sharing; with sharing a run of
         # one sequence's tokens on one depth slot (at most T_total + 2 tokens live)
@@ -232,28 +220,25 @@ class WaveEngine:
 
     # ------------------------------------------------------------------
     # device-side bodies (captured into graphs)
-    def _segment_block(self, blk, x, t: _Tables, j: int, slot: int, cols: torch.Tensor, k_len: torch.Tensor):
-        """Prelude / coda layer: append every row, then attend with segments.
-        cols: the table transposed (n_cols, cap), so each column is contiguous;
-        k_len = position + 1."""
+    def _segment_block(self, blk, x, t: _Tables, slot: int):
+        """Prelude / coda layer: one wave_attn over the body's item table with the
+        layer's slot as the offset.  Several rows of a sequence may share the
+        slot (the C union's commit and draft rows): every row's K / V is appended
+        before any row attends."""
         m = self.model
         q, k, v = m.qkv(blk, x, pos=t.dev[:, 1])
-        self.cache.write_tokens(t.const(slot), cols[3], cols[1], k, v)
-        o = wa.attn_segments(q, self.Kflat, self.Vflat, t.row_ids, cols[5], cols[6 + j], k_len, 1, causal=False)
+        o = wa.wave_attn(q, k, v, self.cache.K, self.cache.V, t.items, 1, lens=self.cache.lens, slot_offset=slot)
         return m.finish_block(blk, x, o)
 
     def _body(self, kind: str, t: _Tables) -> None:
         m, cfg = self.model, self.cfg
         tab = t.dev
         rows = tab[:, 0]
-        if kind != "R":
-            # one transpose (and one add) per body instead of a copy per strided column per layer
-            cols = tab.t().contiguous()
-            k_len = cols[1] + 1
         if kind == "P":
             x = fused.gather_rows(m.embed, tab[:, 2])
+            fused.items_from_table(tab, 4, 3, 1, 5, t.items)   # (0, seq, position, live, row)
             for j, blk in enumerate(m.prelude):
-                x = self._segment_block(blk, x, t, j, cfg.slot_prelude(j), cols, k_len)
+                x = self._segment_block(blk, x, t, cfg.slot_prelude(j))
             fused.scatter_rows(x, rows, self.pool_e, zero=self.pool_h)
         elif kind == "R":
             x = fused.gather_rows(self.pool_h, rows, b=self.pool_e)
@@ -266,8 +251,9 @@ class WaveEngine:
             fused.scatter_rows(x, rows, self.pool_h)
         else:
             x = fused.gather_rows(self.pool_h, rows)
+            fused.items_from_table(tab, 4, 3, 1, 5, t.items)
             for j, blk in enumerate(m.coda):
-                x = self._segment_block(blk, x, t, j, cfg.slot_coda(j), cols, k_len)
+                x = self._segment_block(blk, x, t, cfg.slot_coda(j))
             m.greedy_ids(x, t.out)
 
     def _run(self, kind: str, t: _Tables) -> None:
