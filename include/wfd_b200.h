@@ -35,7 +35,9 @@
 extern "C" {
 #endif
 
-#define WFD_ABI_VERSION 1
+/* Raised whenever a declaration or a struct layout below changes
+ * (2: wfd_sched_params.depth_slots). */
+#define WFD_ABI_VERSION 2
 
 enum wfd_status {
   WFD_OK = 0,

@@ -43,6 +43,9 @@ class wfd_item(ctypes.Structure):
                 ("q_len", ctypes.c_int32), ("q_row0", ctypes.c_int32)]
 
 
+ABI_VERSION = 2  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
+
+
 class wfd_sched_params(ctypes.Structure):
     """include/wfd_b200.h: wfd_sched_params (field order and types must match)."""
     _fields_ = [(n, ctypes.c_void_p) for n in (
@@ -127,6 +130,9 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
+        if lib.wfd_abi_version() != ABI_VERSION:
+            raise ImportError(f"{LIB_PATH} has ABI version {lib.wfd_abi_version()}, these bindings expect "
+                              f"{ABI_VERSION}: rebuild it (`python wavefront-decoding_b200/build.py`)")
         _lib = lib
     return _lib
 

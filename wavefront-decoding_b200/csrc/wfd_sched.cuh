@@ -93,18 +93,24 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
     s_keys[0] = s_keys[1] = 0ull;
   }
   __syncthreads();
+  // This sequence's token slots are read once, all loads independent: bit j of
+  // `live` = slot j in the wave, of `queued` = slot j queued for the prelude.
   int cnt = 0;
+  uint32_t live = 0;
   if (b < p.B) {
     int32_t* prow = p.p_tab + (long long)b * p.p_cols;
     int pj = -1;
     if (!p.done[b]) {
+      uint32_t queued = 0;
+#pragma unroll 4
       for (int j = 0; j < p.W; ++j) {
         const int s = b * p.W + j;
-        if (p.alive[s] && p.state[s] == 1) {
-          if (pj >= 0) set_error(p.err, kErrSched);
-          pj = s;
-        }
+        const int a = p.alive[s], st = p.state[s];
+        if (a && st == 2) live |= 1u << j;
+        if (a && st == 1) queued |= 1u << j;
       }
+      if (__popc(queued) > 1) set_error(p.err, kErrSched);
+      if (queued) pj = b * p.W + (31 - __clz(queued));  // the last queued slot
     }
     if (pj >= 0) {
       p.state[pj] = 2;
@@ -112,11 +118,11 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
       sched_fill_row(prow, p.p_cols, p, p.p_slot0, b, pj, 0);
       s_any_p = 1;
       atomicAdd(&s_keys[0], (unsigned long long)(p.pos[pj] + 1));
+      live |= 1u << (pj - b * p.W);
     } else {
       sched_pad_row(prow, p.p_cols, p, p.p_slot0);
     }
-    if (!p.done[b])
-      for (int j = 0; j < p.W; ++j) cnt += (p.alive[b * p.W + j] && p.state[b * p.W + j] == 2) ? 1 : 0;
+    cnt = __popc(live);
     if (cnt > 0) p.seq_ct[b * kSeqCounters + kCtR] += 1;
   }
   s_cnt[b] = cnt;
@@ -134,38 +140,40 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
     // consecutive positions on one depth slot (KV sharing) becomes one window:
     // its first row carries the run length in column 5 (the item's q_len), the
     // other rows 0, so the shared slot prefix is read once per run
-    // (ouro_blocks_batch.py:184-205).  Without sharing every run is one token.
-    // Without sharing the live tokens of a sequence have distinct steps, so every
-    // run is one token and the rows keep token-slot order.
+    // (ouro_blocks_batch.py:184-205).  Without sharing the live tokens of a
+    // sequence have distinct steps, so every run is one token and the rows keep
+    // token-slot order.
     const bool shared = p.depth_slots > 0 && p.depth_slots < p.T_total;
-    auto dslot = [&](int s) { return shared ? p.step[s] % p.depth_slots : p.step[s]; };
-    int ord[kSchedMaxW];
+    int ord[kSchedMaxW], dsl[kSchedMaxW], psn[kSchedMaxW];
     int m = 0;
-    for (int j = 0; j < p.W && m < kSchedMaxW; ++j) {
-      const int s = b * p.W + j;
-      if (p.alive[s] && p.state[s] == 2) {
-        int k = m++;
-        while (shared && k > 0 && (dslot(ord[k - 1]) > dslot(s) ||
-                                   (dslot(ord[k - 1]) == dslot(s) && p.pos[ord[k - 1]] > p.pos[s]))) {
-          ord[k] = ord[k - 1];
-          --k;
-        }
-        ord[k] = s;
+    for (uint32_t bits = live; bits; bits &= bits - 1) {
+      const int s = b * p.W + (__ffs(bits) - 1);
+      const int d = shared ? p.step[s] % p.depth_slots : p.step[s];
+      const int ps = p.pos[s];
+      int k = m++;
+      while (shared && k > 0 && (dsl[k - 1] > d || (dsl[k - 1] == d && psn[k - 1] > ps))) {
+        ord[k] = ord[k - 1];
+        dsl[k] = dsl[k - 1];
+        psn[k] = psn[k - 1];
+        --k;
       }
+      ord[k] = s;
+      dsl[k] = d;
+      psn[k] = ps;
     }
     int r = s_cnt[b] - cnt;
     unsigned long long kk = 0;
     for (int i = 0; i < m;) {
       int e = i + 1;
-      while (shared && e < m && dslot(ord[e]) == dslot(ord[i]) && p.pos[ord[e]] == p.pos[ord[e - 1]] + 1) ++e;
+      while (shared && e < m && dsl[e] == dsl[i] && psn[e] == psn[e - 1] + 1) ++e;
       for (int k = i; k < e; ++k, ++r) {
         if (r < p.r_cap) {
           int32_t* row = p.r_tab + (long long)r * 6;
-          sched_fill_row(row, 6, p, 0, b, ord[k], dslot(ord[k]) * p.n_core);
+          sched_fill_row(row, 6, p, 0, b, ord[k], dsl[k] * p.n_core);
           row[5] = k == i ? e - i : 0;
         }
       }
-      kk += (unsigned long long)(p.pos[ord[e - 1]] + 1);  // the run's window reads its slot prefix once
+      kk += (unsigned long long)(psn[e - 1] + 1);  // the run's window reads its slot prefix once
       i = e;
     }
     atomicAdd(&s_keys[1], kk);
@@ -200,9 +208,16 @@ __global__ void __launch_bounds__(kSchedThreads) sched_route_kernel(const SchedP
   if (b < p.B) {
     int vs = -1, ds = -1;
     if (!p.done[b]) {
+      // the sequence's slots in the wave, read once (independent loads)
+      uint32_t wave = 0;
+#pragma unroll 4
       for (int j = 0; j < p.W; ++j) {
         const int s = b * p.W + j;
-        if (!(p.alive[s] && p.state[s] == 2)) continue;
+        const int a = p.alive[s], st = p.state[s];
+        if (a && st == 2) wave |= 1u << j;
+      }
+      for (uint32_t bits = wave; bits; bits &= bits - 1) {
+        const int s = b * p.W + (__ffs(bits) - 1);
         const int st = ++p.step[s];
         if (st == p.T_total) {
           if (vs >= 0) set_error(p.err, kErrSched);
@@ -234,23 +249,6 @@ __global__ void __launch_bounds__(kSchedThreads) sched_route_kernel(const SchedP
   }
 }
 
-__device__ __forceinline__ bool sched_queue(const SchedParams& p, int b, int token, int position) {
-  for (int j = 0; j < p.W; ++j) {
-    const int s = b * p.W + j;
-    if (!p.alive[s]) {
-      p.alive[s] = 1;
-      p.state[s] = 1;
-      p.tok[s] = token;
-      p.pos[s] = position;
-      p.step[s] = 0;
-      p.seq_ct[b * kSeqCounters + kCtP] += 1;
-      return true;
-    }
-  }
-  set_error(p.err, kErrSched);
-  return false;
-}
-
 __device__ __forceinline__ void sched_commit(const SchedParams& p, int b, int token) {
   const int n = p.n_commit[b];
   if (n < p.max_new) p.committed[(long long)b * p.max_new + n] = token;
@@ -259,27 +257,61 @@ __device__ __forceinline__ void sched_commit(const SchedParams& p, int b, int to
 }
 
 // Settle: accept / reject the commit point's successor, cascade rollback, queue
-// the next token and the new leading-edge draft.  One thread per sequence.
+// the next token and the new leading-edge draft.  One thread per sequence; the
+// sequence's token slots are read once and updated in registers.
 __global__ void __launch_bounds__(kSchedThreads) sched_settle_kernel(const SchedParams p) {
   griddep_wait();  // launched with programmatic stream serialization (no early trigger)
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= p.B || p.done[b]) return;
   const int vs = p.c_slot[2 * b], ds = p.c_slot[2 * b + 1];
   int32_t* ct = p.seq_ct + b * kSeqCounters;
+  const int base = b * p.W;
+  uint32_t alive = 0, wave = 0;  // bit j: slot j alive / alive and in the wave
+  int pos[kSchedMaxW];
+#pragma unroll 4
+  for (int j = 0; j < p.W; ++j) {
+    const int a = p.alive[base + j], st = p.state[base + j];
+    pos[j] = p.pos[base + j];
+    if (a) alive |= 1u << j;
+    if (a && st == 2) wave |= 1u << j;
+  }
+  const uint32_t all = p.W >= 32 ? 0xffffffffu : ((1u << p.W) - 1u);
+  auto drop = [&](int j) {
+    p.alive[base + j] = 0;
+    p.state[base + j] = 0;
+    alive &= ~(1u << j);
+    wave &= ~(1u << j);
+  };
+  // queue a token for the prelude in the first free slot (sched order of the host)
+  auto queue = [&](int token, int position) {
+    const uint32_t free_slots = ~alive & all;
+    if (!free_slots) {
+      set_error(p.err, kErrSched);
+      return;
+    }
+    const int j = __ffs(free_slots) - 1, s = base + j;
+    p.alive[s] = 1;
+    p.state[s] = 1;
+    p.tok[s] = token;
+    p.pos[s] = position;
+    p.step[s] = 0;
+    alive |= 1u << j;
+    pos[j] = position;
+    ct[kCtP] += 1;
+  };
   bool rejected = false;
   if (vs >= 0) {
     const int gold = p.c_out[2 * b];
-    p.alive[vs] = 0;
-    p.state[vs] = 0;
-    const int next_pos = p.pos[vs] + 1;
+    const int next_pos = pos[vs - base] + 1;
+    drop(vs - base);
     int nxt = -1;
-    for (int j = 0; j < p.W; ++j) {
-      const int s = b * p.W + j;
-      if (p.alive[s] && p.state[s] == 2 && p.pos[s] == next_pos) nxt = s;
+    for (uint32_t bits = wave; bits; bits &= bits - 1) {
+      const int j = __ffs(bits) - 1;
+      if (pos[j] == next_pos) nxt = base + j;
     }
     if (nxt < 0) {  // boundary: nothing speculated at next_pos
       sched_commit(p, b, gold);
-      if (!p.done[b]) sched_queue(p, b, gold, next_pos);
+      if (!p.done[b]) queue(gold, next_pos);
       else ct[kCtP] += 1;  // the host queues it before noticing the sequence is done
     } else {
       bool accept;
@@ -299,30 +331,27 @@ __global__ void __launch_bounds__(kSchedThreads) sched_settle_kernel(const Sched
         ct[kCtRoll] += 1;
         rejected = true;
         sched_commit(p, b, gold);
-        for (int j = 0; j < p.W; ++j) {  // rollback: every token at or after next_pos
-          const int s = b * p.W + j;
-          if (p.alive[s] && p.pos[s] >= next_pos) {
-            p.alive[s] = 0;
-            p.state[s] = 0;
-          }
+        for (uint32_t bits = alive; bits; bits &= bits - 1) {  // rollback: every token at or after next_pos
+          const int j = __ffs(bits) - 1;
+          if (pos[j] >= next_pos) drop(j);
         }
         for (int k = 0; k < p.n_kv_slots; ++k) {
           int32_t* l = p.lens + (long long)k * p.lens_stride + b;
           if (*l > next_pos) *l = next_pos;
         }
-        if (!p.done[b]) sched_queue(p, b, gold, next_pos);
+        if (!p.done[b]) queue(gold, next_pos);
         else ct[kCtP] += 1;
       }
     }
   }
   if (p.done[b]) {  // finished: drop the working state (clear_working_state)
     for (int j = 0; j < p.W; ++j) {
-      p.alive[b * p.W + j] = 0;
-      p.state[b * p.W + j] = 0;
+      p.alive[base + j] = 0;
+      p.state[base + j] = 0;
     }
     return;
   }
-  if (!rejected && ds >= 0) sched_queue(p, b, p.c_out[2 * b + 1], p.pos[ds] + 1);
+  if (!rejected && ds >= 0) queue(p.c_out[2 * b + 1], pos[ds - base] + 1);
 }
 
 }  // namespace wfd
