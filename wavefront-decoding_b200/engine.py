@@ -46,6 +46,33 @@ def _bucket(n: int) -> int:
     raise ValueError(f"union of {n} rows exceeds the largest bucket {_BUCKETS[-1]}")
 
 
+def r_windows(seq_ids: list, slot_bases: list, positions: list):
+    """Attention windows of an R union (ouro_blocks_batch.py:184-205).
+
+    Rows of one sequence on one depth slot (KV sharing, or the sources of a
+    draft-then-verify round) are reordered by (sequence, slot, position), and a
+    run of consecutive positions becomes one bottom-right-causal window.
+    Returns (order, runs): order is None when no sequence has two rows on one
+    slot (rows keep their order), else the row permutation; runs[i] is the
+    window's row count on its first row and 0 on the others."""
+    n = len(seq_ids)
+    key = list(zip(seq_ids, slot_bases))
+    order = None
+    if len(set(key)) < n:
+        order = sorted(range(n), key=lambda i: (key[i], positions[i]))
+        key = [key[i] for i in order]
+        positions = [positions[i] for i in order]
+    runs = [0] * n
+    i = 0
+    while i < n:
+        e = i + 1
+        while e < n and key[e] == key[i] and positions[e] == positions[e - 1] + 1:
+            e += 1
+        runs[i] = e - i
+        i = e
+    return order, runs
+
+
 class _Tables:
     """Device tables of one (kind, bucket) and their pinned staging copy.
     int32 columns: 0 pool row, 1 position, 2 token id, 3 cache sequence,
@@ -146,27 +173,12 @@ class WaveEngine:
         n = len(toks)
         runs = None
         if kind == "R":
-            # rows in (sequence, depth slot, position) order; a run of consecutive
-            # positions of one sequence on one depth slot (KV sharing) is one
-            # attention window: column 5 holds the run length on its first row and
-            # 0 on the others (ouro_blocks_batch.py:184-205).  Without sharing every
-            # run is a single token.
-            slot_of = [(int(seq_ids[i]), cfg.core_slot_base(toks[i].step)) for i in range(n)]
-            if len(set(slot_of)) < n:   # some sequence has several tokens on one depth slot
-                order = sorted(range(n), key=lambda i: (slot_of[i], toks[i].position))
+            order, runs = r_windows([int(x) for x in seq_ids], [cfg.core_slot_base(tk.step) for tk in toks],
+                                    [tk.position for tk in toks])
+            if order is not None:
                 toks = [toks[i] for i in order]
                 seq_ids = [seq_ids[i] for i in order]
                 rows = [rows[i] for i in order]
-            runs = [0] * n
-            i = 0
-            while i < n:
-                e = i + 1
-                while (e < n and seq_ids[e] == seq_ids[i]
-                       and cfg.core_slot_base(toks[e].step) == cfg.core_slot_base(toks[i].step)
-                       and toks[e].position == toks[e - 1].position + 1):
-                    e += 1
-                runs[i] = e - i
-                i = e
             if max(runs, default=0) > self.r_max_q:
                 raise ValueError(f"R window of {max(runs)} rows exceeds {self.r_max_q}")
         cap = _bucket(n)
