@@ -27,8 +27,11 @@
 //               O^T accumulated in registers with the online-softmax rescale
 // The persistent grid splits the flattened (segment, query group, kv head,
 // key) space into equal key shares exactly like the CUDA-core kernel; units
-// that straddle CTAs are merged by the last CTA to arrive.  Every wait is
-// bounded and reports through the error word; no multicast, no cluster launch.
+// that straddle CTAs are merged by the last CTA to arrive.  A CTA starts from
+// its 64-byte start record (first segment, its bounds, its Seg), written by the
+// plan kernel, and every role keeps the current segment in registers.  Every
+// wait is bounded and reports through the error word; no multicast, no cluster
+// launch.
 //
 // Head pairs (head_dim 64): with `pair` set, a unit is two consecutive kv heads
 // of a head_dim-64 cache read as one 128-dim head (the two 64-dim boxes are the
@@ -39,9 +42,9 @@
 // head_dim 128: the tensor-core issue rate, not the HBM, bounds a 64-dim tile.
 //
 // Window keys are read from the KV cache: the window rows are appended by the
-// plan kernel's extra blocks in the launch before this one.  Launched with programmatic
-// stream serialization: barrier set-up and the TMEM allocation overlap the
-// previous kernel; griddep_wait() precedes every read of its outputs.
+// plan kernel's extra blocks in the launch before this one.  Launched with
+// programmatic stream serialization: barrier set-up and the TMEM allocation
+// overlap the previous kernel; griddep_wait() precedes every read of its outputs.
 #pragma once
 
 #include <cuda.h>
