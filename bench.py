@@ -70,12 +70,14 @@ CFG5 = dict(B=64, R=16, H=32, Hkv=8, Dh=128, L0=32768, W=8, seed=5, alpha=0.8)
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # timed attention kernel, from the ncu captures summarised under profiles/
 # (wave_decode_cfg2.md for the CUDA-core kernel, wave_tc_cfg2.md / wave_tc_cfg3.md /
-# wave_tc_cfg4attn.md for tcgen05).
-# cfg3 was captured at batch 8 and scaled by the units processed (x4 at batch 32).
+# wave_tc_cfg4attn.md / wave_tc_cfg5.md for tcgen05).
+# cfg3 was captured at batch 8 and cfg5 at batch 2, scaled by the units processed
+# (x4 to batch 32, x32 to batch 64).
 NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
                      ("cfg2", "tc"): 543_152_128 + 4_816_384,
-                     ("cfg3", "tc"): (2_189_340_160 + 8_944_640) * 4,
-                     ("cfg4attn", "tc"): 3_631_393_536 + 6_166_272}
+                     ("cfg3", "tc"): (2_189_589_504 + 9_263_104) * 4,
+                     ("cfg4attn", "tc"): 3_631_393_536 + 6_166_272,
+                     ("cfg5", "tc"): (4_314_130_176 + 6_834_176) * 32}
 
 
 def ncu_traffic(workload: str, tc: bool, c: dict):
