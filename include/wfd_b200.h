@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-/* Raised whenever a declaration or a struct layout below changes
+/* Raised whenever a declaration or a struct layout below changes incompatibly
  * (2: wfd_sched_params.depth_slots). */
 #define WFD_ABI_VERSION 2
 
@@ -301,6 +301,10 @@ typedef struct {
   int32_t p_slot0, n_prelude, c_slot0, n_coda;
   int32_t depth_slots; /* core depth slots: T_total, or the KV-sharing budget s (depth r -> slot r % s) */
 } wfd_sched_params;
+
+/* sizeof(wfd_sched_params) as compiled into the library: a host that mirrors the
+ * struct (ctypes, cgo, JNI) checks its layout against it. */
+size_t wfd_sched_params_bytes(void);
 
 /* Before the P union: queue -> wave for each sequence's queued token (P table
  * row b), compacted R table of every live token.  B <= 1024, W <= 32. */

@@ -47,9 +47,11 @@ def test_abi_version_and_status_strings(lib):
     assert b"workspace" in lib.wfd_status_string(3)
 
 
-def test_item_struct_layout():
+def test_item_struct_layout(lib):
     from wavefront_decoding_b200 import _abi
     assert ctypes.sizeof(_abi.wfd_item) == 20
+    # the ctypes mirror of the scheduler parameters matches the compiled struct
+    assert ctypes.sizeof(_abi.wfd_sched_params) == lib.wfd_sched_params_bytes()
 
 
 def test_product_does_not_import_oracle():

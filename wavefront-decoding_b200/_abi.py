@@ -25,7 +25,7 @@ EXPORTED = (
     "wfd_write_prefill", "wfd_commit_drop", "wfd_commit_window", "wfd_gather_pack",
     "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul", "wfd_gather_rows", "wfd_scatter_rows",
     "wfd_items_from_table", "wfd_argmax_rows",
-    "wfd_sched_pre_tick", "wfd_sched_route", "wfd_sched_settle",
+    "wfd_sched_pre_tick", "wfd_sched_route", "wfd_sched_settle", "wfd_sched_params_bytes",
     "wfd_set_batch_invariant", "wfd_get_batch_invariant",
 )
 
@@ -64,6 +64,7 @@ _S = ctypes.c_size_t
 
 _SIGS = {
     "wfd_abi_version": ([], _I),
+    "wfd_sched_params_bytes": ([], _S),
     "wfd_status_string": ([_I], ctypes.c_char_p),
     "wfd_read_error": ([_P, _P, _P], _I),
     "wfd_workspace_bytes": ([_I, _I, _I], _S),

@@ -923,6 +923,8 @@ static_assert(offsetof(wfd_sched_params, n_coda) == offsetof(wfd::SchedParams, n
 static_assert(offsetof(wfd_sched_params, depth_slots) == offsetof(wfd::SchedParams, depth_slots),
               "wfd_sched_params layout");
 
+extern "C" size_t wfd_sched_params_bytes(void) { return sizeof(wfd_sched_params); }
+
 namespace {
 int sched_check(const wfd_sched_params* p) {
   if (!p) return WFD_ERR_INVALID_ARG;
