@@ -53,6 +53,17 @@ def test_device_matches_host_emulated(cuda_dev, alpha, T_draft):
     assert sum(x[6] for x in d[1]) > 0          # rollbacks exercised
 
 
+@pytest.mark.parametrize("s,alpha,T_draft", [(1, 0.6, 1), (1, 0.8, 2), (2, 0.5, 1)])
+def test_device_matches_host_kv_sharing(cuda_dev, s, alpha, T_draft):
+    """KV sharing under emulated acceptance (many rollbacks): the pre-tick kernel's
+    ordering of each sequence's rows and its shared-slot windows reproduce the host
+    scheduler's tables exactly (tokens, counters, union sizes, KV lengths)."""
+    cfg = _small_cfg(n_kv_heads=4, kv_budget_s=s)
+    h, d, _ = _both(cfg, 5, 9, 30, T_draft, alpha=alpha)
+    assert d == h
+    assert sum(x[6] for x in d[1]) > 0          # rollbacks exercised
+
+
 def test_device_cache_matches_oracle(cuda_dev):
     cfg = _small_cfg()
     _, _, (model, eng, prompts, bt) = _both(cfg, 2, 10, 14, 2)
