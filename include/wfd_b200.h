@@ -92,6 +92,16 @@ int wfd_read_error(int32_t* d_err, int32_t* h_err, void* stream);
 int wfd_set_batch_invariant(int32_t on);
 int wfd_get_batch_invariant(void);
 
+/* Test hook (process-wide): iterations of one bounded mbarrier wait of the
+ * tcgen05 attention kernel before it gives up.  iterations >= 0 sets the limit
+ * (0: every wait gives up at once), < 0 restores the default (2^20, a
+ * multi-second ceiling).  A wait that gives up sets bit 1 of the error word
+ * (WFD_ERR_DEVICE_TIMEOUT from wfd_read_error); the kernel then stops issuing
+ * copies and MMAs, waits (with the default bound) for the ones in flight, frees
+ * its tensor memory and returns, and its outputs are undefined.  Read when a
+ * launch is built.  No counterpart in the reference. */
+int wfd_set_wait_limit(int32_t iterations);
+
 /* Bytes of device workspace the attention entry points need for up to
  * `max_items` work items / segments.  The workspace must be zero-filled once
  * after allocation (wfd_workspace_init); the kernels leave it zeroed again. */
@@ -126,24 +136,25 @@ int wfd_wave_attn(const void* q, const void* k_new, const void* v_new, void* k_c
                   void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream);
 
 /* wfd_wave_attn without a caller-supplied workspace, for callers that cannot
- * allocate device memory when they call: code that runs while a CUDA graph is
- * being captured without having reserved a buffer first, serving runtimes
- * that fix their memory plan at start-up and must not allocate (an allocation
- * can synchronise the device or fail under memory pressure mid-request), and
- * foreign-language hosts with no device allocator of their own.  Has no
- * counterpart in the reference.
+ * allocate device memory when they call: serving runtimes that fix their
+ * memory plan at start-up and must not allocate per request (an allocation can
+ * synchronise the device or fail under memory pressure mid-request), and
+ * foreign-language hosts that hold raw device pointers but have no device
+ * allocator of their own.  Has no counterpart in the reference.
  *
  * The scratch memory is a fixed array inside the library (5.5 MB on every
  * device that loads the library, held until the process exits).  Limits:
  * bf16 tensors, head_dim 128 (the tcgen05 kernel), at most 4096 items, at
- * most 160 SMs; anything else returns WFD_ERR_UNSUPPORTED or
- * WFD_ERR_WORKSPACE before launching.  The first call on a device looks up the
- * array's device address (once per device, with that device current), so make
- * that first call before any stream capture.  Every call shares the one array:
- * each call clears the part that must start at zero, but calls that overlap on
- * the GPU (different streams, or different threads racing on one stream)
- * corrupt each other's results.  Allocates nothing: no cudaMalloc, no
- * allocating library routine.  Arguments as wfd_wave_attn. */
+ * most 160 SMs, fewer than 2^31 cache rows; anything else returns
+ * WFD_ERR_UNSUPPORTED or WFD_ERR_WORKSPACE, and every host-side argument check
+ * runs before anything is queued on the stream.  The first call on a device,
+ * whatever its arguments, looks up the array's device address (once per
+ * device, with that device current), so make that first call before any
+ * stream capture.  Every call shares the one array: each call clears the part
+ * that must start at zero, but calls that overlap on the GPU (different
+ * streams, or different threads racing on one stream) corrupt each other's
+ * results.  Allocates nothing: no cudaMalloc, no allocating library routine.
+ * Arguments as wfd_wave_attn. */
 int wfd_wave_attn_static(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
                          void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
                          int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,

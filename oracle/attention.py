@@ -34,7 +34,8 @@ def _segment(q: np.ndarray, k: np.ndarray, v: np.ndarray, limits: np.ndarray, sc
     qg = q.reshape(sq, Hkv, G, Dh).transpose(1, 2, 0, 3)            # (Hkv, G, sq, Dh)
     kt = k.transpose(1, 0, 2)                                        # (Hkv, sk, Dh)
     vt = v.transpose(1, 0, 2)
-    s = np.einsum("hgqd,hkd->hgqk", qg, kt) * scale                  # (Hkv, G, sq, sk)
+    # batched matrix products per kv head (BLAS), float64
+    s = np.matmul(qg.reshape(Hkv, G * sq, Dh), kt.transpose(0, 2, 1)).reshape(Hkv, G, sq, sk) * scale
     mask = np.arange(sk)[None, :] <= limits[:, None]                 # (sq, sk)
     s = np.where(mask[None, None], s, -np.inf)
     m = s.max(axis=-1, keepdims=True)
@@ -42,7 +43,7 @@ def _segment(q: np.ndarray, k: np.ndarray, v: np.ndarray, limits: np.ndarray, sc
     p = np.exp(s - m)
     p = np.where(mask[None, None], p, 0.0)
     l = p.sum(axis=-1, keepdims=True)
-    o = np.einsum("hgqk,hkd->hgqd", p, vt) / np.where(l > 0, l, 1.0)
+    o = np.matmul(p.reshape(Hkv, G * sq, sk), vt).reshape(Hkv, G, sq, Dh) / np.where(l > 0, l, 1.0)
     return o.transpose(2, 0, 1, 3).reshape(sq, H, Dh)                # (sq, H, Dh)
 
 

@@ -402,3 +402,40 @@ def test_tc_more_items_than_staged_and_append_blocks(cuda_dev):
             assert int(lens[slot, seq]) == p0 + ql
     assert torch.equal(Kh[0, 7], K[0, 7])
     assert int(lens[0, 7]) == 0
+
+
+def test_tc_bounded_wait_gives_up_and_next_launch_is_exact(cuda_dev):
+    """Every bounded wait of the tcgen05 kernel is made to give up at once (wait
+    limit 0, a test hook): the launch still returns, the error word reports a
+    timeout (WFD_ERR_DEVICE_TIMEOUT), and the next launches with the default
+    limit, on the same workspace, are exact — the aborted launch drained its
+    copies and MMAs and left the split-K arrival counters zeroed."""
+    from wavefront_decoding_b200 import runtime as rt
+    from wavefront_decoding_b200._abi import WfdError
+    rng = np.random.default_rng(5)
+    n_slots, B, S, H, Hkv = 3, 8, 1500, 16, 4
+    items = []
+    for r in range(n_slots):
+        for b in range(B):
+            ql = 1 if (r + b) % 2 else 8
+            items.append([r, b, int(rng.integers(200, S - 8)), ql, 0])
+    row = 0
+    for it in items:
+        it[4] = row
+        row += it[3]
+    K, V, q, kn, vn = _wave_case(55, n_slots, B, S, H, Hkv, 128, items, torch.bfloat16)
+    ref, o = _oracle_wave(K, V, q, kn, vn, items)
+    assert rt.read_device_error(cuda_dev) == 0
+    rt.set_wait_limit(0)
+    try:
+        _run_wave(cuda_dev, K, V, q, kn, vn, items, 8, kernel=1)
+    finally:
+        rt.set_wait_limit(None)
+    with pytest.raises(WfdError) as err:
+        rt.read_device_error(cuda_dev)
+    assert err.value.status == 16
+    for _ in range(2):
+        out, Kd, Vd, lens = _run_wave(cuda_dev, K, V, q, kn, vn, items, 8, kernel=1)
+        no_device_error(cuda_dev)
+        assert maxdiff(out, ref) < TOL_BF16
+        assert maxdiff(Kd, o.K) == 0.0 and maxdiff(Vd, o.V) == 0.0

@@ -26,7 +26,7 @@ EXPORTED = (
     "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul", "wfd_gather_rows", "wfd_scatter_rows",
     "wfd_items_from_table", "wfd_argmax_rows",
     "wfd_sched_pre_tick", "wfd_sched_route", "wfd_sched_settle", "wfd_sched_params_bytes",
-    "wfd_set_batch_invariant", "wfd_get_batch_invariant",
+    "wfd_set_batch_invariant", "wfd_get_batch_invariant", "wfd_set_wait_limit",
 )
 
 
@@ -104,6 +104,7 @@ _SIGS = {
     "wfd_argmax_rows": ([_P, _P, _I, _I, _I, _P], _I),
     "wfd_set_batch_invariant": ([_I], _I),
     "wfd_get_batch_invariant": ([], _I),
+    "wfd_set_wait_limit": ([_I], _I),
     # const wfd_sched_params*, stream
     "wfd_sched_pre_tick": ([_P, _P], _I),
     "wfd_sched_route": ([_P, _P], _I),

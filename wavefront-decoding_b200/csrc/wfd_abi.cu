@@ -29,6 +29,9 @@ constexpr int kMaxDevices = 64;
 // Batch-invariant attention (wfd_set_batch_invariant): read when a launch is
 // built, so a captured CUDA graph keeps the mode it was captured with.
 std::atomic<int> g_batch_invariant{0};
+// Per-wait spin limit of the tensor-core kernel (wfd_set_wait_limit): kSpinLimit
+// unless a test lowers it to make the waits run out.  Read when a launch is built.
+std::atomic<uint32_t> g_spin_limit{kSpinLimit};
 constexpr int kGridPerSm = 4;  // upper bound on resident decode CTAs per SM used for sizing
 
 struct DevInfo {
@@ -381,6 +384,7 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     vp.ws_part = reinterpret_cast<float*>(ws + L.part);
     vp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
     vp.err = A.err;
+    vp.spin_limit = g_spin_limit.load(std::memory_order_relaxed);
     return launch_verify(NQ, verify_active(NQ, Gv, max_q), vp, A.k, A.v, A.key_rows, A.Hkv, A.Dh, pair ? 128 : A.Dh,
                          sms, st);
   }
@@ -408,15 +412,30 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   return launch_decode(A.dtype, A.Dh, NQ, dp, sms, st);
 }
 
+// Host-side checks of a slot-table call that need no device data (the ones
+// run_attention would otherwise make after the plan has been queued).
+int wave_validate(const void* q, const void* k_new, const void* v_new, const void* k_cache, const void* v_cache,
+                  const void* out, const wfd_item* items, int32_t n_items, int32_t slot_offset, int32_t n_rows,
+                  int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_heads, int32_t n_kv_heads) {
+  if (!items || !k_new || !v_new || !k_cache || !v_cache || !q || !out || n_items < 0) return WFD_ERR_INVALID_ARG;
+  if (n_slots <= 0 || n_seqs <= 0 || max_seq <= 0 || n_rows < 0) return WFD_ERR_INVALID_ARG;
+  if (slot_offset < 0 || slot_offset >= n_slots) return WFD_ERR_INVALID_ARG;
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(out) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(k_new) ||
+      !aligned16(v_new))
+    return WFD_ERR_ALIGNMENT;
+  return WFD_OK;
+}
+
 int wave_common(int which, const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
                 void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
                 int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
                 int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
                 void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream) {
   if (n_items == 0) return WFD_OK;  // empty tick: nothing to append or attend
-  if (!items || !k_new || !v_new || !k_cache || !v_cache || n_items < 0) return WFD_ERR_INVALID_ARG;
-  if (n_slots <= 0 || n_seqs <= 0 || max_seq <= 0 || n_rows < 0) return WFD_ERR_INVALID_ARG;
-  if (slot_offset < 0 || slot_offset >= n_slots) return WFD_ERR_INVALID_ARG;
+  const int rc = wave_validate(q, k_new, v_new, k_cache, v_cache, out, items, n_items, slot_offset, n_rows, n_slots,
+                               n_seqs, max_seq, n_heads, n_kv_heads);
+  if (rc != WFD_OK) return rc;
   AttnArgs A;
   memset(&A, 0, sizeof(A));
   A.mode = kPlanSlots;
@@ -517,14 +536,22 @@ int wfd_wave_attn_static(const void* q, const void* k_new, const void* v_new, vo
                          int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
                          int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
                          int32_t* d_err, void* stream) {
+  // first, whatever the arguments: the array's device address on this device,
+  // so that a first call of any shape (an empty one included) does the lookup
+  void* ws = static_ws_device_ptr();
+  if (ws == nullptr) return WFD_ERR_CUDA;
   if (dtype != WFD_DTYPE_BF16 || head_dim != 128) return WFD_ERR_UNSUPPORTED;
   if (n_items < 0 || n_items > kStaticMaxItems) return WFD_ERR_WORKSPACE;
   const int sms = current_sms();
   if (sms <= 0) return WFD_ERR_CUDA;
   if (sms > kStaticMaxSms) return WFD_ERR_WORKSPACE;
   if (n_items == 0) return WFD_OK;
-  void* ws = static_ws_device_ptr();
-  if (ws == nullptr) return WFD_ERR_CUDA;
+  // every host-side check before the first thing is queued on the stream: a
+  // rejected call leaves the stream untouched
+  const int rc = wave_validate(q, k_new, v_new, k_cache, v_cache, out, items, n_items, slot_offset, n_rows, n_slots,
+                               n_seqs, max_seq, n_heads, n_kv_heads);
+  if (rc != WFD_OK) return rc;
+  if ((long long)n_slots * n_seqs * (long long)max_seq >= (1ll << 31)) return WFD_ERR_UNSUPPORTED;
   const WsLayout L = ws_layout(n_items, head_dim, sms, true);
   if (L.total > kStaticWsBytes) return WFD_ERR_WORKSPACE;
   // the split-K arrival counters must start at zero; the array keeps whatever
@@ -558,6 +585,11 @@ int wfd_set_batch_invariant(int32_t on) {
 }
 
 int wfd_get_batch_invariant(void) { return g_batch_invariant.load(); }
+
+int wfd_set_wait_limit(int32_t iterations) {
+  g_spin_limit.store(iterations < 0 ? kSpinLimit : (uint32_t)iterations);
+  return WFD_OK;
+}
 
 int wfd_read_error(int32_t* d_err, int32_t* h_err, void* stream) {
   if (!d_err || !h_err) return WFD_ERR_INVALID_ARG;

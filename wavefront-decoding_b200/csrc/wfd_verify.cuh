@@ -77,6 +77,9 @@ struct VerifyParams {
   float* ws_part;
   int* ws_cnt;
   int* err;
+  // iterations of one bounded wait before it gives up (kSpinLimit unless a
+  // test lowers it to make the waits run out)
+  uint32_t spin_limit;
 };
 
 template <int NQP, int DH>
@@ -197,10 +200,11 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float (&v)[32]) {
 // flag) or as soon as another role has aborted.  After an abort the roles keep
 // their control flow (same loop trips, same named barriers) but issue no more
 // TMA or MMA work, so nothing in the CTA can block without a bound.
-__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                        uint32_t limit) {
   bool ok = false;
   if (!*abort_flag) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    for (uint32_t i = 0; i < limit; ++i) {
       if (mbar_try_wait(bar, parity)) {
         ok = true;
         break;
@@ -345,6 +349,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   __shared__ __align__(8) uint64_t bar_ofree;
   __shared__ __align__(8) uint64_t bar_qready[2];  // unit's Q^T written (producer)
   __shared__ __align__(8) uint64_t bar_qfree[2];   // unit's S MMAs done with its Q^T (MMA commit)
+  __shared__ __align__(8) uint64_t bar_drain;      // every MMA of the CTA complete (final MMA commit)
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
   __shared__ int s_flag;
@@ -367,6 +372,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       mbar_init(&bar_qready[s], 1);
       mbar_init(&bar_qfree[s], 1);
     }
+    mbar_init(&bar_drain, 1);
     fence_mbar_init();
     s_abort = 0;
   }
@@ -442,6 +448,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
     int u, r_lo, r_hi;
     long long ustart;
     uint32_t it = 0, units = 0;
+    uint32_t n_iss = 0;  // tiles whose TMA loads were issued (a prefix of the sequence: issue stops at an abort)
     while (itr.next(p, S, u, r_lo, r_hi, ustart)) {
       const int h = u % p.Hkv, qg = u / p.Hkv;
       const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
@@ -449,7 +456,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
 
       for (int t = 0; t < n_t; ++t, ++it) {
         const int stage = (int)(it % STAGES);
-        const bool go = (it >= (uint32_t)STAGES) ? tc_wait(&bar_empty[stage], ((it / STAGES) - 1) & 1u, &s_abort, p.err)
+        const bool go = (it >= (uint32_t)STAGES) ? tc_wait(&bar_empty[stage], ((it / STAGES) - 1) & 1u, &s_abort, p.err, p.spin_limit)
                                                  : !s_abort;
         if (go && lane == 0) {
           unsigned char* dst = kvs + stage * C::KV_STAGE;
@@ -462,6 +469,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
             tma_load_3d(dst + bx * C::BOX_BYTES, &tm_k, cx, ch, row, &bar_full[stage]);
             tma_load_3d(dst + (KB + bx) * C::BOX_BYTES, &tm_v, cx, ch, row, &bar_full[stage]);
           }
+          n_iss = it + 1;
         }
         __syncwarp();
         if (t == 0) {
@@ -473,7 +481,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
           {
             const int qb = (int)(units & 1u);
             const bool qgo =
-                units >= 2 ? tc_wait(&bar_qfree[qb], ((units >> 1) - 1) & 1u, &s_abort, p.err) : !s_abort;
+                units >= 2 ? tc_wait(&bar_qfree[qb], ((units >> 1) - 1) & 1u, &s_abort, p.err, p.spin_limit) : !s_abort;
             if (qgo) {
               const int nvh = S.q_len * p.G;
               const int nvec = (p.pair ? 2 * nvh : nvh) - qg * NQP;
@@ -511,10 +519,19 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
     // the MMA warp's last commits arrive on these barriers: see them land
     // before this CTA may exit
     for (uint32_t k = (units > 2 ? units - 2 : 0); k < units; ++k)
-      tc_wait(&bar_qfree[k & 1u], (k >> 1) & 1u, &s_abort, p.err);
+      tc_wait(&bar_qfree[k & 1u], (k >> 1) & 1u, &s_abort, p.err, p.spin_limit);
     const uint32_t n_used = it;
     for (uint32_t j = (n_used > (uint32_t)STAGES ? n_used - STAGES : 0); j < n_used; ++j)
-      tc_wait(&bar_empty[j % STAGES], (j / STAGES) & 1u, &s_abort, p.err);
+      tc_wait(&bar_empty[j % STAGES], (j / STAGES) & 1u, &s_abort, p.err, p.spin_limit);
+    // Copies in flight must land before the CTA exits, also after an abort (which
+    // skips the waits above): wait, with the fixed bound and whatever the abort
+    // flag says, for the last phase of every stage this lane filled.  Earlier
+    // phases of a stage completed before it was refilled.
+    if (lane == 0) {
+      for (uint32_t j = (n_iss > (uint32_t)STAGES ? n_iss - STAGES : 0); j < n_iss; ++j)
+        if (!mbar_wait_bounded(&bar_full[j % STAGES], (j / STAGES) & 1u)) set_error(p.err, kErrTimeout);
+    }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     UnitIter itr = make_iter();
@@ -530,15 +547,15 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
       const int qb = (int)(units & 1u);
       const uint32_t qa = q_addr + (uint32_t)(qb * C::Q_BYTES);
-      tc_wait(&bar_qready[qb], (units >> 1) & 1u, &s_abort, p.err);
+      tc_wait(&bar_qready[qb], (units >> 1) & 1u, &s_abort, p.err, p.spin_limit);
       tc_fence_after();
       for (int t = 0; t <= n_t; ++t) {
         if (t < n_t) {
           const uint32_t ti = it + t;
           const int stage = (int)(ti % STAGES);
           const int sb = (int)(ti & 1u);
-          bool go = tc_wait(&bar_full[stage], (ti / STAGES) & 1u, &s_abort, p.err);
-          if (ti >= 2) go = tc_wait(&bar_sfree[sb], ((ti >> 1) - 1) & 1u, &s_abort, p.err) && go;
+          bool go = tc_wait(&bar_full[stage], (ti / STAGES) & 1u, &s_abort, p.err, p.spin_limit);
+          if (ti >= 2) go = tc_wait(&bar_sfree[sb], ((ti >> 1) - 1) & 1u, &s_abort, p.err, p.spin_limit) && go;
           tc_fence_after();
           if (go && lane == 0) {
             const uint32_t k_addr = smem_u32(kvs + stage * C::KV_STAGE);
@@ -556,8 +573,8 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
           __syncwarp();
         }
         if (t >= 1) {
-          bool go = tc_wait(&bar_pfull, pv & 1u, &s_abort, p.err);
-          if (pv >= 1) go = tc_wait(&bar_ofree, (pv - 1) & 1u, &s_abort, p.err) && go;
+          bool go = tc_wait(&bar_pfull, pv & 1u, &s_abort, p.err, p.spin_limit);
+          if (pv >= 1) go = tc_wait(&bar_ofree, (pv - 1) & 1u, &s_abort, p.err, p.spin_limit) && go;
           tc_fence_after();
           const uint32_t tp = it + t - 1;
           const int stage = (int)(tp % STAGES);
@@ -580,6 +597,14 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       it += n_t;
       ++units;
     }
+    // Every MMA this lane issued must be complete before TMEM is freed and the
+    // CTA exits, also after an abort (whose consumers stop waiting for them):
+    // one last commit tracks all of them.
+    if (lane == 0) {
+      umma_commit(&bar_drain);
+      if (!mbar_wait_bounded(&bar_drain, 0)) set_error(p.err, kErrTimeout);
+    }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax warps
     // 4 * H2 warps: warp w reads TMEM lane quadrant w % 4 (32 keys of S^T, then 32
@@ -618,7 +643,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       for (int t = 0; t < n_t; ++t) {
         const uint32_t ti = it + t;
         const int sb = (int)(ti & 1u);
-        tc_wait(&bar_sfull[sb], (ti >> 1) & 1u, &s_abort, p.err);
+        tc_wait(&bar_sfull[sb], (ti >> 1) & 1u, &s_abort, p.err, p.spin_limit);
         tc_fence_after();
         float s[LW];
         tmem_ld<LW>(tq + (uint32_t)(sb * NQP + col0), s);
@@ -686,7 +711,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         // the previous tile's P.V: its MMA is done once o_full fires, which also
         // frees the P^T buffer.  oacc holds O_{t-2} already rescaled to m_{t-1}.
         if (t >= 1) {
-          tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err);
+          tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err, p.spin_limit);
           tc_fence_after();
           float o[LW];
           tmem_ld<LW>(tq + (uint32_t)(2 * NQP + col0), o);
@@ -758,7 +783,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         if (stid == 0) mbar_arrive(&bar_pfull);
       }
       {
-        tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err);
+        tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err, p.spin_limit);
         tc_fence_after();
         float o[LW];
         tmem_ld<LW>(tq + (uint32_t)(2 * NQP + col0), o);

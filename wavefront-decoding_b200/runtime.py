@@ -128,3 +128,9 @@ class batch_invariant:
     def __exit__(self, *exc):
         set_batch_invariant(self.old)
 
+
+
+def set_wait_limit(iterations: int | None) -> None:
+    """Test hook: iterations of one bounded wait of the tcgen05 attention kernel
+    before it gives up and reports a timeout (None restores the default)."""
+    _abi.check(_abi.load().wfd_set_wait_limit(-1 if iterations is None else int(iterations)), "wfd_set_wait_limit")
