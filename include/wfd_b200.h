@@ -36,8 +36,8 @@ extern "C" {
 #endif
 
 /* Raised whenever a declaration or a struct layout below changes incompatibly
- * (2: wfd_sched_params.depth_slots). */
-#define WFD_ABI_VERSION 2
+ * (2: wfd_sched_params.depth_slots; 3: wfd_commit_window takes n_rows). */
+#define WFD_ABI_VERSION 3
 
 enum wfd_status {
   WFD_OK = 0,
@@ -92,15 +92,14 @@ int wfd_read_error(int32_t* d_err, int32_t* h_err, void* stream);
 int wfd_set_batch_invariant(int32_t on);
 int wfd_get_batch_invariant(void);
 
-/* Test hook (process-wide): iterations of one bounded mbarrier wait of the
- * tcgen05 attention kernel before it gives up.  iterations >= 0 sets the limit
- * (0: every wait gives up at once), < 0 restores the default (2^20, a
- * multi-second ceiling).  A wait that gives up sets bit 1 of the error word
- * (WFD_ERR_DEVICE_TIMEOUT from wfd_read_error); the kernel then stops issuing
- * copies and MMAs, waits (with the default bound) for the ones in flight, frees
- * its tensor memory and returns, and its outputs are undefined.  Read when a
- * launch is built.  No counterpart in the reference. */
-int wfd_set_wait_limit(int32_t iterations);
+/* Test hook (process-wide, default off): on != 0 makes every CTA of the tcgen05
+ * attention kernel give up right after issuing its first K/V copies, as it does
+ * when a bounded mbarrier wait runs out (2^20 polls, a multi-second ceiling):
+ * bit 1 of the error word is set (WFD_ERR_DEVICE_TIMEOUT from wfd_read_error),
+ * the CTA stops issuing copies and MMAs, waits (with the normal bound) for the
+ * ones in flight, frees its tensor memory and returns; outputs are undefined.
+ * Read when a launch is built.  No counterpart in the reference. */
+int wfd_test_fail_waits(int32_t on);
 
 /* Bytes of device workspace the attention entry points need for up to
  * `max_items` work items / segments.  The workspace must be zero-filled once
@@ -223,11 +222,14 @@ int wfd_commit_drop(int32_t* lens, const int32_t* drop_pos, int32_t n_slots, int
  * rows are compacted in place to positions pos0, pos0+1, ... of the slot (a
  * no-op when they already form a prefix), lens[slot+slot_offset][seq] is set to
  * pos0 + n_accepted, acc_rows[q_row0 + k] receives the q row of the k-th
- * accepted row and acc_count[i] the count (either output may be NULL). */
+ * accepted row and acc_count[i] the count (either output may be NULL).
+ * n_rows: entries of accept_mask / acc_rows (q rows); an item whose window rows
+ * fall outside [0, n_rows) is skipped and reported in the error word. */
 int wfd_commit_window(void* k_cache, void* v_cache, int32_t* lens, const wfd_item* items, int32_t n_items,
                       const int32_t* accept_len, const uint8_t* accept_mask, int32_t* acc_rows,
-                      int32_t* acc_count, int32_t slot_offset, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
-                      int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t* d_err, void* stream);
+                      int32_t* acc_count, int32_t n_rows, int32_t slot_offset, int32_t n_slots, int32_t n_seqs,
+                      int32_t max_seq, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t* d_err,
+                      void* stream);
 
 /* Gather packed prefixes, BatchStaticKVCache.gather_pack (batch_kv_cache.py:75-96):
  * segment i copies positions [0, uptos[i]] of (slots[i], seqs[i]) into rows

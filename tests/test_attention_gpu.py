@@ -405,11 +405,11 @@ def test_tc_more_items_than_staged_and_append_blocks(cuda_dev):
 
 
 def test_tc_bounded_wait_gives_up_and_next_launch_is_exact(cuda_dev):
-    """Every bounded wait of the tcgen05 kernel is made to give up at once (wait
-    limit 0, a test hook): the launch still returns, the error word reports a
-    timeout (WFD_ERR_DEVICE_TIMEOUT), and the next launches with the default
-    limit, on the same workspace, are exact — the aborted launch drained its
-    copies and MMAs and left the split-K arrival counters zeroed."""
+    """Every CTA of the tcgen05 kernel is made to give up as a wait that ran out
+    would, with its first K/V copies in flight (a test hook): the launch still
+    returns, the error word reports a timeout (WFD_ERR_DEVICE_TIMEOUT), and the
+    next launches, on the same workspace, are exact — the aborted launch drained
+    its copies and MMAs and left the split-K arrival counters zeroed."""
     from wavefront_decoding_b200 import runtime as rt
     from wavefront_decoding_b200._abi import WfdError
     rng = np.random.default_rng(5)
@@ -426,11 +426,11 @@ def test_tc_bounded_wait_gives_up_and_next_launch_is_exact(cuda_dev):
     K, V, q, kn, vn = _wave_case(55, n_slots, B, S, H, Hkv, 128, items, torch.bfloat16)
     ref, o = _oracle_wave(K, V, q, kn, vn, items)
     assert rt.read_device_error(cuda_dev) == 0
-    rt.set_wait_limit(0)
+    rt.test_fail_waits(True)
     try:
         _run_wave(cuda_dev, K, V, q, kn, vn, items, 8, kernel=1)
     finally:
-        rt.set_wait_limit(None)
+        rt.test_fail_waits(False)
     with pytest.raises(WfdError) as err:
         rt.read_device_error(cuda_dev)
     assert err.value.status == 16

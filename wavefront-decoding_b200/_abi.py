@@ -26,7 +26,7 @@ EXPORTED = (
     "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul", "wfd_gather_rows", "wfd_scatter_rows",
     "wfd_items_from_table", "wfd_argmax_rows",
     "wfd_sched_pre_tick", "wfd_sched_route", "wfd_sched_settle", "wfd_sched_params_bytes",
-    "wfd_set_batch_invariant", "wfd_get_batch_invariant", "wfd_set_wait_limit",
+    "wfd_set_batch_invariant", "wfd_get_batch_invariant", "wfd_test_fail_waits",
 )
 
 
@@ -43,7 +43,7 @@ class wfd_item(ctypes.Structure):
                 ("q_len", ctypes.c_int32), ("q_row0", ctypes.c_int32)]
 
 
-ABI_VERSION = 2  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
+ABI_VERSION = 3  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
 
 
 class wfd_sched_params(ctypes.Structure):
@@ -84,8 +84,9 @@ _SIGS = {
     # k v kc vc lens slot L n_slots n_seqs max_seq Hkv Dh dtype stream
     "wfd_write_prefill": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P], _I),
     "wfd_commit_drop": ([_P, _P, _I, _I, _P], _I),
-    # kc vc lens items n accept_len accept_mask acc_rows acc_count slot_off n_slots n_seqs max_seq Hkv Dh dtype err stream
-    "wfd_commit_window": ([_P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
+    # kc vc lens items n accept_len accept_mask acc_rows acc_count n_rows slot_off n_slots n_seqs max_seq Hkv Dh dtype
+    # err stream
+    "wfd_commit_window": ([_P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     # kc vc kp vp slots seqs cu_k n n_slots n_seqs max_seq Hkv Dh dtype err stream
     "wfd_gather_pack": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     # x w y n d eps dtype stream
@@ -104,7 +105,7 @@ _SIGS = {
     "wfd_argmax_rows": ([_P, _P, _I, _I, _I, _P], _I),
     "wfd_set_batch_invariant": ([_I], _I),
     "wfd_get_batch_invariant": ([], _I),
-    "wfd_set_wait_limit": ([_I], _I),
+    "wfd_test_fail_waits": ([_I], _I),
     # const wfd_sched_params*, stream
     "wfd_sched_pre_tick": ([_P, _P], _I),
     "wfd_sched_route": ([_P, _P], _I),

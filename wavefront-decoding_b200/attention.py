@@ -12,12 +12,15 @@ Layouts (reference fa4_attention.py:187-300):
 Semantics: scale 1/sqrt(Dh); GQA head h reads kv head h // (H/Hkv); causal means
 bottom-right aligned (row r of a (q_len, k_len) segment sees keys <= k_len-q_len+r).
 There is one implementation (CUDA, sm_100a); nothing here computes on the CPU.
+`attn_varlen` and `wave_attn` go through the dispatcher ops `torch.ops.wfd.*`
+(ops.py), which a call site can also use directly.
 """
 from __future__ import annotations
 
 import torch
 
 from . import _abi
+from . import ops as _ops
 from . import runtime as rt
 
 # The reference selects among "torch" | "fa4" | "sdpa" (fa4_attention.py:107-118).
@@ -38,50 +41,31 @@ def backend() -> str:
     return _BACKEND
 
 
-def _heads(q: torch.Tensor, k: torch.Tensor) -> tuple[int, int, int]:
-    H, Dh = q.shape[-2], q.shape[-1]
-    Hkv = k.shape[-2]
-    if k.shape[-1] != Dh:
-        raise ValueError(f"head_dim mismatch: q {Dh} vs k {k.shape[-1]}")
-    if H % Hkv != 0:
-        raise ValueError(f"query heads {H} not a multiple of kv heads {Hkv}")
-    return H, Hkv, Dh
-
-
-def _i32(t, device) -> torch.Tensor:
-    t = torch.as_tensor(t)
-    if t.dtype != torch.int32 or t.device != device:
-        t = t.to(device=device, dtype=torch.int32)
-    return t.contiguous()
+_heads = _ops.heads
+_i32 = _ops.i32
 
 
 def attn_varlen(q, k, v, cu_q, cu_k, max_q, max_k, causal: bool = False, *, scale: float | None = None,
                 out: torch.Tensor | None = None):
-    """Reference `attn_varlen` (fa4_attention.py:301-317).  causal=False: every
-    row of a segment sees the whole segment; causal=True: bottom-right causal per
-    segment.  cu_q / cu_k may be device tensors whose contents change between
-    CUDA-graph replays (the graph engine's lengths-as-data contract,
-    graph_blocks.py:5-11); max_q / max_k are upper bounds."""
+    """Reference `attn_varlen` (fa4_attention.py:301-317), through the
+    dispatcher op torch.ops.wfd.attn (torch.ops.wfd.attn_out with `out`).
+    causal=False: every row of a segment sees the whole segment; causal=True:
+    bottom-right causal per segment.  cu_q / cu_k may be device tensors whose
+    contents change between CUDA-graph replays (the graph engine's
+    lengths-as-data contract, graph_blocks.py:5-11); max_q / max_k are upper
+    bounds."""
     dev = rt.require_cuda(q, k, v)
     if q.dim() != 3 or k.dim() != 3 or v.shape != k.shape:
         raise ValueError("attn_varlen expects q (total_q, H, Dh), k/v (total_k, Hkv, Dh)")
-    H, Hkv, Dh = _heads(q, k)
+    _heads(q, k)
     if q.dtype != k.dtype or k.dtype != v.dtype:
         raise TypeError("q, k, v must share a dtype")
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     cu_q, cu_k = _i32(cu_q, dev), _i32(cu_k, dev)
-    n = cu_q.numel() - 1
-    if cu_k.numel() != n + 1:
+    if cu_k.numel() != cu_q.numel():
         raise ValueError("cu_q and cu_k must have the same number of segments")
     if out is None:
-        out = torch.empty_like(q)
-    ws, wsb = rt.workspace(dev, n, Dh)
-    lib = _abi.load()
-    st = lib.wfd_attn_varlen(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), cu_q.data_ptr(),
-                             cu_k.data_ptr(), n, int(max_q), q.shape[0], k.shape[0], H, Hkv, Dh,
-                             rt.dtype_code(q.dtype), 1 if causal else 0, float(scale or 0.0), ws.data_ptr(), wsb,
-                             rt.error_word(dev).data_ptr(), rt.stream_ptr(dev))
-    _abi.check(st, "wfd_attn_varlen")
+        return torch.ops.wfd.attn(q, k, v, cu_q, cu_k, int(max_q), int(max_k), bool(causal), scale)
+    torch.ops.wfd.attn_out(q, k, v, cu_q, cu_k, int(max_q), int(max_k), bool(causal), scale, out)
     return out
 
 
@@ -153,7 +137,9 @@ def attn_cutoff_multi(q, k, v, qpos):
 
 def wave_attn(q, k_new, v_new, k_cache, v_cache, items, max_q: int, *, lens=None, slot_offset: int = 0,
               out: torch.Tensor | None = None, scale: float | None = None, kernel: int = -1):
-    """Wavefront decode / verify attention with the K/V append fused.
+    """Wavefront decode / verify attention with the K/V append fused, through
+    the dispatcher op torch.ops.wfd.wave_attn (torch.ops.wfd.wave_attn_out with
+    `out`).
 
     q (n_rows, H, Dh); k_new / v_new (n_rows, Hkv, Dh); k_cache / v_cache
     (n_slots, n_seqs, max_seq, Hkv, Dh); items: device int32 (n_items, 5) rows of
@@ -161,32 +147,10 @@ def wave_attn(q, k_new, v_new, k_cache, v_cache, items, max_q: int, *, lens=None
     n_seqs).  Row j of an item writes its K/V at pos0+j of (slot+slot_offset, seq)
     and attends positions [0, pos0+j].  kernel: -1 auto, 0 CUDA-core decode,
     1 tcgen05 verify."""
-    dev = rt.require_cuda(q, k_new, v_new, k_cache, v_cache, items)
-    if k_cache.dim() != 5 or v_cache.shape != k_cache.shape:
-        raise ValueError("k_cache / v_cache must be (n_slots, n_seqs, max_seq, Hkv, Dh)")
-    n_slots, n_seqs, max_seq, Hkv, Dh = k_cache.shape
-    H = q.shape[1]
-    if q.dim() != 3 or q.shape[2] != Dh or k_new.shape != (q.shape[0], Hkv, Dh) or v_new.shape != k_new.shape:
-        raise ValueError("q (n_rows, H, Dh) and k_new / v_new (n_rows, Hkv, Dh) must match the cache")
-    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
-        raise ValueError("k_cache / v_cache must be contiguous")
-    if items.dtype != torch.int32 or items.dim() != 2 or items.shape[1] != 5 or not items.is_contiguous():
-        raise ValueError("items must be a contiguous int32 (n_items, 5) device tensor")
-    if lens is not None and (lens.dtype != torch.int32 or tuple(lens.shape) != (n_slots, n_seqs)):
-        raise ValueError("lens must be int32 (n_slots, n_seqs)")
-    q, k_new, v_new = q.contiguous(), k_new.contiguous(), v_new.contiguous()
+    rt.require_cuda(q, k_new, v_new, k_cache, v_cache, items)
     if out is None:
-        out = torch.empty_like(q)
-    n = items.shape[0]
-    ws, wsb = rt.workspace(dev, n, Dh)
-    lib = _abi.load()
-    args = (q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-            out.data_ptr(), rt.ptr(lens), items.data_ptr(), n, int(max_q), int(slot_offset), q.shape[0], n_slots,
-            n_seqs, max_seq, H, Hkv, Dh, rt.dtype_code(q.dtype), float(scale or 0.0), ws.data_ptr(), wsb,
-            rt.error_word(dev).data_ptr(), rt.stream_ptr(dev))
-    if kernel < 0:
-        st = lib.wfd_wave_attn(*args)
-    else:
-        st = lib.wfd_wave_attn_kernel(int(kernel), *args)
-    _abi.check(st, "wfd_wave_attn")
+        return torch.ops.wfd.wave_attn(q, k_new, v_new, k_cache, v_cache, items, int(max_q), lens, int(slot_offset),
+                                       scale, int(kernel))
+    torch.ops.wfd.wave_attn_out(q, k_new, v_new, k_cache, v_cache, items, int(max_q), lens, int(slot_offset), scale,
+                                int(kernel), out)
     return out

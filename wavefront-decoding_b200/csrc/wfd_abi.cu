@@ -29,9 +29,9 @@ constexpr int kMaxDevices = 64;
 // Batch-invariant attention (wfd_set_batch_invariant): read when a launch is
 // built, so a captured CUDA graph keeps the mode it was captured with.
 std::atomic<int> g_batch_invariant{0};
-// Per-wait spin limit of the tensor-core kernel (wfd_set_wait_limit): kSpinLimit
-// unless a test lowers it to make the waits run out.  Read when a launch is built.
-std::atomic<uint32_t> g_spin_limit{kSpinLimit};
+// Test hook (wfd_test_fail_waits): every bounded wait of the tensor-core kernel
+// gives up at once.  Read when a launch is built.
+std::atomic<int> g_fail_waits{0};
 constexpr int kGridPerSm = 4;  // upper bound on resident decode CTAs per SM used for sizing
 
 struct DevInfo {
@@ -330,7 +330,11 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   pp.qg_split = 1;
   pp.segs = reinterpret_cast<Seg*>(ws + L.segs);
   pp.prefix = reinterpret_cast<long long*>(ws + L.prefix);
-  if (which == 1) {  // the tcgen05 grid: one CTA per SM over (pair) kv-head units
+  // Small slot tables: the tcgen05 CTAs plan their own start from the items
+  // (and start streaming before the plan kernel ends); otherwise the plan
+  // kernel writes one start record per CTA.
+  const bool self_plan = which == 1 && A.mode == kPlanSlots && A.n <= kSelfPlanMax;
+  if (which == 1 && !self_plan) {  // the tcgen05 grid: one CTA per SM over (pair) kv-head units
     pp.start = reinterpret_cast<CtaStart*>(ws + L.start);
     pp.seg_grid = sms;
     pp.seg_units = pair ? A.Hkv / 2 : A.Hkv;
@@ -384,7 +388,16 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     vp.ws_part = reinterpret_cast<float*>(ws + L.part);
     vp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
     vp.err = A.err;
-    vp.spin_limit = g_spin_limit.load(std::memory_order_relaxed);
+    vp.fail_waits = g_fail_waits.load(std::memory_order_relaxed);
+    if (self_plan) {
+      vp.items = A.items;
+      vp.n_slots = A.n_slots;
+      vp.n_seqs = A.n_seqs;
+      vp.max_seq = A.max_seq;
+      vp.n_rows = A.n_rows;
+      vp.Gv = Gv;
+      vp.NQ = NQ;
+    }
     return launch_verify(NQ, verify_active(NQ, Gv, max_q), vp, A.k, A.v, A.key_rows, A.Hkv, A.Dh, pair ? 128 : A.Dh,
                          sms, st);
   }
@@ -586,8 +599,8 @@ int wfd_set_batch_invariant(int32_t on) {
 
 int wfd_get_batch_invariant(void) { return g_batch_invariant.load(); }
 
-int wfd_set_wait_limit(int32_t iterations) {
-  g_spin_limit.store(iterations < 0 ? kSpinLimit : (uint32_t)iterations);
+int wfd_test_fail_waits(int32_t on) {
+  g_fail_waits.store(on ? 1 : 0);
   return WFD_OK;
 }
 
@@ -750,16 +763,16 @@ int wfd_commit_drop(int32_t* lens, const int32_t* drop_pos, int32_t n_slots, int
 
 int wfd_commit_window(void* k_cache, void* v_cache, int32_t* lens, const wfd_item* items, int32_t n_items,
                       const int32_t* accept_len, const uint8_t* accept_mask, int32_t* acc_rows, int32_t* acc_count,
-                      int32_t slot_offset, int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_kv_heads,
-                      int32_t head_dim, int32_t dtype, int32_t* d_err, void* stream) {
+                      int32_t n_rows, int32_t slot_offset, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
+                      int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t* d_err, void* stream) {
   if (!geom_ok(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype)) return WFD_ERR_INVALID_ARG;
-  if (n_items < 0 || !lens || !items || !k_cache || !v_cache) return WFD_ERR_INVALID_ARG;
+  if (n_items < 0 || n_rows < 0 || !lens || !items || !k_cache || !v_cache) return WFD_ERR_INVALID_ARG;
   if ((accept_len == nullptr) == (accept_mask == nullptr)) return WFD_ERR_INVALID_ARG;
   if (!aligned16(k_cache) || !aligned16(v_cache)) return WFD_ERR_ALIGNMENT;
   if (n_items == 0) return WFD_OK;
   commit_window_kernel<<<n_items, kCommitThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<char*>(k_cache), static_cast<char*>(v_cache), lens, items, n_items, accept_len, accept_mask,
-      acc_rows, acc_count, slot_offset, geom(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype), d_err);
+      acc_rows, acc_count, n_rows, slot_offset, geom(n_slots, n_seqs, max_seq, n_kv_heads, head_dim, dtype), d_err);
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 

@@ -82,7 +82,7 @@ constexpr int kCommitThreads = 256;
 __global__ void __launch_bounds__(kCommitThreads)
     commit_window_kernel(char* kc, char* vc, int32_t* lens, const wfd_item* items, int n_items,
                          const int32_t* accept_len, const uint8_t* accept_mask, int32_t* acc_rows, int32_t* acc_count,
-                         int slot_offset, CacheGeom g, int* err) {
+                         int n_rows, int slot_offset, CacheGeom g, int* err) {
   const int it_idx = blockIdx.x;
   if (it_idx >= n_items) return;
   const wfd_item it = items[it_idx];
@@ -91,6 +91,11 @@ __global__ void __launch_bounds__(kCommitThreads)
   const bool ok_pos = it.pos0 >= 0 && it.q_len >= 0 && (long long)it.pos0 + it.q_len <= g.max_seq;
   if (!ok_slot || !ok_pos) {
     if (threadIdx.x == 0) set_error(err, ok_slot ? kErrBadPos : kErrBadSlot);
+    return;
+  }
+  // the window's q rows index accept_mask and acc_rows (n_rows entries)
+  if (it.q_row0 < 0 || (long long)it.q_row0 + it.q_len > n_rows) {
+    if (threadIdx.x == 0) set_error(err, kErrBadRows);
     return;
   }
   __shared__ int s_rank[1024];

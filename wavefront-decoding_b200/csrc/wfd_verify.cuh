@@ -54,6 +54,10 @@
 namespace wfd {
 
 constexpr int kVerifyMaxRows = 32;  // query vectors per unit (larger windows -> query groups)
+constexpr int kSelfPlanMax = 256;
+#ifndef WFD_MMA_CHAINS
+#define WFD_MMA_CHAINS 2
+#endif   // item tables up to this size are planned by the attention CTAs themselves
 constexpr int kTcTile = 128;        // keys per tile == MMA M
 // threads: TMA warp + MMA warp + 4 softmax warps per 16 query columns
 __host__ __device__ constexpr int tc_threads(int nqp) { return nqp == 32 ? 320 : 192; }
@@ -77,9 +81,18 @@ struct VerifyParams {
   float* ws_part;
   int* ws_cnt;
   int* err;
-  // iterations of one bounded wait before it gives up (kSpinLimit unless a
-  // test lowers it to make the waits run out)
-  uint32_t spin_limit;
+  // Self-planned start (slot-table calls with at most kSelfPlanMax items, else
+  // null): every CTA computes its share's first segment from the item table
+  // itself, before the plan kernel has finished, and streams the key tiles the
+  // window append cannot touch before it waits for that kernel.
+  const wfd_item* items;
+  int n_slots, n_seqs, max_seq, n_rows;  // the plan kernel's item checks
+  int Gv, NQ;                            // query vectors per kv (pair) head, per unit
+  // 1 (a test hook): the CTA gives up as a wait that ran out of its bound does
+  // (timeout bit, abort flag) right after its first K/V copies are issued.
+  // Checked once per CTA, not in the waits: the wait loops stay as lean as
+  // possible (a runtime trip count in them cost 8 us a config-2 step).
+  int fail_waits;
 };
 
 template <int NQP, int DH>
@@ -98,11 +111,19 @@ struct TcCfg {
   static constexpr int RED_FLOATS = 2 * 4 * NQP;           // double-buffered per-warp column values
   static constexpr int SMEM =
       STAGES * KV_STAGE + GUARD + 2 * Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + (2 * NQP + 4) * 4 + 1024;
-  static constexpr int TMEM_COLS = NQP == 16 ? 64 : 128;   // S (x2) and O accumulators
+  // Each accumulation (S^T of a tile, O^T of a tile) is split over CH
+  // independent TMEM accumulators (k-steps j with j % CH == c go to chain c,
+  // summed by the softmax warps): consecutive MMAs into one accumulator wait
+  // for each other, so CH chains keep CH MMAs in flight.
+  static constexpr int CH = WFD_MMA_CHAINS;
+  static constexpr int S_COL = 0;                          // S^T buffer sb, chain c: (sb * CH + c) * NQP
+  static constexpr int O_COL = 2 * CH * NQP;               // O^T chain c: O_COL + c * NQP
+  static constexpr int TMEM_USED = 3 * CH * NQP;
+  static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128 : 256;
   static constexpr int PART_FLOATS = NQP * (DH + 2);
   static_assert(NQP == 16 || NQP == 32, "N of the swap-AB MMA");
   static_assert(DH == 64 || DH == 128, "head dim");
-  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert(SMEM + 3072 <= 232448, "shared memory per CTA (dynamic + the kernel's static arrays)");
 };
 
 // Any window size runs on the tensor cores: more than kVerifyMaxRows query
@@ -200,11 +221,10 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float (&v)[32]) {
 // flag) or as soon as another role has aborted.  After an abort the roles keep
 // their control flow (same loop trips, same named barriers) but issue no more
 // TMA or MMA work, so nothing in the CTA can block without a bound.
-__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                        uint32_t limit) {
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
   bool ok = false;
   if (!*abort_flag) {
-    for (uint32_t i = 0; i < limit; ++i) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
       if (mbar_try_wait(bar, parity)) {
         ok = true;
         break;
@@ -255,6 +275,31 @@ __device__ __forceinline__ int reduced_col(int lane) {
   return (int)(__brev((unsigned)(lane & (N - 1))) >> (32 - LOGN));
 }
 
+// Segment i of a slot-mode item table exactly as the plan kernel builds it
+// (invalid items get no work); returns its work in unit-keys per kv head.
+__device__ __forceinline__ long long slot_segment(const VerifyParams& p, const wfd_item& it, Seg& s) {
+  s.k_row0 = 0;
+  s.k_len = 0;
+  s.q_row0 = 0;
+  s.q_len = 0;
+  s.new_row0 = -1;
+  s.lens_idx = -1;
+  s.n_qg = 0;
+  const bool ok = it.slot >= 0 && it.slot < p.n_slots && it.seq >= 0 && it.seq < p.n_seqs && it.pos0 >= 0 &&
+                  it.q_len >= 0 && (long long)it.pos0 + it.q_len <= p.max_seq && it.q_row0 >= 0 &&
+                  (long long)it.q_row0 + it.q_len <= p.n_rows;
+  if (!ok) return 0;
+  s.k_row0 = ((long long)it.slot * p.n_seqs + it.seq) * (long long)p.max_seq;
+  s.k_len = it.pos0 + it.q_len;
+  s.q_row0 = it.q_row0;
+  s.q_len = it.q_len;
+  s.new_row0 = it.q_row0;
+  s.lens_idx = it.slot * p.n_seqs + it.seq;
+  const long long qv = (long long)it.q_len * p.Gv;
+  s.n_qg = qv == 0 ? 0 : (int)((qv + p.NQ - 1) / p.NQ);
+  return (long long)s.n_qg * s.k_len;
+}
+
 // The (segment, unit, key range) pieces of one CTA's share, in order; every
 // role walks the same sequence.  The current segment (its Seg, its first and
 // the next segment's first work index) stays in registers, so moving to the
@@ -265,6 +310,7 @@ struct UnitIter {
   bool have = false;
   Seg S{};
   long long base = 0, nbase = 0;
+  bool waited = true;  // false: griddep_wait() not yet executed by this thread (self-planned start)
   __device__ __forceinline__ long long seg_base(const VerifyParams& p, int i) const {
     return i <= p.n_segs - 1 ? (long long)p.Hkv * p.prefix[i] : 0x7fffffffffffffffll;
   }
@@ -273,6 +319,10 @@ struct UnitIter {
     for (;;) {
       if (pos >= b) return false;
       if (!have || pos >= nbase) {
+        if (!waited) {  // the segment table and prefix are the plan kernel's outputs
+          griddep_wait();
+          waited = true;
+        }
         if (!have) {
           base = seg_base(p, seg);
           nbase = seg_base(p, seg + 1);
@@ -356,6 +406,28 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
+  // Self-planned start: the item table comes from the plan kernel's
+  // predecessor, which had completed before the plan kernel let this grid start,
+  // so it is read before griddep_wait(); everything the plan kernel writes
+  // (segment table, prefix, appended window rows) is read only after it.  The
+  // loads go out first, under the barrier and TMEM set-up; thread t holds items
+  // [t * IPT, t * IPT + IPT).
+  const bool self = p.items != nullptr;
+  constexpr int IPT = (kSelfPlanMax + THREADS - 1) / THREADS;
+  wfd_item my[IPT];
+  if (self) {
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      const int i = tid * IPT + k;
+      if (i < p.n_segs) my[k] = p.items[i];
+    }
+  }
+  // the tensor maps' descriptors are fetched while the CTA sets up
+  if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_k)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_v)) : "memory");
+  }
+
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bar_full[s], 1);
@@ -382,17 +454,53 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  griddep_wait();  // plan outputs, appended window rows and the workspace
+  __shared__ long long s_wtot[THREADS / 32];  // self-planned: work of each warp's items
+  __shared__ Seg s_S0;                         // self-planned: the share's first segment
+  __shared__ long long s_base0, s_nbase0;
+  __shared__ int s_seg0, s_slot0, s_seq0, s_minpos;
+  if (!self) griddep_wait();  // plan outputs, appended window rows and the workspace
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  // independent loads in flight together: this CTA's start record (from the
-  // plan kernel) and the total work
   CtaStart cs{};
-  if (p.start != nullptr) cs = p.start[blockIdx.x];
-  const long long total = (long long)p.Hkv * p.prefix[p.n_segs];
+  long long total;
+  long long w[IPT];
+  long long excl = 0;
+  if (self) {
+    // per-item work (the plan kernel's rule; invalid items have none), then an
+    // exclusive prefix over the CTA: warp shuffles, one barrier
+    long long tsum = 0;
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      Seg sg;
+      w[k] = (tid * IPT + k < p.n_segs) ? slot_segment(p, my[k], sg) : 0;
+      tsum += w[k];
+    }
+    long long incl = tsum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_wtot[warp] = incl;
+    if (tid == 0) s_minpos = 0x7fffffff;
+    __syncthreads();
+    long long before = 0, all = 0;
+#pragma unroll
+    for (int k = 0; k < THREADS / 32; ++k) {
+      before += (k < warp) ? s_wtot[k] : 0;
+      all += s_wtot[k];
+    }
+    excl = before + incl - tsum;
+    total = (long long)p.Hkv * all;
+  } else {
+    // independent loads in flight together: this CTA's start record (from the
+    // plan kernel) and the total work
+    if (p.start != nullptr) cs = p.start[blockIdx.x];
+    total = (long long)p.Hkv * p.prefix[p.n_segs];
+  }
   long long share = 1, a = 0, b = 0;
   if (total > 0) {
     share = (total + gridDim.x - 1) / gridDim.x;
@@ -404,7 +512,47 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   // threads probe 192 pivots of [lo, hi] at once, so up to 192 segments take
   // one round of loads instead of a chain of dependent ones.
   int seg0 = 0;
-  if (a < b && p.start != nullptr) {
+  int minpos = 0;  // self-planned: keys of the first segment below this are never written by the append
+  if (self) {
+    // the item whose work holds a (the largest i with Hkv * prefix[i] <= a has
+    // work: a < total) is found by its owner thread
+    if (a < b) {
+      long long pf = excl;
+#pragma unroll
+      for (int k = 0; k < IPT; ++k) {
+        const int i = tid * IPT + k;
+        if (w[k] > 0 && (long long)p.Hkv * pf <= a && a < (long long)p.Hkv * (pf + w[k])) {
+          slot_segment(p, my[k], s_S0);
+          s_base0 = (long long)p.Hkv * pf;
+          s_nbase0 = i + 1 <= p.n_segs - 1 ? (long long)p.Hkv * (pf + w[k]) : 0x7fffffffffffffffll;
+          s_seg0 = i;
+          s_slot0 = my[k].slot;
+          s_seq0 = my[k].seq;
+        }
+        pf += w[k];
+      }
+    }
+    __syncthreads();
+    if (a < b) {
+      // the lowest window position any item appends to the first segment's
+      // (slot, sequence): items of one call may share a slot
+      const int sl0 = s_slot0, sq0 = s_seq0;
+      int mp = 0x7fffffff;
+#pragma unroll
+      for (int k = 0; k < IPT; ++k)
+        if (w[k] > 0 && my[k].slot == sl0 && my[k].seq == sq0 && my[k].pos0 < mp) mp = my[k].pos0;
+      if (mp != 0x7fffffff) atomicMin(&s_minpos, mp);
+    }
+    __syncthreads();
+    if (a < b) {
+      seg0 = s_seg0;
+      cs.S = s_S0;
+      cs.base = s_base0;
+      cs.nbase = s_nbase0;
+      cs.seg = seg0;
+    }
+    minpos = s_minpos;
+  } else if (a < b && p.start != nullptr) {
     seg0 = cs.seg;
   } else if (a < b) {
     int lo = 0, hi = p.n_segs - 1;
@@ -432,12 +580,13 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   // already in registers
   auto make_iter = [&]() {
     UnitIter r{a, b, seg0};
-    if (a < b && p.start != nullptr) {
+    if (a < b && (p.start != nullptr || self)) {
       r.have = true;
       r.S = cs.S;
       r.base = cs.base;
       r.nbase = cs.nbase;
     }
+    r.waited = !self;
     return r;
   };
 
@@ -456,7 +605,12 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
 
       for (int t = 0; t < n_t; ++t, ++it) {
         const int stage = (int)(it % STAGES);
-        const bool go = (it >= (uint32_t)STAGES) ? tc_wait(&bar_empty[stage], ((it / STAGES) - 1) & 1u, &s_abort, p.err, p.spin_limit)
+        if (!itr.waited && (itr.seg != seg0 || r_lo + (t + 1) * kTcTile > minpos)) {
+          // this tile may hold rows the plan kernel's append writes
+          griddep_wait();
+          itr.waited = true;
+        }
+        const bool go = (it >= (uint32_t)STAGES) ? tc_wait(&bar_empty[stage], ((it / STAGES) - 1) & 1u, &s_abort, p.err)
                                                  : !s_abort;
         if (go && lane == 0) {
           unsigned char* dst = kvs + stage * C::KV_STAGE;
@@ -470,6 +624,10 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
             tma_load_3d(dst + (KB + bx) * C::BOX_BYTES, &tm_v, cx, ch, row, &bar_full[stage]);
           }
           n_iss = it + 1;
+          if (p.fail_waits && n_iss == 1) {  // test hook: give up with this tile's copies in flight
+            set_error(p.err, kErrTimeout);
+            s_abort = 1;
+          }
         }
         __syncwarp();
         if (t == 0) {
@@ -481,7 +639,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
           {
             const int qb = (int)(units & 1u);
             const bool qgo =
-                units >= 2 ? tc_wait(&bar_qfree[qb], ((units >> 1) - 1) & 1u, &s_abort, p.err, p.spin_limit) : !s_abort;
+                units >= 2 ? tc_wait(&bar_qfree[qb], ((units >> 1) - 1) & 1u, &s_abort, p.err) : !s_abort;
             if (qgo) {
               const int nvh = S.q_len * p.G;
               const int nvec = (p.pair ? 2 * nvh : nvh) - qg * NQP;
@@ -519,10 +677,10 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
     // the MMA warp's last commits arrive on these barriers: see them land
     // before this CTA may exit
     for (uint32_t k = (units > 2 ? units - 2 : 0); k < units; ++k)
-      tc_wait(&bar_qfree[k & 1u], (k >> 1) & 1u, &s_abort, p.err, p.spin_limit);
+      tc_wait(&bar_qfree[k & 1u], (k >> 1) & 1u, &s_abort, p.err);
     const uint32_t n_used = it;
     for (uint32_t j = (n_used > (uint32_t)STAGES ? n_used - STAGES : 0); j < n_used; ++j)
-      tc_wait(&bar_empty[j % STAGES], (j / STAGES) & 1u, &s_abort, p.err, p.spin_limit);
+      tc_wait(&bar_empty[j % STAGES], (j / STAGES) & 1u, &s_abort, p.err);
     // Copies in flight must land before the CTA exits, also after an abort (which
     // skips the waits above): wait, with the fixed bound and whatever the abort
     // flag says, for the last phase of every stage this lane filled.  Earlier
@@ -547,15 +705,15 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       const int n_t = (r_hi - r_lo + kTcTile - 1) / kTcTile;
       const int qb = (int)(units & 1u);
       const uint32_t qa = q_addr + (uint32_t)(qb * C::Q_BYTES);
-      tc_wait(&bar_qready[qb], (units >> 1) & 1u, &s_abort, p.err, p.spin_limit);
+      tc_wait(&bar_qready[qb], (units >> 1) & 1u, &s_abort, p.err);
       tc_fence_after();
       for (int t = 0; t <= n_t; ++t) {
         if (t < n_t) {
           const uint32_t ti = it + t;
           const int stage = (int)(ti % STAGES);
           const int sb = (int)(ti & 1u);
-          bool go = tc_wait(&bar_full[stage], (ti / STAGES) & 1u, &s_abort, p.err, p.spin_limit);
-          if (ti >= 2) go = tc_wait(&bar_sfree[sb], ((ti >> 1) - 1) & 1u, &s_abort, p.err, p.spin_limit) && go;
+          bool go = tc_wait(&bar_full[stage], (ti / STAGES) & 1u, &s_abort, p.err);
+          if (ti >= 2) go = tc_wait(&bar_sfree[sb], ((ti >> 1) - 1) & 1u, &s_abort, p.err) && go;
           tc_fence_after();
           if (go && lane == 0) {
             const uint32_t k_addr = smem_u32(kvs + stage * C::KV_STAGE);
@@ -564,8 +722,8 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
               // K step j: dims 16j..16j+15 = box j/4, byte 32*(j%4) inside the 128B row
               const uint32_t koff = (uint32_t)((j >> 2) * C::BOX_BYTES + (j & 3) * 32);
               const uint32_t qoff = (uint32_t)((j >> 2) * (NQP * 128) + (j & 3) * 32);
-              umma_f16(tmem + (uint32_t)(sb * NQP), umma_desc(k_addr + koff, 16, 1024, 2),
-                       umma_desc(qa + qoff, 16, 1024, 2), IDESC_S, j > 0 ? 1u : 0u);
+              umma_f16(tmem + (uint32_t)((sb * C::CH + j % C::CH) * NQP), umma_desc(k_addr + koff, 16, 1024, 2),
+                       umma_desc(qa + qoff, 16, 1024, 2), IDESC_S, j >= C::CH ? 1u : 0u);
             }
             umma_commit(&bar_sfull[sb]);
             if (t == n_t - 1) umma_commit(&bar_qfree[qb]);  // the unit's Q^T buffer may be rewritten
@@ -573,8 +731,8 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
           __syncwarp();
         }
         if (t >= 1) {
-          bool go = tc_wait(&bar_pfull, pv & 1u, &s_abort, p.err, p.spin_limit);
-          if (pv >= 1) go = tc_wait(&bar_ofree, (pv - 1) & 1u, &s_abort, p.err, p.spin_limit) && go;
+          bool go = tc_wait(&bar_pfull, pv & 1u, &s_abort, p.err);
+          if (pv >= 1) go = tc_wait(&bar_ofree, (pv - 1) & 1u, &s_abort, p.err) && go;
           tc_fence_after();
           const uint32_t tp = it + t - 1;
           const int stage = (int)(tp % STAGES);
@@ -583,9 +741,9 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               // K step j: keys 16j..16j+15 = two 8-row groups of both V boxes / of P^T
-              umma_f16(tmem + (uint32_t)(2 * NQP), umma_desc(v_addr + j * 2048, C::BOX_BYTES, 1024, 2),
+              umma_f16(tmem + (uint32_t)(C::O_COL + (j % C::CH) * NQP), umma_desc(v_addr + j * 2048, C::BOX_BYTES, 1024, 2),
                        umma_desc(p_addr + j * 2 * C::P_ATOM, 16, C::P_ATOM, C::P_LAYOUT), IDESC_PV,
-                       j > 0 ? 1u : 0u);
+                       j >= C::CH ? 1u : 0u);
             }
             umma_commit(&bar_ofull);
             umma_commit(&bar_empty[stage]);
@@ -643,10 +801,17 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       for (int t = 0; t < n_t; ++t) {
         const uint32_t ti = it + t;
         const int sb = (int)(ti & 1u);
-        tc_wait(&bar_sfull[sb], (ti >> 1) & 1u, &s_abort, p.err, p.spin_limit);
+        tc_wait(&bar_sfull[sb], (ti >> 1) & 1u, &s_abort, p.err);
         tc_fence_after();
         float s[LW];
-        tmem_ld<LW>(tq + (uint32_t)(sb * NQP + col0), s);
+        tmem_ld<LW>(tq + (uint32_t)(sb * C::CH * NQP + col0), s);
+        if constexpr (C::CH == 2) {
+          float s1[LW];
+          tmem_ld<LW>(tq + (uint32_t)((sb * C::CH + 1) * NQP + col0), s1);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < LW; ++j) s[j] += s1[j];
+        }
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -711,10 +876,17 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         // the previous tile's P.V: its MMA is done once o_full fires, which also
         // frees the P^T buffer.  oacc holds O_{t-2} already rescaled to m_{t-1}.
         if (t >= 1) {
-          tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err, p.spin_limit);
+          tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err);
           tc_fence_after();
           float o[LW];
-          tmem_ld<LW>(tq + (uint32_t)(2 * NQP + col0), o);
+          tmem_ld<LW>(tq + (uint32_t)(C::O_COL + col0), o);
+          if constexpr (C::CH == 2) {
+            float o1[LW];
+            tmem_ld<LW>(tq + (uint32_t)(C::O_COL + NQP + col0), o1);
+            tc_wait_ld();
+#pragma unroll
+            for (int j = 0; j < LW; ++j) o[j] += o1[j];
+          }
           tc_wait_ld();
           tc_fence_before();
           __syncwarp();
@@ -783,10 +955,17 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         if (stid == 0) mbar_arrive(&bar_pfull);
       }
       {
-        tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err, p.spin_limit);
+        tc_wait(&bar_ofull, pv & 1u, &s_abort, p.err);
         tc_fence_after();
         float o[LW];
-        tmem_ld<LW>(tq + (uint32_t)(2 * NQP + col0), o);
+        tmem_ld<LW>(tq + (uint32_t)(C::O_COL + col0), o);
+        if constexpr (C::CH == 2) {
+          float o1[LW];
+          tmem_ld<LW>(tq + (uint32_t)(C::O_COL + NQP + col0), o1);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < LW; ++j) o[j] += o1[j];
+        }
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -926,6 +1105,9 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
     }
   }
 
+  // a self-planned CTA may not have needed the plan kernel's outputs; it still
+  // completes only after that kernel, so stream order holds for what follows
+  if (self) griddep_wait();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -18,6 +18,7 @@ import torch
 
 from . import _abi
 from . import attention as _attn
+from . import ops as _ops
 from . import runtime as rt
 
 
@@ -92,9 +93,9 @@ class SlotKVCache:
             for p in positions:
                 if p >= self.S:
                     raise IndexError(f"position {p} exceeds max_seq_len={self.S}")
-        sl = _attn._i32(slots, self.device)
-        sq = _attn._i32(seq_ids, self.device)
-        ps = _attn._i32(positions, self.device)
+        sl = _ops.i32(slots, self.device)
+        sq = _ops.i32(seq_ids, self.device)
+        ps = _ops.i32(positions, self.device)
         k, v = k.contiguous(), v.contiguous()
         st = _abi.load().wfd_append(k.data_ptr(), v.data_ptr(), self.K.data_ptr(), self.V.data_ptr(),
                                     self.lens.data_ptr(), sl.data_ptr(), sq.data_ptr(), ps.data_ptr(), n,
@@ -114,8 +115,8 @@ class SlotKVCache:
         k_pack = torch.empty((total, self.n_kv_head, self.head_dim), dtype=self.dtype, device=self.device)
         v_pack = torch.empty_like(k_pack)
         cu_k = torch.tensor(cu_host, dtype=torch.int32, device=self.device)
-        sl = _attn._i32(slots, self.device)
-        sq = _attn._i32(seq_ids, self.device)
+        sl = _ops.i32(slots, self.device)
+        sq = _ops.i32(seq_ids, self.device)
         st = _abi.load().wfd_gather_pack(self.K.data_ptr(), self.V.data_ptr(), k_pack.data_ptr(), v_pack.data_ptr(),
                                          sl.data_ptr(), sq.data_ptr(), cu_k.data_ptr(), len(lengths), *self._geom(),
                                          rt.error_word(self.device).data_ptr(), self._stream())
@@ -131,11 +132,9 @@ class SlotKVCache:
         self.drop_many(drop.to(self.device))
 
     def drop_many(self, drop_pos: torch.Tensor) -> None:
-        """Batched rollback: drop_pos (B,) int32 device tensor, -1 = keep."""
-        drop_pos = _attn._i32(drop_pos, self.device)
-        st = _abi.load().wfd_commit_drop(self.lens.data_ptr(), drop_pos.data_ptr(), self.n_slots, self.B,
-                                         self._stream())
-        _abi.check(st, "wfd_commit_drop")
+        """Batched rollback: drop_pos (B,) int32 device tensor, -1 = keep
+        (torch.ops.wfd.commit_drop)."""
+        torch.ops.wfd.commit_drop(self.lens, _ops.i32(drop_pos, self.device))
 
     def commit_window(self, items: torch.Tensor, *, accept_len: torch.Tensor | None = None,
                       accept_mask: torch.Tensor | None = None, slot_offset: int = 0, n_rows: int | None = None,
@@ -149,27 +148,19 @@ class SlotKVCache:
         capture)."""
         if (accept_len is None) == (accept_mask is None):
             raise ValueError("give exactly one of accept_len / accept_mask")
-        items = _attn._i32(items, self.device).reshape(-1, 5)
+        items = _ops.i32(items, self.device).reshape(-1, 5)
         n = items.shape[0]
-        if out is not None:
-            acc_rows, acc_count = out
-            if n_rows is None:
-                n_rows = acc_rows.numel()
-        else:
-            if n_rows is None:
-                n_rows = int((items[:, 4] + items[:, 3]).max().item()) if n else 0
-            acc_rows = torch.full((max(n_rows, 1),), -1, dtype=torch.int32, device=self.device)
-            acc_count = torch.zeros((max(n, 1),), dtype=torch.int32, device=self.device)
-        al = None if accept_len is None else _attn._i32(accept_len, self.device)
+        al = None if accept_len is None else _ops.i32(accept_len, self.device)
         am = None
         if accept_mask is not None:
             am = torch.as_tensor(accept_mask).to(device=self.device, dtype=torch.uint8).contiguous()
-        st = _abi.load().wfd_commit_window(self.K.data_ptr(), self.V.data_ptr(), self.lens.data_ptr(),
-                                           items.data_ptr(), n, rt.ptr(al), rt.ptr(am), acc_rows.data_ptr(),
-                                           acc_count.data_ptr(), int(slot_offset), *self._geom(),
-                                           rt.error_word(self.device).data_ptr(), self._stream())
-        _abi.check(st, "wfd_commit_window")
-        return acc_rows[:n_rows], acc_count[:n]
+        if out is not None:
+            acc_rows, acc_count = out
+            torch.ops.wfd.commit_out(self.K, self.V, self.lens, items, al, am, int(slot_offset), acc_rows, acc_count)
+            return (acc_rows if n_rows is None else acc_rows[:n_rows]), acc_count[:n]
+        if n_rows is None:
+            n_rows = int((items[:, 4] + items[:, 3]).max().item()) if n else 0
+        return torch.ops.wfd.commit(self.K, self.V, self.lens, items, al, am, int(slot_offset), int(n_rows))
 
     # ------------------------------------------------------------------
     def wave_attn(self, q, k_new, v_new, items, max_q: int, *, slot_offset: int = 0, out=None, kernel: int = -1,

@@ -130,7 +130,8 @@ class batch_invariant:
 
 
 
-def set_wait_limit(iterations: int | None) -> None:
-    """Test hook: iterations of one bounded wait of the tcgen05 attention kernel
-    before it gives up and reports a timeout (None restores the default)."""
-    _abi.check(_abi.load().wfd_set_wait_limit(-1 if iterations is None else int(iterations)), "wfd_set_wait_limit")
+def test_fail_waits(on: bool) -> None:
+    """Test hook: every CTA of the tcgen05 attention kernel gives up right after
+    issuing its first K/V copies, as when a bounded wait runs out, and reports a
+    timeout (launches built while it is on)."""
+    _abi.check(_abi.load().wfd_test_fail_waits(1 if on else 0), "wfd_test_fail_waits")
