@@ -5,8 +5,8 @@ Implements the batch-blocks interface the reference's schedulers drive
 (`prefill`, `prelude_union`, `advance_union`, `coda_argmax_union`,
 ouro_blocks_batch.py:123-248, huginn_blocks_batch.py:207-346), B200-first:
 
-* Token state (hidden, injected input) lives in a device pool; an ActiveToken's
-  `hidden` is its pool row, so a union call gathers rows instead of stacking
+* Token state (hidden, injected input) lives in a device pool; the `hidden`
+  of a token in flight is its pool row, so a union call gathers rows instead of stacking
   per-token tensors, and writes them back in place.
 * One R tick is one attention launch per core layer for the whole union
   (`wfd_wave_attn`: window append + attention in one call, one item table shared by all

@@ -1,25 +1,34 @@
-"""Fixed-batch wavefront (WFD) and autoregressive schedulers over union P/R/C calls.
+"""Host-side batch schedulers over the engine's union P / R / C calls.
 
-Mirrors the reference's `src/decoding/scheduler_batch.py` (`generate_wavefront_batch`
-:228-362, `ar_generate_batch` :185-222), `batch_state.SeqState` (:272-323),
-`emu.EmulatedAcceptance` (:19-43) and `policy.SsdPolicy` (:16-59): same names,
-arguments, decisions and counters, so a trace from either implementation can be
-compared field by field.  The decision logic stays on the host (one token-id
-read-back per tick, as in the reference, `scheduler_batch.py:312`); every tensor
-operation runs in the `blocks` object (the GPU engine, engine.WaveEngine).
+A *lane* is one sequence of the batch.  Its *wave* holds the tokens that are in
+the recurrent block, keyed by absolute position; a token that enters the wave
+at step 0 advances one loop step per tick and is read out by the coda twice:
+at depth T_draft (its greedy id drafts the next position, which then enters
+the wave right behind it) and at depth T_total (its greedy id is the gold for
+the next position, which confirms or refutes the draft in flight there).  This
+is the state the device scheduler keeps in fixed token slots
+(csrc/wfd_sched.cuh); here it is a dict per lane, and a tick is
 
-Per tick: P union (tokens queued for the prelude) -> R union (one loop step for
-every live wave token) -> route (commit point: step == T_total -> verify; draft
-point: step == T_draft -> copy for a draft C) -> C union (greedy ids) -> settle
-(accept / reject cascade / rollback per sequence, new leading-edge draft).
+    prelude  the lane's queued tokens enter the wave        (one P union)
+    advance  every token in flight takes one loop step      (one R union)
+    read     tokens at full depth leave the wave; tokens at
+             draft depth are read as drafts                 (one C union)
+    settle   per lane, in position order: confirm the next draft or commit
+             the gold and cut the wave there (the KV slots of the sequence
+             drop the positions from the cut on); queue the next token
 
-`generate_dtv_batch` is the reference's draft-then-verify scheduler
-(scheduler_batch.py:365-501): per sequence, rounds of K drafts at depth T_draft
-followed by one verify of all K + 1 sources at full depth.
+Behaviour follows the reference's batch schedulers
+(src/decoding/scheduler_batch.py: ar_generate_batch :185-222,
+generate_wavefront_batch :228-362, generate_dtv_batch :365-501): the same
+decisions in the same order, the same counters, the same union sizes, the same
+rollback calls and, under emulated acceptance, the same order of draws from
+each sequence's random.Random stream (emu.py:19-43), so the reference's own
+traces pin this module (tests/golden/reference_scheduler.json).  The engine
+(engine.WaveEngine) does every tensor operation; the host reads back one
+vector of greedy ids per tick.
 """
 from __future__ import annotations
 
-import copy
 import random
 import time
 import warnings
@@ -28,44 +37,50 @@ from typing import Optional
 
 
 # ---------------------------------------------------------------------------
-# policy / emulated acceptance (policy.py:16-59, emu.py:19-43)
+# depths and emulated acceptance
 # ---------------------------------------------------------------------------
-@dataclass
+@dataclass(frozen=True)
 class SsdPolicy:
+    """Wave depths (reference policy.py:16-59): a token is read as a draft at
+    loop step T_draft and verified at step T_total.  Greedy decoding only."""
     T_total: int = 8
     T_draft: int = 2
     mode: str = "greedy"
 
     def __post_init__(self) -> None:
-        if self.T_draft < 1 or self.T_total < self.T_draft:
-            raise ValueError(f"Invalid policy: T_total={self.T_total}, T_draft={self.T_draft}. "
-                             "Require 1 <= T_draft <= T_total.")
+        if not 1 <= self.T_draft <= self.T_total:
+            raise ValueError(f"SsdPolicy needs 1 <= T_draft <= T_total; got T_draft={self.T_draft}, "
+                             f"T_total={self.T_total}")
         if self.mode != "greedy":
-            raise ValueError(f"Unknown sampling mode: {self.mode!r} (this engine decodes greedily).")
-        if self.T_total % self.T_draft != 0:
-            warnings.warn(f"T_total ({self.T_total}) is not a multiple of T_draft ({self.T_draft}); "
-                          "active wave size will fluctuate.", stacklevel=2)
+            raise ValueError(f"SsdPolicy: only greedy decoding is built (mode={self.mode!r})")
+        if self.T_total % self.T_draft:
+            warnings.warn(f"T_draft={self.T_draft} does not divide T_total={self.T_total}: the number of tokens "
+                          "in flight per sequence will vary from tick to tick", stacklevel=2)
 
     @property
     def steady_state_active_size(self) -> int:
+        """Tokens in flight per sequence once the wave is full."""
         return self.T_total // self.T_draft
 
 
 class EmulatedAcceptance:
-    """Bernoulli(rate) accept stream, one per sequence (seed = base + index)."""
+    """Draft outcomes drawn instead of compared (reference emu.py:19-43): each
+    draw accepts with probability `rate`, from a random.Random(seed) stream of
+    its own per sequence; one draw per verified draft, in commit order."""
 
     def __init__(self, rate: float, seed: int = 0):
-        assert 0.0 <= rate <= 1.0, f"acceptance rate must be in [0,1], got {rate}"
+        if not 0.0 <= rate <= 1.0:
+            raise ValueError(f"EmulatedAcceptance: rate {rate} is not a probability")
         self.rate = float(rate)
         self.seed = seed
-        self.rng = random.Random(seed)
+        self._stream = random.Random(seed)
         self.n_draws = 0
         self.n_accepts = 0
 
     def draw(self) -> bool:
+        ok = self._stream.random() < self.rate
         self.n_draws += 1
-        ok = self.rng.random() < self.rate
-        self.n_accepts += int(ok)
+        self.n_accepts += ok
         return ok
 
     @property
@@ -74,23 +89,12 @@ class EmulatedAcceptance:
 
 
 # ---------------------------------------------------------------------------
-# state (state.py:20-65, batch_state.py:272-323)
+# traces (the reference's counter names: they are compared field by field)
 # ---------------------------------------------------------------------------
 @dataclass
-class ActiveToken:
-    """One token in flight.  `hidden` is an opaque handle the blocks own (a
-    row of a device-resident state pool in the GPU engine)."""
-    token_id: int
-    position: int
-    role: str
-    step: int = 0
-    hidden: object = None
-    static_state: object = None
-    is_alive: bool = True
-
-
-@dataclass
 class GenerationTrace:
+    """Per-sequence record: committed tokens and the counters of the reference's
+    state.GenerationTrace."""
     tokens: list = field(default_factory=list)
     walltime_s: float = 0.0
     n_r_calls: int = 0
@@ -107,54 +111,8 @@ class GenerationTrace:
 
 
 @dataclass
-class SeqState:
-    idx: int
-    prefix_len: int
-    emu: Optional[EmulatedAcceptance] = None
-    trace: GenerationTrace = field(default_factory=GenerationTrace)
-    committed: list = field(default_factory=list)
-    done: bool = False
-    active_p: list = field(default_factory=list)
-    active_r: list = field(default_factory=list)
-    active_c: list = field(default_factory=list)
-    # DtV round state (batch_state.py:38-49): phase "need_p" (the next source needs
-    # its prelude), "draft" (the current source runs steps 0..T_draft), "verify"
-    # (all K + 1 sources run T_draft..T_total), "idle" once done
-    phase: str = "need_p"
-    K: int = 0                 # drafts this round
-    j: int = 0                 # index of the current source (0..K)
-    sources: list = field(default_factory=list)
-    drafts: list = field(default_factory=list)
-    cur_tok: int = 0           # token forwarded as source j, and its position
-    cur_pos: int = 0
-    last_token: int = 0        # last committed token (the round's seed), and its position
-    p: int = 0
-
-    def commit(self, token_id: int) -> None:
-        self.committed.append(token_id)
-        self.trace.tokens.append(token_id)
-
-    def find_active(self, position: int) -> Optional[ActiveToken]:
-        for lst in (self.active_r, self.active_p, self.active_c):
-            for t in lst:
-                if t.is_alive and t.position == position:
-                    return t
-        return None
-
-    def rollback(self, position: int, cache) -> None:
-        self.active_p = [t for t in self.active_p if t.position < position]
-        self.active_r = [t for t in self.active_r if t.position < position]
-        self.active_c = [t for t in self.active_c if t.position < position]
-        cache.drop_positions_at_and_after(self.idx, position)
-
-    def clear_working_state(self) -> None:
-        self.active_p, self.active_r, self.active_c = [], [], []
-        self.sources, self.drafts = [], []
-        self.phase = "idle"
-
-
-@dataclass
 class BatchTrace:
+    """Batch record: union-call counts, R-union sizes and the per-sequence traces."""
     walltime_s: float = 0.0
     prefill_s: float = 0.0
     n_r_calls: int = 0
@@ -183,336 +141,380 @@ class BatchTrace:
     @property
     def acceptance_rate(self) -> float:
         prop = sum(t.n_drafts_proposed for t in self.per_seq)
-        acc = sum(t.n_drafts_accepted for t in self.per_seq)
-        return acc / prop if prop else float("nan")
+        return sum(t.n_drafts_accepted for t in self.per_seq) / prop if prop else float("nan")
+
+    def count_union(self, kind: str, rows: int = 0) -> None:
+        if kind == "P":
+            self.n_p_calls += 1
+        elif kind == "C":
+            self.n_c_calls += 1
+        else:
+            self.n_r_calls += 1
+            self.r_union_total += rows
+            self.r_union_max = max(self.r_union_max, rows)
 
 
-def _record_r(bt: BatchTrace, n_union: int) -> None:
-    bt.n_r_calls += 1
-    bt.r_union_total += n_union
-    bt.r_union_max = max(bt.r_union_max, n_union)
+# ---------------------------------------------------------------------------
+# lanes
+# ---------------------------------------------------------------------------
+class Flight:
+    """One token in flight: what the engine's union calls read and update
+    (`hidden` / `static_state`: the engine's handle of its state rows; `step`:
+    loop steps taken)."""
+    __slots__ = ("token_id", "position", "step", "hidden", "static_state")
+
+    def __init__(self, token_id: int, position: int):
+        self.token_id = int(token_id)
+        self.position = int(position)
+        self.step = 0
+        self.hidden = None
+        self.static_state = None
 
 
-def _sync(blocks) -> None:
-    fn = getattr(blocks, "synchronize", None)
-    if fn is not None:
-        fn()
+class _Lane:
+    def __init__(self, idx: int, prompt_len: int, acceptance: Optional[EmulatedAcceptance]):
+        self.idx = idx
+        self.prompt_len = prompt_len
+        self.acceptance = acceptance
+        self.trace = GenerationTrace()
+        self.finished = False
+        self.wave: dict[int, Flight] = {}   # position -> token in the recurrent block (ascending positions)
+        self.queue: list[Flight] = []       # tokens waiting for the prelude
+        # draft-then-verify round (generate_dtv_batch)
+        self.anchor_tok = 0                 # last committed token and its position: the next round's seed
+        self.anchor_pos = 0
+        self.round: Optional[_DtvRound] = None
+
+    @property
+    def n_committed(self) -> int:
+        return len(self.trace.tokens)
+
+    def emit(self, token_id: int, limit: int) -> None:
+        self.trace.tokens.append(int(token_id))
+        if self.n_committed >= limit:
+            self.finished = True
+
+    def enqueue(self, token_id: int, position: int) -> None:
+        self.queue.append(Flight(token_id, position))
+        self.trace.n_p_calls += 1
+
+    def cut(self, position: int, cache) -> None:
+        """Forget every token at or after `position` and drop those positions
+        from the sequence's KV slots (BatchStaticKVCache.drop_positions_at_and_after)."""
+        self.wave = {p: f for p, f in self.wave.items() if p < position}
+        self.queue = [f for f in self.queue if f.position < position]
+        cache.drop_positions_at_and_after(self.idx, position)
+
+    def retire(self) -> None:
+        self.wave, self.queue, self.round = {}, [], None
 
 
-def _prefill_and_first(blocks, prompt_ids, emus, max_new_tokens, bt: BatchTrace, t0: float):
-    """scheduler_batch.py:123-159: prefill, commit the greedy first token."""
-    cache, last_logits = blocks.prefill(prompt_ids)
-    first = [int(x) for x in last_logits.argmax(dim=-1).tolist()]
-    _sync(blocks)
+def _start(blocks, prompt_ids, emus, max_new_tokens: int, bt: BatchTrace, t0: float):
+    """Prefill every prompt and commit each sequence's first greedy token
+    (scheduler_batch.py:123-159)."""
+    cache, logits = blocks.prefill(prompt_ids)
+    first = logits.argmax(dim=-1).tolist()
+    _synchronize(blocks)
     bt.prefill_s = time.perf_counter() - t0
     L = int(prompt_ids.shape[1])
-    seqs = []
-    for b in range(int(prompt_ids.shape[0])):
-        s = SeqState(idx=b, prefix_len=L, emu=(emus[b] if emus is not None else None))
-        s.commit(first[b])
-        if len(s.committed) >= max_new_tokens:
-            s.done = True
-        seqs.append(s)
-    return cache, seqs
+    lanes = [_Lane(b, L, emus[b] if emus is not None else None) for b in range(int(prompt_ids.shape[0]))]
+    for lane, tok in zip(lanes, first):
+        lane.emit(tok, max_new_tokens)
+    return cache, lanes
 
 
-def _finalize(bt: BatchTrace, seqs, t0: float, blocks) -> BatchTrace:
-    _sync(blocks)
+def _synchronize(blocks) -> None:
+    sync = getattr(blocks, "synchronize", None)
+    if sync is not None:
+        sync()
+
+
+def _close(bt: BatchTrace, lanes, t0: float, blocks) -> BatchTrace:
+    _synchronize(blocks)
     bt.walltime_s = time.perf_counter() - t0
-    for s in seqs:
-        s.trace.walltime_s = bt.walltime_s
-    bt.per_seq = [s.trace for s in seqs]
+    for lane in lanes:
+        lane.trace.walltime_s = bt.walltime_s
+    bt.per_seq = [lane.trace for lane in lanes]
     return bt
 
 
+def _tick_bound(max_new_tokens: int, per_token: int) -> int:
+    """Ticks after which a run that has not finished is a scheduler fault: every
+    tick commits a token of some live sequence within `per_token` ticks."""
+    return (max_new_tokens + 2) * (per_token + 4) + 128
+
+
+def _advance(blocks, cache, bt: BatchTrace, entries) -> None:
+    """One R union over (lane, token) entries; counts the call per lane once."""
+    blocks.advance_union([lane.idx for lane, _ in entries], [f for _, f in entries], cache)
+    bt.count_union("R", len(entries))
+    seen = set()
+    for lane, _ in entries:
+        if lane.idx not in seen:
+            seen.add(lane.idx)
+            lane.trace.n_r_calls += 1
+
+
+# ---------------------------------------------------------------------------
+# sequential loop decoding
+# ---------------------------------------------------------------------------
 def ar_generate_batch(blocks, prompt_ids, max_new_tokens: int) -> BatchTrace:
-    """Lockstep batched sequential loop decoding (scheduler_batch.py:185-222):
-    every live sequence runs P, T_total R steps and C per committed token."""
+    """Batched sequential loop decoding (scheduler_batch.py:185-222): per
+    committed token, every live sequence runs the prelude, T_total loop steps
+    and the coda in lockstep."""
     bt = BatchTrace()
     t0 = time.perf_counter()
-    cache, seqs = _prefill_and_first(blocks, prompt_ids, None, max_new_tokens, bt, t0)
-    T_total = blocks.T_total
+    cache, lanes = _start(blocks, prompt_ids, None, max_new_tokens, bt, t0)
+    depth = blocks.T_total
     while True:
-        act = [s for s in seqs if not s.done]
-        if not act:
+        live = [lane for lane in lanes if not lane.finished]
+        if not live:
             break
-        toks = []
-        for s in act:
-            pos = s.prefix_len + len(s.committed) - 1
-            toks.append(ActiveToken(token_id=s.committed[-1], position=pos, role="verify"))
-            s.trace.n_p_calls += 1
-        seq_ids = [s.idx for s in act]
-        blocks.prelude_union(seq_ids, toks, cache)
-        bt.n_p_calls += 1
-        for _ in range(T_total):
-            blocks.advance_union(seq_ids, toks, cache)
-            _record_r(bt, len(toks))
-            for s in act:
-                s.trace.n_r_calls += 1
-        out_ids = blocks.coda_argmax_union(seq_ids, toks, cache)
-        bt.n_c_calls += 1
-        for s, nid in zip(act, out_ids):
-            s.trace.n_c_calls += 1
-            s.commit(int(nid))
-            if len(s.committed) >= max_new_tokens:
-                s.done = True
-    return _finalize(bt, seqs, t0, blocks)
+        batch = []
+        for lane in live:
+            lane.trace.n_p_calls += 1
+            batch.append((lane, Flight(lane.trace.tokens[-1], lane.prompt_len + lane.n_committed - 1)))
+        ids = [lane.idx for lane, _ in batch]
+        toks = [f for _, f in batch]
+        blocks.prelude_union(ids, toks, cache)
+        bt.count_union("P")
+        for _ in range(depth):
+            _advance(blocks, cache, bt, batch)
+        heads = blocks.coda_argmax_union(ids, toks, cache)
+        bt.count_union("C")
+        for (lane, _), tok in zip(batch, heads):
+            lane.trace.n_c_calls += 1
+            lane.emit(tok, max_new_tokens)
+    return _close(bt, lanes, t0, blocks)
+
+
+# ---------------------------------------------------------------------------
+# wavefront decoding
+# ---------------------------------------------------------------------------
+def _wave_settle(lane: _Lane, full, gold, drafts, draft_ids, cache, limit: int) -> None:
+    """Resolve one lane's read-outs of a tick.  `full`: tokens that reached
+    T_total (ascending positions) with their gold ids; `drafts`: tokens read at
+    T_draft with their greedy ids."""
+    trace = lane.trace
+    cut = False
+    for k, (tok, g) in enumerate(zip(full, gold)):
+        nxt = tok.position + 1
+        following = full[k + 1] if k + 1 < len(full) else lane.wave.get(nxt)
+        if following is None:
+            # nothing in flight behind it: the gold is committed and starts the wave again
+            lane.emit(g, limit)
+            lane.enqueue(g, nxt)
+            stop = True
+        else:
+            trace.n_drafts_proposed += 1
+            agree = lane.acceptance.draw() if lane.acceptance is not None else g == following.token_id
+            if agree:
+                trace.n_drafts_accepted += 1
+                lane.emit(following.token_id, limit)
+                stop = False
+            else:
+                trace.n_drafts_rejected += 1
+                trace.n_rollback_events += 1
+                lane.emit(g, limit)
+                lane.cut(nxt, cache)
+                lane.enqueue(g, nxt)
+                cut = stop = True
+        if lane.finished or stop:
+            break
+    if lane.finished:
+        lane.retire()
+        return
+    if not cut and drafts:
+        lane.enqueue(draft_ids[0], drafts[0].position + 1)
 
 
 def generate_wavefront_batch(blocks, prompt_ids, max_new_tokens: int, policy: SsdPolicy,
                              emus: list | None = None) -> BatchTrace:
-    """One independent wave per sequence, union P/R/C per tick
-    (scheduler_batch.py:228-362).  emus[b] = EmulatedAcceptance replaces the
-    gold == draft comparison of sequence b (None: real comparison)."""
+    """Wavefront decoding, one independent wave per sequence, union P / R / C
+    calls per tick (scheduler_batch.py:228-362).  emus[b] (an
+    EmulatedAcceptance) replaces the gold == draft comparison of sequence b."""
     bt = BatchTrace()
     t0 = time.perf_counter()
-    cache, seqs = _prefill_and_first(blocks, prompt_ids, emus, max_new_tokens, bt, t0)
-    T_total, T_draft = policy.T_total, policy.T_draft
-    if emus is None:
-        emus = [None] * len(seqs)
-
-    for s in seqs:
-        if s.done:
-            continue
-        s.active_p.append(ActiveToken(token_id=s.committed[-1], position=s.prefix_len, role="draft"))
-        s.trace.n_p_calls += 1
-
-    ticks, max_ticks = 0, max_new_tokens * (T_total + 4) + 100
-    while True:
-        alive = [s for s in seqs if not s.done]
-        if not alive:
+    cache, lanes = _start(blocks, prompt_ids, emus, max_new_tokens, bt, t0)
+    deep, shallow = policy.T_total, policy.T_draft
+    for lane in lanes:
+        if not lane.finished:
+            lane.enqueue(lane.trace.tokens[-1], lane.prompt_len)
+    bound = _tick_bound(max_new_tokens, deep)
+    for _tick in range(bound + 1):
+        live = [lane for lane in lanes if not lane.finished]
+        if not live:
+            return _close(bt, lanes, t0, blocks)
+        if _tick == bound:
             break
-        ticks += 1
-        if ticks > max_ticks:
-            raise RuntimeError(f"wfd batch exceeded tick guard ({max_ticks}) — scheduler bug?")
-
-        # ---- P: union of queued tokens
-        p_pairs = [(s, t) for s in alive for t in s.active_p]
-        if p_pairs:
-            blocks.prelude_union([s.idx for s, _ in p_pairs], [t for _, t in p_pairs], cache)
-            for s, t in p_pairs:
-                s.active_r.append(t)
-            for s in alive:
-                s.active_p = []
-            bt.n_p_calls += 1
-
-        # ---- R: one loop step for every live wave token
-        r_pairs = [(s, t) for s in alive for t in s.active_r if t.is_alive]
-        if r_pairs:
-            blocks.advance_union([s.idx for s, _ in r_pairs], [t for _, t in r_pairs], cache)
-            _record_r(bt, len(r_pairs))
-            for s in alive:
-                if any(t.is_alive for t in s.active_r):
-                    s.trace.n_r_calls += 1
-
-        # ---- route commit / draft points
-        for s in alive:
-            survivors = []
-            for t in s.active_r:
-                if not t.is_alive:
-                    continue
-                if t.step == T_total:
-                    t.role = "verify"
-                    s.active_c.append(t)
-                else:
-                    survivors.append(t)
-                    if t.step == T_draft:
-                        c = copy.copy(t)
-                        c.role = "draft"
-                        s.active_c.append(c)
-            s.active_r = survivors
-
-        # ---- C: one head pass over the union of active_c
-        c_meta, c_toks, c_seq_ids = [], [], []
-        for s in alive:
-            if not s.active_c:
-                continue
-            vs = sorted((t for t in s.active_c if t.role == "verify"), key=lambda t: t.position)
-            ds = [t for t in s.active_c if t.role == "draft"]
-            c_meta.append((s, vs, ds))
-            c_toks += vs + ds
-            c_seq_ids += [s.idx] * (len(vs) + len(ds))
-        gold_of = {}
-        if c_toks:
-            out_ids = blocks.coda_argmax_union(c_seq_ids, c_toks, cache)
-            bt.n_c_calls += 1
-            gold_of = {id(t): int(nid) for t, nid in zip(c_toks, out_ids)}
-            for s, _, _ in c_meta:
-                s.trace.n_c_calls += 1
-
-        # ---- settle per sequence + new leading-edge draft
-        for s, vs, ds in c_meta:
-            rejected = False
-            boundary = False
-            for i, vtok in enumerate(vs):
-                gold = gold_of[id(vtok)]
-                vtok.is_alive = False
-                next_pos = vtok.position + 1
-                nxt = vs[i + 1] if i + 1 < len(vs) else s.find_active(next_pos)
-                if nxt is None:
-                    s.commit(gold)
-                    s.active_p.append(ActiveToken(gold, next_pos, "draft"))
-                    s.trace.n_p_calls += 1
-                    boundary = True
-                else:
-                    accept = s.emu.draw() if s.emu is not None else (gold == nxt.token_id)
-                    s.trace.n_drafts_proposed += 1
-                    if accept:
-                        s.trace.n_drafts_accepted += 1
-                        s.commit(nxt.token_id)
-                    else:
-                        s.trace.n_drafts_rejected += 1
-                        s.trace.n_rollback_events += 1
-                        rejected = True
-                        s.commit(gold)
-                        s.rollback(next_pos, cache)
-                        s.active_p.append(ActiveToken(gold, next_pos, "draft"))
-                        s.trace.n_p_calls += 1
-                if len(s.committed) >= max_new_tokens:
-                    s.done = True
-                if s.done or rejected or boundary:
-                    break
-            if s.done:
-                s.clear_working_state()
-                continue
-            if not rejected and ds:
-                dsrc = ds[0]
-                s.active_p.append(ActiveToken(gold_of[id(dsrc)], dsrc.position + 1, "draft"))
-                s.trace.n_p_calls += 1
-            s.active_c = []
-
-    return _finalize(bt, seqs, t0, blocks)
+        # prelude: queued tokens enter their lane's wave
+        entering = [(lane, f) for lane in live for f in lane.queue]
+        if entering:
+            blocks.prelude_union([lane.idx for lane, _ in entering], [f for _, f in entering], cache)
+            bt.count_union("P")
+            for lane, f in entering:
+                lane.wave[f.position] = f
+            for lane in live:
+                lane.queue = []
+        # one loop step for every token in flight
+        moving = [(lane, f) for lane in live for f in lane.wave.values()]
+        if moving:
+            _advance(blocks, cache, bt, moving)
+        # read-outs: full depth leaves the wave, draft depth is read in place
+        reads = []
+        for lane in live:
+            full = [f for f in lane.wave.values() if f.step == deep]
+            drafts = [f for f in lane.wave.values() if f.step == shallow and f.step != deep]
+            for f in full:
+                del lane.wave[f.position]
+            if full or drafts:
+                reads.append((lane, sorted(full, key=lambda f: f.position), drafts))
+        if not reads:
+            continue
+        rows = [(lane, f) for lane, full, drafts in reads for f in full + drafts]
+        heads = [int(x) for x in blocks.coda_argmax_union([lane.idx for lane, _ in rows], [f for _, f in rows],
+                                                          cache)]
+        bt.count_union("C")
+        at = 0
+        for lane, full, drafts in reads:
+            lane.trace.n_c_calls += 1
+            n_full = len(full)
+            _wave_settle(lane, full, heads[at:at + n_full], drafts, heads[at + n_full:at + n_full + len(drafts)],
+                         cache, max_new_tokens)
+            at += n_full + len(drafts)
+    raise RuntimeError(f"wavefront scheduler: no progress after {bound} ticks")
 
 
 # ---------------------------------------------------------------------------
-# draft-then-verify (scheduler_batch.py:365-501)
+# draft-then-verify
 # ---------------------------------------------------------------------------
-def _dtv_new_round(s: SeqState, max_new_tokens: int, draft_length: int) -> None:
-    """scheduler_batch.py:368-376: K = min(draft_length, tokens still to commit)
-    drafts, seeded by the last committed token."""
-    s.K = min(draft_length, max_new_tokens - len(s.committed))
-    s.j = 0
-    s.sources, s.drafts = [], []
-    s.cur_tok, s.cur_pos = s.last_token, s.p
-    s.phase = "need_p"
+class _DtvRound:
+    """One round of a lane: a chain of up to K + 1 sources, each run to draft
+    depth in turn (its read-out is the next source), then all verified together
+    at full depth."""
+    __slots__ = ("budget", "chain", "guesses", "stage", "next_tok", "next_pos")
+
+    def __init__(self, budget: int, seed_tok: int, seed_pos: int):
+        self.budget = budget        # drafts K of this round
+        self.chain: list[Flight] = []
+        self.guesses: list[int] = []
+        self.stage = "prelude"      # prelude -> draft (-> prelude -> draft ...) -> verify
+        self.next_tok, self.next_pos = seed_tok, seed_pos
+
+
+def _dtv_open(lane: _Lane, limit: int, draft_length: int) -> None:
+    lane.round = _DtvRound(min(draft_length, limit - lane.n_committed), lane.anchor_tok, lane.anchor_pos)
+
+
+def _dtv_verify(lane: _Lane, heads, cache, limit: int, draft_length: int) -> None:
+    """Source i's full-depth id checks guess i; the first mismatch is committed
+    in its place and the sequence's KV is dropped from there; a fully accepted
+    round also commits the last source's id."""
+    rnd, trace = lane.round, lane.trace
+    base = lane.anchor_pos
+    refuted = False
+    for i, guess in enumerate(rnd.guesses):
+        trace.n_drafts_proposed += 1
+        agree = lane.acceptance.draw() if lane.acceptance is not None else heads[i] == guess
+        if agree:
+            trace.n_drafts_accepted += 1
+            lane.emit(guess, limit)
+            if lane.finished:
+                break
+        else:
+            trace.n_drafts_rejected += 1
+            trace.n_rollback_events += 1
+            refuted = True
+            lane.emit(heads[i], limit)
+            cache.drop_positions_at_and_after(lane.idx, base + i + 1)
+            lane.anchor_tok, lane.anchor_pos = heads[i], base + i + 1
+            break
+    if not refuted and not lane.finished:
+        k = len(rnd.guesses)
+        lane.emit(heads[k], limit)
+        lane.anchor_tok, lane.anchor_pos = heads[k], base + k + 1
+    if lane.finished:
+        lane.retire()
+    else:
+        _dtv_open(lane, limit, draft_length)
 
 
 def generate_dtv_batch(blocks, prompt_ids, max_new_tokens: int, policy: SsdPolicy, draft_length: int,
                        emus: list | None = None) -> BatchTrace:
-    """Draft-then-verify over union P / R / C calls (scheduler_batch.py:378-501).
+    """Draft-then-verify over union P / R / C calls (scheduler_batch.py:365-501).
 
-    Each sequence runs rounds: source 0 is the last committed token; each source
-    goes through the prelude and T_draft loop steps, and its draft-depth greedy id
-    is the next source (draft d_{j+1}), K drafts per round.  Then all K + 1
-    sources advance together from T_draft to T_total (one window per sequence:
-    consecutive positions on one depth slot) and the full-depth ids verify the
-    drafts: accept while equal (emus[b] replaces the comparison), commit the
-    first gold on a reject and drop the cache from there, or commit the bonus
-    token when all K are accepted."""
+    A round of a sequence: K = min(draft_length, tokens still to commit)
+    drafts.  Source 0 is the last committed token; each source runs the prelude
+    and T_draft loop steps, and its greedy id there is the next source (a
+    draft).  Then the K + 1 sources advance together from T_draft to T_total
+    (one window per sequence: consecutive positions on one depth slot) and their
+    full-depth ids verify the drafts.  emus[b] replaces the comparison."""
     bt = BatchTrace()
     t0 = time.perf_counter()
-    cache, seqs = _prefill_and_first(blocks, prompt_ids, emus, max_new_tokens, bt, t0)
-    T_total, T_draft = policy.T_total, policy.T_draft
-    rows = getattr(blocks, "ensure_window_rows", None)
-    if rows is not None:
-        rows(draft_length + 1)   # the verify union attends K + 1 sources of a sequence as one window
-    for s in seqs:
-        if not s.done:
-            s.last_token, s.p = s.committed[-1], s.prefix_len
-            _dtv_new_round(s, max_new_tokens, draft_length)
-
-    ticks, max_ticks = 0, max_new_tokens * ((draft_length + 1) * max(T_draft, 1) + T_total + 4) + 100
-    while True:
-        alive = [s for s in seqs if not s.done]
-        if not alive:
+    cache, lanes = _start(blocks, prompt_ids, emus, max_new_tokens, bt, t0)
+    deep, shallow = policy.T_total, policy.T_draft
+    widen = getattr(blocks, "ensure_window_rows", None)
+    if widen is not None:
+        widen(draft_length + 1)   # the verify union attends a sequence's K + 1 sources as one window
+    for lane in lanes:
+        if not lane.finished:
+            lane.anchor_tok, lane.anchor_pos = lane.trace.tokens[-1], lane.prompt_len
+            _dtv_open(lane, max_new_tokens, draft_length)
+    bound = _tick_bound(max_new_tokens, (draft_length + 1) * shallow + deep)
+    for _tick in range(bound + 1):
+        live = [lane for lane in lanes if not lane.finished]
+        if not live:
+            return _close(bt, lanes, t0, blocks)
+        if _tick == bound:
             break
-        ticks += 1
-        if ticks > max_ticks:
-            raise RuntimeError(f"dtv batch exceeded the tick guard ({max_ticks})")
-
-        # P: sequences whose next source needs its prelude
-        need = [s for s in alive if s.phase == "need_p"]
-        if need:
+        # prelude: the next source of every round that needs one
+        starting = [lane for lane in live if lane.round.stage == "prelude"]
+        if starting:
             toks = []
-            for s in need:
-                t = ActiveToken(token_id=s.cur_tok, position=s.cur_pos, role="verify")
-                s.sources.append(t)
-                s.trace.n_p_calls += 1
-                s.phase = "draft"
-                toks.append(t)
-            blocks.prelude_union([s.idx for s in need], toks, cache)
-            bt.n_p_calls += 1
-
-        # R: a drafting sequence advances its current source, a verifying one all
-        # of its sources (until they reach full depth)
-        pairs, took = [], []
-        for s in alive:
-            if s.phase == "draft":
-                pairs.append((s, s.sources[-1]))
-                took.append(s)
-            elif s.phase == "verify" and s.sources[0].step < T_total:
-                pairs += [(s, t) for t in s.sources]
-                took.append(s)
-        if pairs:
-            blocks.advance_union([s.idx for s, _ in pairs], [t for _, t in pairs], cache)
-            _record_r(bt, len(pairs))
-            for s in took:
-                s.trace.n_r_calls += 1
-
-        # C: a draft (the current source reached T_draft) or the verify (all
-        # sources reached T_total)
-        entries = []
-        for s in alive:
-            if s.phase == "draft" and s.sources[-1].step == T_draft:
-                entries.append((s, "draft", [s.sources[-1]]))
-            elif s.phase == "verify" and s.sources[0].step == T_total:
-                entries.append((s, "verify", list(s.sources)))
-        if not entries:
+            for lane in starting:
+                rnd = lane.round
+                src = Flight(rnd.next_tok, rnd.next_pos)
+                rnd.chain.append(src)
+                rnd.stage = "draft"
+                lane.trace.n_p_calls += 1
+                toks.append(src)
+            blocks.prelude_union([lane.idx for lane in starting], toks, cache)
+            bt.count_union("P")
+        # loop step: the current source of a drafting round, or every source of
+        # a verifying round that has not reached full depth
+        moving = []
+        for lane in live:
+            rnd = lane.round
+            if rnd.stage == "draft":
+                moving.append((lane, rnd.chain[-1]))
+            elif rnd.stage == "verify" and rnd.chain[0].step < deep:
+                moving += [(lane, f) for f in rnd.chain]
+        if moving:
+            _advance(blocks, cache, bt, moving)
+        # read-outs: a source at draft depth, or a whole chain at full depth
+        reads = []
+        for lane in live:
+            rnd = lane.round
+            if rnd.stage == "draft" and rnd.chain[-1].step == shallow:
+                reads.append((lane, [rnd.chain[-1]]))
+            elif rnd.stage == "verify" and rnd.chain[0].step == deep:
+                reads.append((lane, list(rnd.chain)))
+        if not reads:
             continue
-        flat = [t for _, _, ts in entries for t in ts]
-        ids = blocks.coda_argmax_union([s.idx for s, _, ts in entries for _ in ts], flat, cache)
-        bt.n_c_calls += 1
-        k = 0
-        for s, kind, ts in entries:
-            out = [int(x) for x in ids[k:k + len(ts)]]
-            k += len(ts)
-            s.trace.n_c_calls += 1
-            if kind == "draft":
-                if s.j < s.K:
-                    s.drafts.append(out[0])          # d_{j+1}, at cur_pos + 1
-                s.cur_tok, s.cur_pos = out[0], s.cur_pos + 1
-                s.j += 1
-                s.phase = "need_p" if s.j <= s.K else "verify"
-                continue
-            # verify: source p + i predicts position p + i + 1
-            rejected = False
-            for i in range(s.K):
-                s.trace.n_drafts_proposed += 1
-                accept = s.emu.draw() if s.emu is not None else out[i] == s.drafts[i]
-                if accept:
-                    s.trace.n_drafts_accepted += 1
-                    s.commit(s.drafts[i])
-                    if len(s.committed) >= max_new_tokens:
-                        s.done = True
-                        break
-                else:
-                    s.trace.n_drafts_rejected += 1
-                    s.trace.n_rollback_events += 1
-                    rejected = True
-                    s.commit(out[i])
-                    cache.drop_positions_at_and_after(s.idx, s.p + i + 1)
-                    s.last_token, s.p = out[i], s.p + i + 1
-                    if len(s.committed) >= max_new_tokens:
-                        s.done = True
-                    break
-            if not rejected and not s.done:
-                s.commit(out[s.K])                   # every draft accepted: the bonus token
-                s.last_token, s.p = out[s.K], s.p + s.K + 1
-                if len(s.committed) >= max_new_tokens:
-                    s.done = True
-            if s.done:
-                s.clear_working_state()
+        heads = [int(x) for x in blocks.coda_argmax_union([lane.idx for lane, ts in reads for _ in ts],
+                                                          [f for _, ts in reads for f in ts], cache)]
+        bt.count_union("C")
+        at = 0
+        for lane, ts in reads:
+            mine = heads[at:at + len(ts)]
+            at += len(ts)
+            lane.trace.n_c_calls += 1
+            rnd = lane.round
+            if rnd.stage == "draft":
+                if len(rnd.chain) - 1 < rnd.budget:
+                    rnd.guesses.append(mine[0])     # the draft for the position after this source
+                rnd.next_tok, rnd.next_pos = mine[0], rnd.chain[-1].position + 1
+                rnd.stage = "prelude" if len(rnd.chain) <= rnd.budget else "verify"
             else:
-                _dtv_new_round(s, max_new_tokens, draft_length)
-    return _finalize(bt, seqs, t0, blocks)
-
+                _dtv_verify(lane, mine, cache, max_new_tokens, draft_length)
+    raise RuntimeError(f"draft-then-verify scheduler: no progress after {bound} ticks")
