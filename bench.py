@@ -34,8 +34,13 @@ e2e   : the same metric through the public Python / C-ABI call with host
         run on a copy stream while step i computes (double-buffered inputs).
 Multi-GPU (torchrun): every rank runs its own independent batch (weak scaling);
 the only collectives are the timing max and a final counter gather.
+cfg4_e2e (default line only, --no-cfg4-e2e skips it): a short config-4
+generation (64 new tokens, T_draft 2, the 64 sequences sharded over the ranks)
+timed after the cfg2 measurement, so a 1 -> N GPU series of default runs also
+records end-to-end strong scaling.
 --impl reference: the reference's CPU path (write_tokens + gather_pack + SDPA
-varlen loop, restated in oracle/cpu_path.py) on the host cores, rank 0 only.
+varlen loop, restated in oracle/cpu_path.py) on all host cores (whatever
+OMP_NUM_THREADS says), rank 0 only, with the repo arm's config.
 """
 from __future__ import annotations
 
@@ -68,11 +73,9 @@ CFG4A = dict(B=64, R=8, H=24, Hkv=24, Dh=64, S=1100, seed=4)
 CFG5 = dict(B=64, R=16, H=32, Hkv=8, Dh=128, L0=32768, W=8, seed=5, alpha=0.8)
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# timed attention kernel, from the ncu captures summarised under profiles/
-# (wave_decode_cfg2.md for the CUDA-core kernel, wave_tc_cfg2.md / wave_tc_cfg3.md /
-# wave_tc_cfg4attn.md / wave_tc_cfg5.md for tcgen05).
-# cfg3 was captured at batch 8 and cfg5 at batch 2, scaled by the units processed
-# (x4 to batch 32, x32 to batch 64).
+# timed attention kernel, from one ncu capture of that kernel on the same
+# workload.  cfg3 was captured at batch 8 and cfg5 at batch 2, scaled by the
+# units processed (x4 to batch 32, x32 to batch 64).
 NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
                      ("cfg2", "tc"): 543_152_128 + 4_816_384,
                      ("cfg3", "tc"): (2_189_589_504 + 9_263_104) * 4,
@@ -132,6 +135,8 @@ def parse():
                          "(bit-exact greedy equality with sequential decoding)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cfg4-e2e", action="store_true",
+                    help="cfg2: skip the short config-4 end-to-end generation recorded beside the line")
     ap.add_argument("--kernel", type=int, default=-1, choices=[-1, 0, 1],
                     help="-1 library default, 0 CUDA-core decode kernel, 1 tcgen05 kernel")
     return ap.parse_args()
@@ -347,11 +352,26 @@ def cfg3_cpu_sample(K, V, q, kn, vn, items, n_items: int = 4):
     return Kc, Vc, torch.cat(qs), torch.cat(ks), torch.cat(vs), its
 
 
+def host_threads() -> int:
+    """Every core this process may run on, whatever OMP_NUM_THREADS says (torchrun
+    sets it to 1 per rank): the CPU baseline gets the whole host."""
+    import torch
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(max(1, n))
+    return torch.get_num_threads()
+
+
 def run_reference(args):
-    """--impl reference: the reference's CPU path, rank 0 only."""
+    """--impl reference: the reference's CPU path on all host cores, rank 0 only
+    (the other ranks exit without work)."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
+    host_threads()
     if args.workload == "cfg4":
         print(json.dumps({"impl": "reference", "unavailable": "cfg4 (end-to-end 381M-parameter model, 64 x 1024 "
                           "prompts, 256 tokens) is not timed on the host cores; the reference arm covers the "
@@ -359,6 +379,7 @@ def run_reference(args):
         return
     if args.workload == "cfg2":
         c, q, K, V, kn, vn, items = cfg2_cpu_inputs(CFG2["seed"], args.batch)
+        full_items = items
         label = "cfg2 decode"
     else:
         import torch
@@ -373,14 +394,16 @@ def run_reference(args):
             base = CFG3 if args.workload == "cfg3" else CFG5
             c, q, K, V, kn, vn, items, _ = cfg3_device_inputs(dev, base["seed"], args.batch, base,
                                                               args.alpha if args.workload == "cfg5" else None)
+        full_items = items
         K, V, q, kn, vn, items = cfg3_cpu_sample(K, V, q, kn, vn, items)
         label = f"{args.workload} verify"
     base, n, dt = cpu_baseline(q, K, V, kn, vn, items, 90.0, warmup=max(1, args.warmup), steps=max(1, args.steps),
                                label=label)
+    _, rows = algorithmic_bytes(full_items, c["H"], c["Hkv"], c["Dh"])
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
             "steps": n, "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": workload_config(args.workload, c, 1),
+            "config": workload_config(args.workload, c, world, rows),
             "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -600,12 +623,19 @@ def run_wfd(args):
             # tokens one verify step commits per sequence: accepted drafts + the corrected / bonus token
             line["tokens_per_s"] = world * sum(a + 1 for a in c["accepted"]) / (ms * 1e-3)
             line["accepted_mean"] = sum(c["accepted"]) / len(c["accepted"])
+    if args.workload == "cfg2" and not args.no_cfg4_e2e:
+        del g
+        torch.cuda.empty_cache()
+        rec = cfg4_e2e_record(dev, world, rank)
+        if rank == 0:
+            line["cfg4_e2e"] = rec
     if world > 1:
         dist.barrier(device_ids=[local])
-        del g
+        g = None
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
+            host_threads()
             if args.workload == "cfg2":
                 base, _, _ = cpu_baseline(q, K, V, kn, vn, items, args.cpu_seconds)
             else:
@@ -616,6 +646,123 @@ def run_wfd(args):
         else:
             line["cpu_baseline"] = None
         print(json.dumps(line), flush=True)
+
+
+def cfg4_measure(dev, world: int, rank: int, *, batch: int, new: int, t_draft: int, scheduler: str = "device",
+                 kv_budget: int = 0, batch_invariant: bool = False, alpha: float | None = None,
+                 draft_length: int = 8, warmup: int = 1, steps: int = 1) -> dict:
+    """Config 4 generation on this rank's shard of `batch` sequences: warm-up
+    generations, then `steps` timed ones.  Device times are CUDA events; the
+    results are reduced over ranks (max time, summed counts)."""
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from wavefront_decoding_b200 import runtime as rt
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import DeviceWave
+    from wavefront_decoding_b200.engine import WaveEngine
+    from wavefront_decoding_b200.looped_lm import CONFIG4, LoopedLM
+    from wavefront_decoding_b200.parallel import reduce_over_ranks, shard_range
+
+    cfg = dataclasses.replace(CONFIG4, kv_budget_s=kv_budget)
+    s0, s1 = shard_range(batch, world, rank)
+    Bl = s1 - s0
+    if Bl < 1:
+        raise SystemExit(f"global batch {batch} leaves rank {rank} of {world} without sequences")
+    L = CFG4["L"]
+    prompts_all = torch.randint(0, cfg.vocab, (batch, L), generator=torch.Generator().manual_seed(CFG4["seed"]))
+    prompts = prompts_all[s0:s1].contiguous().pin_memory()
+    model = LoopedLM(cfg, seed=CFG4["model_seed"], dtype=torch.bfloat16, device=dev)
+    eng = WaveEngine(model, Bl, L + new + 2 * cfg.T_total + 8)
+    policy = sch.SsdPolicy(cfg.T_total, t_draft)
+    dwave = DeviceWave(eng, new, policy, batch_invariant) if scheduler == "device" else None
+
+    ev_all0, ev_dec0, ev_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+
+    def generate():
+        emus = None
+        if alpha is not None:
+            emus = [sch.EmulatedAcceptance(alpha, seed=CFG4["emu_seed"] * 1_000_003 + s0 + b) for b in range(Bl)]
+        orig = eng.prefill
+
+        def prefill(ids):
+            out = orig(ids)
+            ev_dec0.record()
+            return out
+
+        eng.prefill = prefill
+        try:
+            ev_all0.record()
+            if dwave is not None:
+                bt = dwave.generate(prompts, emus)
+            elif scheduler == "dtv":
+                bt = sch.generate_dtv_batch(eng, prompts, new, policy, draft_length, emus)
+            else:
+                bt = sch.generate_wavefront_batch(eng, prompts, new, policy, emus)
+            ev_end.record()
+            torch.cuda.synchronize()
+        finally:
+            del eng.prefill
+        return bt, ev_dec0.elapsed_time(ev_end), ev_all0.elapsed_time(ev_end)
+
+    for _ in range(max(1, warmup)):
+        generate()
+    rt.read_device_error(dev)
+    eng.reset_counters()
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize()
+    dec_ms = all_ms = 0.0
+    tokens = proposed = accepted = ticks = 0
+    kv_dev = launches_dev = 0
+    # libwfd kernels of one device tick: 3 scheduling kernels + the P / R / C bodies
+    tick_launches = 3 + sum(eng._launches.values())
+    with ClockSampler(dev.index) as clk:
+        for _ in range(steps):
+            bt, d_ms, a_ms = generate()
+            dec_ms += d_ms
+            all_ms += a_ms
+            tokens += bt.n_tokens
+            proposed += sum(t.n_drafts_proposed for t in bt.per_seq)
+            accepted += sum(t.n_drafts_accepted for t in bt.per_seq)
+            ticks += bt.n_r_calls
+            if dwave is not None:
+                kv_dev += dwave.kv_read_bytes
+                launches_dev += tick_launches * dwave.ticks_replayed
+    torch.cuda.synchronize()
+    rt.read_device_error(dev)
+    kv_bytes = eng.kv_read_bytes if dwave is None else kv_dev
+    launches = eng.wfd_launches if dwave is None else launches_dev
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    (dec_max, all_max), (tot_tokens, tot_prop, tot_acc, tot_kv) = reduce_over_ranks(
+        [dec_ms, all_ms], [tokens, proposed, accepted, kv_bytes], dev)
+    d2h = (eng.d2h_bytes // steps) if dwave is None else dwave.d2h_bytes
+    return dict(cfg=cfg, Bl=Bl, dec_max=dec_max, all_max=all_max, tot_tokens=tot_tokens, tot_prop=tot_prop,
+                tot_acc=tot_acc, kv_bytes=kv_bytes, dec_ms=dec_ms, ticks=ticks, launches=launches,
+                h2d=prompts.numel() * prompts.element_size(), d2h=d2h, clocks=clk.summary())
+
+
+# the short config-4 generation recorded next to the default (config-2) line, so
+# the 1 -> N GPU runs also record end-to-end strong scaling
+CFG4_E2E_NEW = 64
+
+
+def cfg4_e2e_record(dev, world: int, rank: int) -> dict:
+    r = cfg4_measure(dev, world, rank, batch=CFG4["B"], new=CFG4_E2E_NEW, t_draft=2, warmup=1, steps=1)
+    return {"metric": "WFD decode tokens/s (config 4, end to end)", "unit": "tokens/s", "scaling": "strong",
+            "value": r["tot_tokens"] / (r["dec_max"] * 1e-3),
+            "e2e": r["tot_tokens"] / (r["all_max"] * 1e-3),
+            "tokens_per_s_per_gpu": r["tot_tokens"] / (r["dec_max"] * 1e-3) / world,
+            "ms_decode": r["dec_max"], "ms_with_prefill": r["all_max"],
+            "acceptance_rate": (r["tot_acc"] / r["tot_prop"]) if r["tot_prop"] else None,
+            "config": {"model": "looped LM 770M (config 4), random init, bf16", "global_batch": CFG4["B"],
+                       "batch_per_gpu": r["Bl"], "prompt_len": CFG4["L"], "new_tokens": CFG4_E2E_NEW,
+                       "T_draft": 2, "scheduler": "device", "parallelism": f"sequences sharded, {world} rank(s)"},
+            "timing": "one timed generation after one warm-up, CUDA events, max over ranks; value = decode "
+                      "region, e2e = with prompt upload and prefill"}
 
 
 def run_cfg4(args):
@@ -632,103 +779,23 @@ def run_cfg4(args):
     dev = torch.device("cuda", local)
     if world > 1:
         init_dist(dev, 600)
-
-    import __graft_entry__
-    __graft_entry__.load_package()
-    from wavefront_decoding_b200 import runtime as rt
-    from wavefront_decoding_b200 import scheduler as sch
-    from wavefront_decoding_b200.device_scheduler import DeviceWave
-    from wavefront_decoding_b200.engine import WaveEngine
-    from wavefront_decoding_b200.looped_lm import CONFIG4, LoopedLM
-
-    from wavefront_decoding_b200.parallel import reduce_over_ranks, shard_range
-    cfg = dataclasses.replace(CONFIG4, kv_budget_s=args.kv_budget)
     Bg = args.batch or CFG4["B"]
-    s0, s1 = shard_range(Bg, world, rank)
-    Bl = s1 - s0
-    if Bl < 1:
-        raise SystemExit(f"global batch {Bg} leaves rank {rank} of {world} without sequences")
-    L, new = CFG4["L"], args.new_tokens or CFG4["new"]
-    prompts_all = torch.randint(0, cfg.vocab, (Bg, L), generator=torch.Generator().manual_seed(CFG4["seed"]))
-    prompts = prompts_all[s0:s1].contiguous().pin_memory()
-    model = LoopedLM(cfg, seed=CFG4["model_seed"], dtype=torch.bfloat16, device=dev)
-    eng = WaveEngine(model, Bl, L + new + 2 * cfg.T_total + 8)
-    policy = sch.SsdPolicy(cfg.T_total, args.t_draft)
-    dwave = DeviceWave(eng, new, policy, args.batch_invariant) if args.scheduler == "device" else None
-
-    ev_all0, ev_dec0, ev_end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-
-    def generate():
-        emus = None
-        if args.alpha is not None:
-            emus = [sch.EmulatedAcceptance(args.alpha, seed=CFG4["emu_seed"] * 1_000_003 + rank * Bl + b)
-                    for b in range(Bl)]
-        orig = eng.prefill
-
-        def prefill(ids):
-            out = orig(ids)
-            ev_dec0.record()
-            return out
-
-        eng.prefill = prefill
-        try:
-            ev_all0.record()
-            if dwave is not None:
-                bt = dwave.generate(prompts, emus)
-            elif args.scheduler == "dtv":
-                bt = sch.generate_dtv_batch(eng, prompts, new, policy, args.draft_length, emus)
-            else:
-                bt = sch.generate_wavefront_batch(eng, prompts, new, policy, emus)
-            ev_end.record()
-            torch.cuda.synchronize()
-        finally:
-            del eng.prefill
-        return bt, ev_dec0.elapsed_time(ev_end), ev_all0.elapsed_time(ev_end)
-
-    for _ in range(max(1, args.warmup)):
-        generate()
-    rt.read_device_error(dev)
-    eng.reset_counters()
-    if world > 1:
-        dist.barrier(device_ids=[local])
-    torch.cuda.synchronize()
-    dec_ms = all_ms = 0.0
-    tokens = proposed = accepted = ticks = 0
-    kv_dev = launches_dev = 0
-    # libwfd kernels of one device tick: 3 scheduling kernels + the P / R / C bodies
-    tick_launches = 3 + sum(eng._launches.values())
-    with ClockSampler(local) as clk:
-        for _ in range(args.steps):
-            bt, d_ms, a_ms = generate()
-            dec_ms += d_ms
-            all_ms += a_ms
-            tokens += bt.n_tokens
-            proposed += sum(t.n_drafts_proposed for t in bt.per_seq)
-            accepted += sum(t.n_drafts_accepted for t in bt.per_seq)
-            ticks += bt.n_r_calls
-            if dwave is not None:
-                kv_dev += dwave.kv_read_bytes
-                launches_dev += tick_launches * dwave.ticks_replayed
-    torch.cuda.synchronize()
-    rt.read_device_error(dev)
-    kv_bytes = eng.kv_read_bytes if dwave is None else kv_dev
-    launches = eng.wfd_launches if dwave is None else launches_dev
-    if world > 1:
-        dist.barrier(device_ids=[local])
-    (dec_max, all_max), (tot_tokens, tot_prop, tot_acc, tot_kv) = reduce_over_ranks(
-        [dec_ms, all_ms], [tokens, proposed, accepted, kv_bytes], dev)
+    new = args.new_tokens or CFG4["new"]
+    r = cfg4_measure(dev, world, rank, batch=Bg, new=new, t_draft=args.t_draft, scheduler=args.scheduler,
+                     kv_budget=args.kv_budget, batch_invariant=args.batch_invariant, alpha=args.alpha,
+                     draft_length=args.draft_length, warmup=args.warmup, steps=args.steps)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank != 0:
         return
+    cfg, Bl = r["cfg"], r["Bl"]
     peak, peak_kind = measured_peak()
-    value = tot_tokens / (dec_max * 1e-3)
-    kv_gbs = kv_bytes / (dec_ms * 1e-3) / 1e9      # rank 0's attention KV reads over its decode time
-    h2d = prompts.numel() * prompts.element_size()
+    value = r["tot_tokens"] / (r["dec_max"] * 1e-3)
+    kv_gbs = r["kv_bytes"] / (r["dec_ms"] * 1e-3) / 1e9      # rank 0's attention KV reads over its decode time
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(1, args.warmup), "ms_per_step": dec_max / args.steps, "higher_is_better": True,
+        "warmup": max(1, args.warmup), "ms_per_step": r["dec_max"] / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, "
         "uniform random prompt ids)",
         "config": {"workload": "cfg4_looped_lm_e2e_greedy_decode",
@@ -736,7 +803,7 @@ def run_cfg4(args):
                             f"{cfg.n_heads}x{cfg.head_dim} heads (kv {cfg.n_kv_heads}), SwiGLU {cfg.d_ff}, "
                             f"prelude {cfg.n_prelude} / core {cfg.n_core} x R={cfg.T_total} / coda {cfg.n_coda}",
                    "global_batch": Bg, "batch_per_gpu": Bl if Bg % world == 0 else f"{Bg // world}-{-(-Bg // world)}",
-                   "prompt_len": L, "new_tokens": new,
+                   "prompt_len": CFG4["L"], "new_tokens": new,
                    "T_draft": args.t_draft, "scheduler": args.scheduler, "batch_invariant": args.batch_invariant,
                    "draft_length": args.draft_length if args.scheduler == "dtv" else None,
                    "kv_budget_s": args.kv_budget,
@@ -745,18 +812,17 @@ def run_cfg4(args):
                    "timing": "decode region per generation, CUDA events, max over ranks; "
                              "KV working set > L2, no flush"},
         "tokens_per_s_per_gpu": value / world,
-        "acceptance_rate": (tot_acc / tot_prop) if tot_prop else None,
-        "ticks_per_generation": ticks / args.steps,
+        "acceptance_rate": (r["tot_acc"] / r["tot_prop"]) if r["tot_prop"] else None,
+        "ticks_per_generation": r["ticks"] / args.steps,
         "roofline": {"bound": "hbm", "achieved": kv_gbs, "peak": peak, "unit": "GB/s", "frac": kv_gbs / peak,
                      "peak_kind": peak_kind, "traffic": None,
                      "note": "attention K/V bytes read by live rows over the whole decode wall time "
                              "(GEMMs, host scheduling and launches included in the time)"},
-        "e2e": {"value": tot_tokens / (all_max * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": eng.d2h_bytes // args.steps if dwave is None else dwave.d2h_bytes,
-                "ms_per_step": all_max / args.steps,
+        "e2e": {"value": r["tot_tokens"] / (r["all_max"] * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
+                "d2h_bytes_per_step": r["d2h"], "ms_per_step": r["all_max"] / args.steps,
                 "includes": "prefill, prompt upload from pinned host memory, per-tick greedy-id read-back"},
-        "gpu_launches": launches,
-        "clocks": clk.summary(),
+        "gpu_launches": r["launches"],
+        "clocks": r["clocks"],
         "cpu_baseline": None,
     }
     print(json.dumps(line), flush=True)

@@ -138,3 +138,44 @@ def test_oracle_wave_equals_write_pack_varlen():
     mask = torch.arange(23)[None, :] <= (torch.arange(3)[:, None] + 20)
     ref = torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, attn_mask=mask[None, None], enable_gqa=True)
     assert np.abs(out[1:4] - ref.transpose(1, 2)[0].numpy()).max() < 1e-10
+
+
+# ---------------------------------------------------------------------------
+# the timed CPU restatement (bench.py's cpu_baseline / reference arm) computes
+# what the reference computes
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("case", [c for c in gi.VARLEN_CASES if c["dtype"] == "f32"],
+                         ids=[c["name"] for c in gi.VARLEN_CASES if c["dtype"] == "f32"])
+def test_cpu_path_varlen_matches_golden(golden, case):
+    from oracle import cpu_path
+    q, k, v, cu_q, cu_k = gi.varlen_inputs(case)
+    out = cpu_path.attn_varlen_sdpa(q, k, v, cu_q, cu_k, case["causal"])
+    assert float(np.abs(out.double().numpy() - golden[f"varlen/{case['name']}/out"]).max()) < 1e-5
+
+
+@pytest.mark.parametrize("windows", [False, True], ids=["decode", "windows"])
+def test_cpu_path_wave_step_matches_oracle(windows):
+    """write_tokens + gather_pack + SDPA varlen on the host, fp32: the same
+    outputs (1e-5) and cache contents (exact) as the oracle's wave step."""
+    from oracle import cpu_path
+    g = gi.gen(19)
+    n_slots, B, S, H, Hkv, Dh = 3, 2, 80, 8, 2, 64
+    if windows:
+        items = [[0, 0, 40, 4, 0], [1, 1, 70, 1, 4], [2, 0, 10, 8, 5], [2, 1, 0, 3, 13]]
+    else:
+        items = [[r, b, 60 - 9 * r - b, 1, r * B + b] for r in range(n_slots) for b in range(B)]
+    rows = max(it[4] + it[3] for it in items)
+    K = gi.randn((n_slots, B, S, Hkv, Dh), g, torch.float32)
+    V = gi.randn((n_slots, B, S, Hkv, Dh), g, torch.float32)
+    q = gi.randn((rows, H, Dh), g, torch.float32)
+    kn = gi.randn((rows, Hkv, Dh), g, torch.float32)
+    vn = gi.randn((rows, Hkv, Dh), g, torch.float32)
+    o = SlotCacheOracle(n_slots, B, Hkv, Dh, S)
+    o.K[:] = K.numpy()
+    o.V[:] = V.numpy()
+    ref = o.wave_attn(q.numpy(), kn.numpy(), vn.numpy(), items)
+    Kc, Vc = K.clone(), V.clone()
+    out = cpu_path.wave_step(Kc, Vc, q, kn, vn, items).double().numpy()
+    order = [it[4] + j for it in items for j in range(it[3])]   # wave_step packs rows in item order
+    assert float(np.abs(out - ref[order]).max()) < 1e-5
+    assert np.array_equal(Kc.numpy(), o.K) and np.array_equal(Vc.numpy(), o.V)
