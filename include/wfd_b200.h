@@ -231,6 +231,18 @@ int wfd_commit_window(void* k_cache, void* v_cache, int32_t* lens, const wfd_ite
                       int32_t max_seq, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, int32_t* d_err,
                       void* stream);
 
+/* Dense prompt attention over n_seqs segments of equal lengths (the prompt pass,
+ * write_prefill + attn_dense of the reference, ouro_blocks_batch.py:123-144,
+ * fa4_attention.py:191-232): q (n_seqs * q_len, Hq, Dh), k / v (n_seqs * k_len,
+ * Hkv, Dh), out like q.  causal != 0: bottom-right causal per segment (row i
+ * sees keys j <= i + k_len - q_len; q_len == k_len is the ordinary causal
+ * mask), else every row sees its whole segment.  bf16, head_dim 64 or 128 (the
+ * tcgen05 prompt kernel); other dtypes / head dims return WFD_ERR_UNSUPPORTED.
+ * scale <= 0 selects 1/sqrt(head_dim).  Rows that see no key get zeros. */
+int wfd_attn_prefill(const void* q, const void* k, const void* v, void* out, int32_t n_seqs, int32_t q_len,
+                     int32_t k_len, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
+                     int32_t causal, float scale, int32_t* d_err, void* stream);
+
 /* Gather packed prefixes, BatchStaticKVCache.gather_pack (batch_kv_cache.py:75-96):
  * segment i copies positions [0, uptos[i]] of (slots[i], seqs[i]) into rows
  * cu_k[i] .. of k_pack / v_pack.  cu_k (n+1) is a DEVICE int32 array the caller

@@ -21,6 +21,7 @@ WFD_DTYPE_F32 = 1
 EXPORTED = (
     "wfd_abi_version", "wfd_status_string", "wfd_read_error", "wfd_workspace_bytes", "wfd_workspace_init",
     "wfd_wave_attn", "wfd_wave_attn_static", "wfd_wave_attn_kernel", "wfd_attn_varlen", "wfd_attn_segments",
+    "wfd_attn_prefill",
     "wfd_append",
     "wfd_write_prefill", "wfd_commit_drop", "wfd_commit_window", "wfd_gather_pack",
     "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul", "wfd_gather_rows", "wfd_scatter_rows",
@@ -79,6 +80,8 @@ _SIGS = {
     "wfd_attn_varlen": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P, _P], _I),
     # q k v out q_row0 q_len k_row0 k_len n max_q total_q total_k Hq Hkv Dh dtype causal scale ws ws_bytes err stream
     "wfd_attn_segments": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P, _P], _I),
+    # q k v out n_seqs q_len k_len Hq Hkv Dh dtype causal scale err stream
+    "wfd_attn_prefill": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P], _I),
     # k_new v_new kc vc lens slots seqs positions n slot_off n_slots n_seqs max_seq Hkv Dh dtype err stream
     "wfd_append": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     # k v kc vc lens slot L n_slots n_seqs max_seq Hkv Dh dtype stream

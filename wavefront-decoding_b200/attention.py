@@ -99,13 +99,42 @@ def attn_segments(q, k, v, q_row0, q_len, k_row0, k_len, max_q, causal: bool, *,
     return out
 
 
+# Query rows per segment from which dense attention runs on the prompt kernel
+# (query-major tcgen05 tiles of 128 rows) instead of the decode / verify kernels.
+PREFILL_MIN_ROWS = 64
+
+
+def attn_prefill(q, k, v, *, causal: bool, scale: float | None = None, out: torch.Tensor | None = None):
+    """Dense prompt attention on the tcgen05 prompt kernel (wfd_attn_prefill):
+    q (B, Tq, H, Dh), k / v (B, Tk, Hkv, Dh), bf16, Dh 64 or 128; causal is
+    bottom-right aligned.  The prompt pass of every layer (write_prefill +
+    attn_dense, ouro_blocks_batch.py:123-144)."""
+    dev = rt.require_cuda(q, k, v)
+    B, Tq, H, Dh = q.shape
+    Tk, Hkv = k.shape[1], k.shape[2]
+    _heads(q, k)
+    if v.shape != k.shape or k.shape[0] != B:
+        raise ValueError("attn_prefill expects q (B, Tq, H, Dh), k / v (B, Tk, Hkv, Dh)")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    st = _abi.load().wfd_attn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, Tq, Tk, H, Hkv, Dh,
+                                      rt.dtype_code(q.dtype), 1 if causal else 0, float(scale or 0.0),
+                                      rt.error_word(dev).data_ptr(), rt.stream_ptr(dev))
+    _abi.check(st, "wfd_attn_prefill")
+    return out
+
+
 def attn_dense(q, k, v, *, causal: bool):
     """Reference `attn_dense` (fa4_attention.py:191-232): per batch element,
     Tq=1 or causal=False sees the whole prefix; causal is bottom-right aligned
-    (Tq == Tk is the ordinary causal mask)."""
+    (Tq == Tk is the ordinary causal mask).  bf16 prompts (Tq >= 64, head_dim
+    64 / 128) run on the prompt kernel, everything else on the varlen path."""
     rt.require_cuda(q, k, v)
     B, Tq, H, Dh = q.shape
     Tk = k.shape[1]
+    if q.dtype == torch.bfloat16 and Dh in (64, 128) and Tq >= PREFILL_MIN_ROWS:
+        return attn_prefill(q, k, v, causal=bool(causal) and Tq > 1)
     qf = q.reshape(B * Tq, H, Dh)
     kf = k.reshape(B * Tk, k.shape[2], Dh)
     vf = v.reshape(B * Tk, v.shape[2], Dh)

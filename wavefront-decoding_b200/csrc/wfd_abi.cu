@@ -18,6 +18,7 @@
 #include "wfd_model.cuh"
 #include "wfd_sched.cuh"
 #include "wfd_plan.cuh"
+#include "wfd_prefill.cuh"
 #include "wfd_verify.cuh"
 
 using namespace wfd;
@@ -716,6 +717,65 @@ int wfd_attn_segments(const void* q, const void* k, const void* v, void* out, co
   A.which = -1;
   A.key_rows = total_k;
   return run_attention(A, static_cast<cudaStream_t>(stream));
+}
+
+int wfd_attn_prefill(const void* q, const void* k, const void* v, void* out, int32_t n_seqs, int32_t q_len,
+                     int32_t k_len, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
+                     int32_t causal, float scale, int32_t* d_err, void* stream) {
+  if (dtype != WFD_DTYPE_BF16 || (head_dim != 64 && head_dim != 128)) return WFD_ERR_UNSUPPORTED;
+  if (n_seqs < 0 || q_len < 0 || k_len < 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0)
+    return WFD_ERR_INVALID_ARG;
+  if (n_seqs == 0 || q_len == 0) return WFD_OK;
+  if (!q || !k || !v || !out) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return WFD_ERR_ALIGNMENT;
+  const long long q_rows = (long long)n_seqs * q_len, k_rows = (long long)n_seqs * k_len;
+  if (k_len == 0 || q_rows >= (1ll << 31) || k_rows >= (1ll << 31)) return WFD_ERR_UNSUPPORTED;
+  const int sms = current_sms();
+  if (sms <= 0) return WFD_ERR_CUDA;
+  CUtensorMap tq, tk, tv;
+  if (!make_kv_map(&tq, q, q_rows, n_heads, head_dim) || !make_kv_map(&tk, k, k_rows, n_kv_heads, head_dim) ||
+      !make_kv_map(&tv, v, k_rows, n_kv_heads, head_dim))
+    return WFD_ERR_CUDA;
+  PrefillParams pp;
+  memset(&pp, 0, sizeof(pp));
+  pp.out = out;
+  pp.n_seqs = n_seqs;
+  pp.Lq = q_len;
+  pp.Lk = k_len;
+  pp.Hq = n_heads;
+  pp.Hkv = n_kv_heads;
+  pp.G = n_heads / n_kv_heads;
+  pp.causal = causal ? 1 : 0;
+  pp.n_qb = (q_len + 127) / 128;
+  pp.scale_log2 = (scale > 0.f ? scale : 1.0f / std::sqrt((float)head_dim)) * 1.4426950408889634f;
+  pp.err = d_err;
+  const long long tiles = (long long)n_seqs * n_heads * pp.n_qb;
+  if (tiles >= (1ll << 31)) return WFD_ERR_UNSUPPORTED;
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr64[kMaxDevices] = {}, attr128[kMaxDevices] = {};
+  cudaError_t e;
+  if (head_dim == 64) {
+    if (!attr64[dev]) {
+      if (cudaFuncSetAttribute(prefill_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfCfg<64>::SMEM) !=
+          cudaSuccess)
+        return WFD_ERR_CUDA;
+      attr64[dev] = true;
+    }
+    e = launch_pdl(prefill_tc_kernel<64>, dim3(grid), dim3(kPfThreads), PfCfg<64>::SMEM, st, tq, tk, tv, pp);
+  } else {
+    if (!attr128[dev]) {
+      if (cudaFuncSetAttribute(prefill_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PfCfg<128>::SMEM) != cudaSuccess)
+        return WFD_ERR_CUDA;
+      attr128[dev] = true;
+    }
+    e = launch_pdl(prefill_tc_kernel<128>, dim3(grid), dim3(kPfThreads), PfCfg<128>::SMEM, st, tq, tk, tv, pp);
+  }
+  if (e != cudaSuccess) return WFD_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
 int wfd_append(const void* k_new, const void* v_new, void* k_cache, void* v_cache, int32_t* lens,

@@ -25,8 +25,8 @@ import math
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
 
+from . import attention
 from . import fused
 
 
@@ -197,9 +197,8 @@ class LoopedLM:
         def dense_block(blk, x, slot):
             q, k, v = self.qkv(blk, x, pos_period=L)                     # (B, L, H|Hkv, Dh)
             cache.write_prefill(slot, k, v)
-            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                               is_causal=True, enable_gqa=cfg.n_heads != cfg.n_kv_heads)
-            return self.finish_block(blk, x, o.transpose(1, 2))
+            o = attention.attn_dense(q, k, v, causal=True)               # (B, L, H, Dh), libwfd kernels
+            return self.finish_block(blk, x, o)
 
         x = self.embed[ids]
         for i, blk in enumerate(self.prelude):
