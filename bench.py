@@ -71,13 +71,18 @@ CFG4A = dict(B=64, R=8, H=24, Hkv=24, Dh=64, S=1100, seed=4)
 # config 5 as stated needs 9.1 GB of KV per sequence (128 / GPU: 1.17 TB); the stated
 # reduction measured here: one layer's 16 loop-depth slots, 64 sequences per GPU (137 GB)
 CFG5 = dict(B=64, R=16, H=32, Hkv=8, Dh=128, L0=32768, W=8, seed=5, alpha=0.8)
+# config 5 with the reference's KV sharing kv_budget_s = 1 (parcae_blocks.py:77-81): every
+# loop depth of a layer shares one slot, so a sequence holds 8 slots (2 prelude + 4 core +
+# 2 coda) of 32768 positions, 1.07 GB, and 128 sequences per GPU fit (137 GB); the
+# tokens a sequence has in flight on a layer form one 8-row window on that slot
+CFG5S1 = dict(CFG5, B=128, R=1, kv_budget=1)
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # timed attention kernel, from one ncu capture of that kernel on the same
 # workload.  cfg3 was captured at batch 8 and cfg5 at batch 2, scaled by the
 # units processed (x4 to batch 32, x32 to batch 64).
 NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
-                     ("cfg2", "tc"): 543_152_128 + 4_816_384,
+                     ("cfg2", "tc"): 543_108_096 + 4_301_568,
                      ("cfg3", "tc"): (2_189_589_504 + 9_263_104) * 4,
                      ("cfg4attn", "tc"): 3_631_393_536 + 6_166_272,
                      ("cfg5", "tc"): (4_314_130_176 + 6_834_176) * 32}
@@ -90,6 +95,8 @@ def ncu_traffic(workload: str, tc: bool, c: dict):
     if t is None:
         return None
     base = {"cfg2": CFG2, "cfg3": CFG3, "cfg4attn": CFG4A, "cfg5": CFG5}[workload]
+    if workload == "cfg5" and c.get("kv_budget") == 1:
+        return None  # captured for the 16-slot layout only
     return int(t * c["B"] / base["B"])
 
 
@@ -129,7 +136,8 @@ def parse():
                          "or draft-then-verify (host)")
     ap.add_argument("--draft-length", type=int, default=8, help="cfg4 with --scheduler dtv: drafts per round")
     ap.add_argument("--kv-budget", type=int, default=0,
-                    help="cfg4: KV-sharing budget s (core depth r keeps its K/V in slot r %% s); 0 = off")
+                    help="cfg4: KV-sharing budget s (core depth r keeps its K/V in slot r %% s); 0 = off; "
+                         "cfg5: 1 = the kv_budget_s=1 layout (128 sequences per GPU, one slot per layer)")
     ap.add_argument("--batch-invariant", action="store_true",
                     help="cfg4 (device scheduler): fixed union capacities + batch-invariant attention "
                          "(bit-exact greedy equality with sequential decoding)")
@@ -391,7 +399,7 @@ def run_reference(args):
             c = dict(CFG4A, **({"B": args.batch} if args.batch else {}))
             c, q, K, V, kn, vn, items = decode_device_inputs(dev, c, c["seed"])
         else:
-            base = CFG3 if args.workload == "cfg3" else CFG5
+            base = CFG3 if args.workload == "cfg3" else (CFG5S1 if args.kv_budget == 1 else CFG5)
             c, q, K, V, kn, vn, items, _ = cfg3_device_inputs(dev, base["seed"], args.batch, base,
                                                               args.alpha if args.workload == "cfg5" else None)
         full_items = items
@@ -422,6 +430,14 @@ def workload_config(name, c, world, rows=None):
         d = {"workload": "cfg3_wavefront_verify_attention_plus_commit", "batch_per_gpu": c["B"], "slots": c["R"],
              "n_heads": c["H"], "n_kv_heads": c["Hkv"], "head_dim": c["Dh"], "slot_len": "8192-r + 8-row window",
              "window": c["W"], "l2": "KV working set > 126 MB L2, no flush"}
+    elif c.get("kv_budget") == 1:
+        d = {"workload": "cfg5_long_context_verify_plus_commit with KV sharing kv_budget_s=1 (every loop depth "
+                         "of a layer on one slot: 8 slots of 32768 positions per sequence, 137 GB for 128 "
+                         "sequences per GPU; the timed step is one layer: one 8-row window per sequence)",
+             "batch_per_gpu": c["B"], "slots": c["R"], "n_heads": c["H"], "n_kv_heads": c["Hkv"],
+             "head_dim": c["Dh"], "slot_len": "32768 + 8-row window", "window": c["W"],
+             "acceptance": f"Bernoulli({c['alpha']}) seed {c['seed']}, accepted prefix per sequence",
+             "l2": "KV working set 8.6 GB > L2, no flush"}
     else:
         d = {"workload": "cfg5_long_context_verify_plus_commit (stated reduction: one layer's 16 loop-depth "
                          "slots, 64 sequences per GPU; the full model needs 1.17 TB of KV per GPU)",
@@ -468,7 +484,7 @@ def run_wfd(args):
         max_q = 1
         q = kn = vn = K = V = None
     else:
-        base = CFG3 if args.workload == "cfg3" else CFG5
+        base = CFG3 if args.workload == "cfg3" else (CFG5S1 if args.kv_budget == 1 else CFG5)
         c, qd, Kd, Vd, knd, vnd, items, acc = cfg3_device_inputs(dev, base["seed"] + rank, args.batch, base,
                                                                  args.alpha if args.workload == "cfg5" else None)
         max_q = c["W"]
