@@ -123,7 +123,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4attn", "cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4attn", "cfg5", "cfg4tick"], default="cfg2",
+                    help="cfg4tick: per-tick kernel breakdown of config 4 (diagnostic table, no JSON line)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (cfg2 / cfg3) or in total over all GPUs (cfg4); default: the config's")
     ap.add_argument("--t-draft", type=int, default=2, help="cfg4: draft depth T_draft")
@@ -538,18 +539,29 @@ def run_wfd(args):
     rt.read_device_error(dev)
 
     # ---- e2e: the public API call with host buffers every step.  Each step's
-    # inputs are uploaded from pinned host memory on a copy stream while the
-    # previous step computes (two sets of device input / output buffers), and its
-    # output is read back to pinned host memory right after it; every copy of
-    # every step lies inside the timed region.
-    q_h, kn_h, vn_h = qd.cpu().pin_memory(), knd.cpu().pin_memory(), vnd.cpu().pin_memory()
-    it_h = items_t.pin_memory()
+    # inputs (q, the new K / V rows, the item table) sit packed in one pinned host
+    # buffer and go up in one copy on a copy stream while the previous step
+    # computes (two device copies of the packed inputs and of the output); the
+    # output is read back to pinned host memory right after its step; every copy
+    # of every step lies inside the timed region.
+    parts = [qd, knd, vnd, items_t]
+    offs, total_b = [], 0
+    for t in parts:
+        offs.append(total_b)
+        total_b += (t.numel() * t.element_size() + 255) // 256 * 256
+    stage_h = torch.empty(total_b, dtype=torch.uint8).pin_memory()
+    for t, o in zip(parts, offs):
+        nb = t.numel() * t.element_size()
+        stage_h[o:o + nb].copy_(t.detach().cpu().contiguous().view(-1).view(torch.uint8))
     out_h = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
-    h2d = (q_h.numel() + kn_h.numel() + vn_h.numel()) * 2 + it_h.numel() * 4
+    h2d = sum(t.numel() * t.element_size() for t in parts)
     d2h = out_h[0].numel() * 2
-    bufs = [(qd, knd, vnd, itd, out),
-            (torch.empty_like(qd), torch.empty_like(knd), torch.empty_like(vnd), torch.empty_like(itd),
-             torch.empty_like(out))]
+
+    def device_views(buf):
+        return tuple(buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape) for t, o in zip(parts, offs))
+
+    stage_d = [torch.empty(total_b, dtype=torch.uint8, device=dev) for _ in range(2)]
+    bufs = [device_views(b) + (torch.empty_like(out),) for b in stage_d]
     comp = torch.cuda.current_stream(dev)
     copy = torch.cuda.Stream(dev)
     uploaded = [torch.cuda.Event(), torch.cuda.Event()]
@@ -558,13 +570,9 @@ def run_wfd(args):
         e.record(comp)
 
     def upload(i):
-        bq, bk, bv, bi, _ = bufs[i % 2]
         with torch.cuda.stream(copy):
             copy.wait_event(computed[i % 2])          # the step that last used these buffers is done
-            bq.copy_(q_h, non_blocking=True)
-            bk.copy_(kn_h, non_blocking=True)
-            bv.copy_(vn_h, non_blocking=True)
-            bi.copy_(it_h, non_blocking=True)
+            stage_d[i % 2].copy_(stage_h, non_blocking=True)
             uploaded[i % 2].record(copy)
 
     def compute(i):
@@ -844,12 +852,100 @@ def run_cfg4(args):
     print(json.dumps(line), flush=True)
 
 
+def run_tick_profile(args):
+    """--workload cfg4tick: per-tick kernel breakdown of greedy wavefront decoding
+    on the device scheduler (diagnostic; prints a table, no JSON line).  Runs
+    the config-4 model (random init, bf16, 1024-token prompts, --batch
+    sequences, --new-tokens, --t-draft) once to capture the tick graph, then once
+    more under torch.profiler (CUPTI kernel records of the graph replays, no
+    kernel replay) and prints, for the decode ticks only: span and busy time per
+    tick, every kernel's launches and device time per tick, and each attention
+    launch's K/V bytes and read rate."""
+    import collections
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.device_scheduler import DeviceWave
+    from wavefront_decoding_b200.engine import WaveEngine
+    from wavefront_decoding_b200.looped_lm import CONFIG4, LoopedLM
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, new, L = args.batch or 8, args.new_tokens or 32, CFG4["L"]
+    cfg = CONFIG4
+    prompts = torch.randint(0, cfg.vocab, (B, L), generator=torch.Generator().manual_seed(CFG4["seed"])).pin_memory()
+    model = LoopedLM(cfg, seed=CFG4["model_seed"], dtype=torch.bfloat16, device=dev)
+    eng = WaveEngine(model, B, L + new + 2 * cfg.T_total + 8)
+    dw = DeviceWave(eng, new, sch.SsdPolicy(cfg.T_total, args.t_draft))
+    dw.generate(prompts, None)  # captures the tick graph
+    torch.cuda.synchronize()
+    orig = eng.prefill
+
+    def prefill(ids):  # a marker kernel between the prompt pass and the first tick
+        out = orig(ids)
+        torch.cuda._sleep(1000)
+        return out
+
+    eng.prefill = prefill
+    try:
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            bt = dw.generate(prompts, None)
+            torch.cuda.synchronize()
+    finally:
+        del eng.prefill
+    ks = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                if e.device_type == torch.autograd.DeviceType.CUDA)
+    marks = [i for i, k in enumerate(ks) if "spin" in k[2].lower()]
+    if marks:
+        ks = ks[marks[-1] + 1:]
+    ticks = max(dw.ticks_replayed, 1)
+    busy, cur_s, cur_e = 0.0, None, None
+    for s0, e0, _ in ks:
+        if cur_e is None or s0 > cur_e:
+            if cur_e is not None:
+                busy += cur_e - cur_s
+            cur_s, cur_e = s0, e0
+        else:
+            cur_e = max(cur_e, e0)
+    if cur_e is not None:
+        busy += cur_e - cur_s
+    span = ks[-1][1] - ks[0][0] if ks else 0.0
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for s0, e0, nm in ks:
+        agg[nm[:100]][0] += 1
+        agg[nm[:100]][1] += e0 - s0
+    total = sum(a[1] for a in agg.values()) or 1.0
+    print(f"batch {B}: {ticks} ticks, {bt.n_tokens} tokens; per tick: span {span / ticks:.1f} us, "
+          f"busy {busy / ticks:.1f} us, {len(ks) / ticks:.1f} kernels")
+    print(f"  {'launches':>8} {'us/tick':>9} {'share':>6} {'us/launch':>10}  kernel")
+    for nm, (c, t) in sorted(agg.items(), key=lambda x: -x[1][1]):
+        print(f"  {c:8d} {t / ticks:9.2f} {100 * t / total:5.1f}% {t / c:10.2f}  {nm}")
+    # the attention launches of a tick: prelude layers, core layers, coda layers
+    keys = dw.keys.tolist()
+    rb = 2 * eng._row_bytes
+    per_layer = [keys[0]] * cfg.n_prelude + [keys[1]] * cfg.n_core + [keys[2]] * cfg.n_coda
+    tc = [e0 - s0 for s0, e0, nm in ks if "wave_tc_kernel" in nm or "wave_decode_kernel" in nm]
+    n_att = len(per_layer)
+    if tc and len(tc) % n_att == 0:
+        print("  attention launch (position in the tick): mean us, K/V MB, GB/s")
+        for i in range(n_att):
+            m = sum(tc[i::n_att]) / len(tc[i::n_att])
+            mb = per_layer[i] / ticks * rb / 1e6
+            print(f"    {i}: {m:8.2f} us {mb:8.1f} MB {mb / 1e3 / (m * 1e-6):7.0f}")
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "cfg4":
         run_cfg4(args)
+    elif args.workload == "cfg4tick":
+        run_tick_profile(args)
     else:
         run_wfd(args)
 

@@ -168,6 +168,24 @@ int wfd_wave_attn_kernel(int32_t which, const void* q, const void* k_new, const 
                          int32_t max_seq, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype,
                          float scale, void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream);
 
+/* wfd_wave_attn with the kernel choice of wfd_wave_attn_kernel (-1 auto) and
+ * optional per-row positions: row j of item i sits at position
+ * row_pos[(q_row0 + j) * row_pos_stride] (increasing within the item, the first
+ * one equal to pos0) instead of pos0 + j, is appended there and attends keys
+ * [0, that position] of its slot.  This is a gapped window: the reference
+ * pads such runs (the tokens of one sequence on one depth slot under KV
+ * sharing, ouro_blocks_batch.py:184-205) into one zero-padded span; here the
+ * rows keep their own positions and the prefix is still read once per window.
+ * row_pos == NULL is wfd_wave_attn.  Gapped windows run on the tcgen05 kernel
+ * only (bf16, head_dim 64 / 128); otherwise WFD_ERR_UNSUPPORTED.  A middle row
+ * whose position is out of order is skipped and reported in the error word. */
+int wfd_wave_attn_rows(int32_t which, const void* q, const void* k_new, const void* v_new, void* k_cache,
+                       void* v_cache, void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
+                       const int32_t* row_pos, int32_t row_pos_stride, int32_t slot_offset, int32_t n_rows,
+                       int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_heads, int32_t n_kv_heads,
+                       int32_t head_dim, int32_t dtype, float scale, void* workspace, size_t workspace_bytes,
+                       int32_t* d_err, void* stream);
+
 /* Packed varlen attention, drop-in for fa4_attention.attn_varlen
  * (fa4_attention.py:301-317) and for the graph engine's direct
  * aten._flash_attention_forward call (graph_blocks.py:37-43).  Segment i: query

@@ -439,3 +439,44 @@ def test_tc_bounded_wait_gives_up_and_next_launch_is_exact(cuda_dev):
         no_device_error(cuda_dev)
         assert maxdiff(out, ref) < TOL_BF16
         assert maxdiff(Kd, o.K) == 0.0 and maxdiff(Vd, o.V) == 0.0
+
+
+@pytest.mark.parametrize("Dh,H,Hkv", [(128, 16, 4), (64, 6, 6)], ids=["gqa4_d128", "mha_pair_d64"])
+def test_tc_gapped_windows_vs_oracle(cuda_dev, Dh, H, Hkv):
+    """Gapped windows (per-row positions, wfd_wave_attn_rows): the rows of one
+    sequence on one slot at positions with gaps (stride 2, stride 3, irregular)
+    form one window.  Outputs equal the oracle's one-window-per-row result (each
+    row sees keys up to its own position, every row appended before any row
+    attends), only the rows' own positions are written (bit-exact), and each
+    slot length rises to the last row's position + 1.  The positions are read
+    through a strided view (a table column), as the engine passes them."""
+    from wavefront_decoding_b200 import attention as wa
+    windows = [(0, 0, [400, 402, 404, 406]), (1, 1, [500, 503, 506]), (2, 2, [100, 101, 105, 106, 110]),
+               (0, 3, [50]), (1, 0, [7, 9])]
+    items, pos, row = [], [], 0
+    for slot, seq, ps in windows:
+        items.append([slot, seq, ps[0], len(ps), row])
+        pos += ps
+        row += len(ps)
+    K, V, q, kn, vn = _wave_case(61 + Dh, 3, 4, 600, H, Hkv, Dh, items, torch.bfloat16)
+    tab = torch.zeros((row, 6), dtype=torch.int32)
+    tab[:, 1] = torch.tensor(pos, dtype=torch.int32)
+    tabd = tab.to(cuda_dev)
+    Kd, Vd = K.to(cuda_dev).contiguous(), V.to(cuda_dev).contiguous()
+    lens = torch.zeros(K.shape[:2], dtype=torch.int32, device=cuda_dev)
+    it = torch.tensor(items, dtype=torch.int32, device=cuda_dev)
+    out = wa.wave_attn(q.to(cuda_dev), kn.to(cuda_dev), vn.to(cuda_dev), Kd, Vd, it, 5, lens=lens,
+                       row_pos=tabd[:, 1])
+    torch.cuda.synchronize()
+    no_device_error(cuda_dev)
+    per_row = [[slot, seq, p, 1, r] for (slot, seq, ps), base in zip(windows, [it_[4] for it_ in items])
+               for r, p in zip(range(base, base + len(ps)), ps)]
+    ref, o = _oracle_wave(K, V, q, kn, vn, per_row)
+    assert maxdiff(out, ref) < TOL_BF16
+    assert maxdiff(Kd, o.K) == 0.0 and maxdiff(Vd, o.V) == 0.0
+    for slot, seq, ps in windows:
+        assert int(lens[slot, seq]) == max(ps) + 1
+    # the same table without per-row positions is a different (contiguous) window: not what was asked
+    with pytest.raises(Exception):
+        wa.wave_attn(q.to(cuda_dev).float(), kn.to(cuda_dev).float(), vn.to(cuda_dev).float(), Kd.float(),
+                     Vd.float(), it, 5, row_pos=tabd[:, 1])  # fp32 has no gapped-window kernel

@@ -82,7 +82,7 @@ def test_wave_attn_op_vs_oracle_and_graph_capture(cuda_dev):
     rt.error_word(cuda_dev)
 
     def body():
-        torch.ops.wfd.wave_attn_out(qd, knd, vnd, Kd, Vd, it, 7, lens, 0, None, -1, out)
+        torch.ops.wfd.wave_attn_out(qd, knd, vnd, Kd, Vd, it, 7, lens, 0, None, -1, None, out)
 
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())

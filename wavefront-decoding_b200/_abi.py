@@ -21,7 +21,7 @@ WFD_DTYPE_F32 = 1
 EXPORTED = (
     "wfd_abi_version", "wfd_status_string", "wfd_read_error", "wfd_workspace_bytes", "wfd_workspace_init",
     "wfd_wave_attn", "wfd_wave_attn_static", "wfd_wave_attn_kernel", "wfd_attn_varlen", "wfd_attn_segments",
-    "wfd_attn_prefill",
+    "wfd_attn_prefill", "wfd_wave_attn_rows",
     "wfd_append",
     "wfd_write_prefill", "wfd_commit_drop", "wfd_commit_window", "wfd_gather_pack",
     "wfd_rmsnorm", "wfd_rope_split", "wfd_silu_mul", "wfd_gather_rows", "wfd_scatter_rows",
@@ -74,6 +74,10 @@ _SIGS = {
     "wfd_wave_attn": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S, _P, _P], _I),
     "wfd_wave_attn_kernel": ([_I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _S,
                               _P, _P], _I),
+    # which q k_new v_new kc vc out lens items n max_q row_pos rp_stride slot_off n_rows n_slots n_seqs max_seq Hq Hkv
+    # Dh dtype scale ws ws_bytes err stream
+    "wfd_wave_attn_rows": ([_I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F,
+                            _P, _S, _P, _P], _I),
     # as wfd_wave_attn without (ws, ws_bytes)
     "wfd_wave_attn_static": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P], _I),
     # q k v out cu_q cu_k n max_q total_q total_k Hq Hkv Dh dtype causal scale ws ws_bytes err stream

@@ -165,7 +165,8 @@ def attn_cutoff_multi(q, k, v, qpos):
 
 
 def wave_attn(q, k_new, v_new, k_cache, v_cache, items, max_q: int, *, lens=None, slot_offset: int = 0,
-              out: torch.Tensor | None = None, scale: float | None = None, kernel: int = -1):
+              out: torch.Tensor | None = None, scale: float | None = None, kernel: int = -1,
+              row_pos: torch.Tensor | None = None):
     """Wavefront decode / verify attention with the K/V append fused, through
     the dispatcher op torch.ops.wfd.wave_attn (torch.ops.wfd.wave_attn_out with
     `out`).
@@ -175,11 +176,13 @@ def wave_attn(q, k_new, v_new, k_cache, v_cache, items, max_q: int, *, lens=None
     (slot, seq, pos0, q_len, q_row0); lens: optional device int32 (n_slots,
     n_seqs).  Row j of an item writes its K/V at pos0+j of (slot+slot_offset, seq)
     and attends positions [0, pos0+j].  kernel: -1 auto, 0 CUDA-core decode,
-    1 tcgen05 verify."""
+    1 tcgen05 verify.  row_pos (int32, one position per q row, any stride):
+    gapped windows, row j of an item at row_pos[q_row0 + j] instead of pos0 + j
+    (tcgen05 kernel only)."""
     rt.require_cuda(q, k_new, v_new, k_cache, v_cache, items)
     if out is None:
         return torch.ops.wfd.wave_attn(q, k_new, v_new, k_cache, v_cache, items, int(max_q), lens, int(slot_offset),
-                                       scale, int(kernel))
+                                       scale, int(kernel), row_pos)
     torch.ops.wfd.wave_attn_out(q, k_new, v_new, k_cache, v_cache, items, int(max_q), lens, int(slot_offset), scale,
-                                int(kernel), out)
+                                int(kernel), row_pos, out)
     return out

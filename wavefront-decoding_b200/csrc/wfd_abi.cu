@@ -265,6 +265,8 @@ struct AttnArgs {
   int* err;
   int which;           // -1 auto, 0 decode kernel, 1 verify kernel
   long long key_rows;  // rows of (Hkv * Dh) elements in k / v (tensor-map extent)
+  const int32_t* row_pos;  // slot mode, optional: per-row positions (gapped windows)
+  int row_pos_stride;
 };
 
 int run_attention(const AttnArgs& A, cudaStream_t st) {
@@ -291,8 +293,10 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
   const bool pair_ok = A.Dh == 64 && A.Hkv % 2 == 0 && 2ll * G * max_q <= kVerifyMaxRows;
   const bool odd_mha_d64_decode = A.Dh == 64 && !pair_ok && (long long)G * max_q == 1;
   const bool invariant = g_batch_invariant.load(std::memory_order_relaxed) != 0;
-  if (which < 0) which = (tc_ok && (invariant || !odd_mha_d64_decode)) ? 1 : 0;
+  if (which < 0) which = (tc_ok && (invariant || !odd_mha_d64_decode || A.row_pos != nullptr)) ? 1 : 0;
   if (which == 1 && !tc_ok) return WFD_ERR_UNSUPPORTED;
+  // gapped windows (per-row positions) are read by the tensor-core kernel only
+  if (A.row_pos != nullptr && (which != 1 || A.mode != kPlanSlots || A.row_pos_stride < 1)) return WFD_ERR_UNSUPPORTED;
   const bool pair = which == 1 && pair_ok;
   const int Gv = pair ? 2 * G : G;  // query vectors per unit and kv (pair) head
 
@@ -340,6 +344,8 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     pp.seg_grid = sms;
     pp.seg_units = pair ? A.Hkv / 2 : A.Hkv;
   }
+  pp.row_pos = A.row_pos;
+  pp.row_pos_stride = A.row_pos_stride;
   pp.out = A.out;
   pp.Hq = A.Hq;
   pp.Dh = A.Dh;
@@ -390,6 +396,8 @@ int run_attention(const AttnArgs& A, cudaStream_t st) {
     vp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt);
     vp.err = A.err;
     vp.fail_waits = g_fail_waits.load(std::memory_order_relaxed);
+    vp.row_pos = A.row_pos;
+    vp.row_pos_stride = A.row_pos_stride;
     if (self_plan) {
       vp.items = A.items;
       vp.n_slots = A.n_slots;
@@ -445,7 +453,8 @@ int wave_common(int which, const void* q, const void* k_new, const void* v_new, 
                 void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
                 int32_t slot_offset, int32_t n_rows, int32_t n_slots, int32_t n_seqs, int32_t max_seq,
                 int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t dtype, float scale,
-                void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream) {
+                void* workspace, size_t workspace_bytes, int32_t* d_err, void* stream,
+                const int32_t* row_pos = nullptr, int32_t row_pos_stride = 1) {
   if (n_items == 0) return WFD_OK;  // empty tick: nothing to append or attend
   const int rc = wave_validate(q, k_new, v_new, k_cache, v_cache, out, items, n_items, slot_offset, n_rows, n_slots,
                                n_seqs, max_seq, n_heads, n_kv_heads);
@@ -482,6 +491,8 @@ int wave_common(int which, const void* q, const void* k_new, const void* v_new, 
   A.err = d_err;
   A.which = which;
   A.key_rows = (long long)n_slots * n_seqs * (long long)max_seq;
+  A.row_pos = row_pos;
+  A.row_pos_stride = row_pos_stride;
   return run_attention(A, static_cast<cudaStream_t>(stream));
 }
 
@@ -650,6 +661,19 @@ int wfd_wave_attn_kernel(int32_t which, const void* q, const void* k_new, const 
   return wave_common(which, q, k_new, v_new, k_cache, v_cache, out, lens, items, n_items, max_q, slot_offset,
                      n_rows, n_slots, n_seqs, max_seq, n_heads, n_kv_heads, head_dim, dtype, scale, workspace,
                      workspace_bytes, d_err, stream);
+}
+
+int wfd_wave_attn_rows(int32_t which, const void* q, const void* k_new, const void* v_new, void* k_cache,
+                       void* v_cache, void* out, int32_t* lens, const wfd_item* items, int32_t n_items, int32_t max_q,
+                       const int32_t* row_pos, int32_t row_pos_stride, int32_t slot_offset, int32_t n_rows,
+                       int32_t n_slots, int32_t n_seqs, int32_t max_seq, int32_t n_heads, int32_t n_kv_heads,
+                       int32_t head_dim, int32_t dtype, float scale, void* workspace, size_t workspace_bytes,
+                       int32_t* d_err, void* stream) {
+  if (which < -1 || which > 1) return WFD_ERR_INVALID_ARG;
+  if (row_pos != nullptr && row_pos_stride < 1) return WFD_ERR_INVALID_ARG;
+  return wave_common(which, q, k_new, v_new, k_cache, v_cache, out, lens, items, n_items, max_q, slot_offset, n_rows,
+                     n_slots, n_seqs, max_seq, n_heads, n_kv_heads, head_dim, dtype, scale, workspace,
+                     workspace_bytes, d_err, stream, row_pos, row_pos_stride);
 }
 
 int wfd_attn_varlen(const void* q, const void* k, const void* v, void* out, const int32_t* cu_q, const int32_t* cu_k,

@@ -56,6 +56,25 @@ __device__ __forceinline__ void set_error(int* err, int bits) {
   if (err) atomicOr(err, bits);
 }
 
+// Checks of a slot-table work item (wfd_item) and the position of its last row:
+// row j sits at pos0 + j, or, with per-row positions (gapped windows), at
+// row_pos[(q_row0 + j) * rp_stride], increasing, the first one pos0.  Returns
+// the error bit (0: valid).
+__device__ __forceinline__ int check_slot_item(const wfd_item& it, int n_slots, int n_seqs, int max_seq, int n_rows,
+                                               const int32_t* row_pos, int rp_stride, int& last) {
+  if (it.slot < 0 || it.slot >= n_slots || it.seq < 0 || it.seq >= n_seqs) return kErrBadSlot;
+  if (it.q_row0 < 0 || it.q_len < 0 || (long long)it.q_row0 + it.q_len > n_rows) return kErrBadRows;
+  if (it.pos0 < 0) return kErrBadPos;
+  last = it.pos0 + it.q_len - 1;
+  if (row_pos != nullptr && it.q_len > 0) {
+    if (row_pos[(long long)it.q_row0 * rp_stride] != it.pos0) return kErrBadPos;
+    last = row_pos[(long long)(it.q_row0 + it.q_len - 1) * rp_stride];
+    if (last < it.pos0) return kErrBadPos;
+  }
+  if ((long long)last + 1 > max_seq) return kErrBadPos;
+  return 0;
+}
+
 // ---------------------------------------------------------------------------
 // mbarrier + bulk copy (PTX ISA 8.x, sm_90+; used here on sm_100a)
 // ---------------------------------------------------------------------------

@@ -56,6 +56,10 @@ struct PlanParams {
   long long row_bytes, k_row_offset;
   int32_t* lens;
   int lens_offset;
+  // optional per-row positions of slot-table windows (gapped windows): row j of
+  // an item sits at row_pos[(q_row0 + j) * row_pos_stride]
+  const int32_t* row_pos;
+  int row_pos_stride;
 };
 
 constexpr int kPlanThreads = 1024;
@@ -101,19 +105,25 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) 
     const long long nvec = p.row_bytes / 16;
     for (int i = blockIdx.x - 1; i < p.n; i += gridDim.x - 1) {
       const wfd_item it = p.items[i];
-      if (it.slot < 0 || it.slot >= p.n_slots || it.seq < 0 || it.seq >= p.n_seqs || it.pos0 < 0 || it.q_len <= 0 ||
-          (long long)it.pos0 + it.q_len > p.max_seq || it.q_row0 < 0 || (long long)it.q_row0 + it.q_len > p.n_rows)
+      int last = 0;
+      if (it.q_len <= 0 ||
+          check_slot_item(it, p.n_slots, p.n_seqs, p.max_seq, p.n_rows, p.row_pos, p.row_pos_stride, last) != 0)
         continue;
-      const long long row0 = ((long long)it.slot * p.n_seqs + it.seq) * p.max_seq + p.k_row_offset + it.pos0;
+      const long long row0 = ((long long)it.slot * p.n_seqs + it.seq) * p.max_seq + p.k_row_offset;
       for (long long e = threadIdx.x; e < (long long)it.q_len * nvec; e += blockDim.x) {
         const long long j = e / nvec, c = e % nvec;
+        const int pos = p.row_pos != nullptr ? p.row_pos[(it.q_row0 + j) * p.row_pos_stride] : it.pos0 + (int)j;
+        if (pos < it.pos0 || pos > last) {  // a gapped window's middle row out of order: skipped, reported
+          if (c == 0) set_error(p.err, kErrBadPos);
+          continue;
+        }
         const long long src = (it.q_row0 + j) * p.row_bytes + c * 16;
-        const long long dst = (row0 + j) * p.row_bytes + c * 16;
+        const long long dst = (row0 + pos) * p.row_bytes + c * 16;
         *reinterpret_cast<uint4*>(p.k_app + dst) = ld_nc_v4(p.k_new + src);
         *reinterpret_cast<uint4*>(p.v_app + dst) = ld_nc_v4(p.v_new + src);
       }
       if (threadIdx.x == 0 && p.lens != nullptr)
-        atomicMax(p.lens + it.slot * p.n_seqs + it.seq + p.lens_offset, it.pos0 + it.q_len);
+        atomicMax(p.lens + it.slot * p.n_seqs + it.seq + p.lens_offset, last + 1);
     }
     return;
   }
@@ -136,19 +146,15 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const PlanParams p) 
       bool ok = true;
       if (p.mode == kPlanSlots) {
         const wfd_item it = p.items[i];
-        if (it.slot < 0 || it.slot >= p.n_slots || it.seq < 0 || it.seq >= p.n_seqs) {
-          set_error(p.err, kErrBadSlot);
-          ok = false;
-        } else if (it.pos0 < 0 || it.q_len < 0 || (long long)it.pos0 + it.q_len > p.max_seq) {
-          set_error(p.err, kErrBadPos);
-          ok = false;
-        } else if (it.q_row0 < 0 || (long long)it.q_row0 + it.q_len > p.n_rows) {
-          set_error(p.err, kErrBadRows);
+        int last = 0;
+        const int bad = check_slot_item(it, p.n_slots, p.n_seqs, p.max_seq, p.n_rows, p.row_pos, p.row_pos_stride, last);
+        if (bad) {
+          set_error(p.err, bad);
           ok = false;
         }
         if (ok) {
           s.k_row0 = ((long long)it.slot * p.n_seqs + it.seq) * (long long)p.max_seq;
-          s.k_len = it.pos0 + it.q_len;
+          s.k_len = last + 1;
           s.q_row0 = it.q_row0;
           s.q_len = it.q_len;
           s.new_row0 = it.q_row0;

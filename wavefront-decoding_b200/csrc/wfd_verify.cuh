@@ -88,6 +88,11 @@ struct VerifyParams {
   const wfd_item* items;
   int n_slots, n_seqs, max_seq, n_rows;  // the plan kernel's item checks
   int Gv, NQ;                            // query vectors per kv (pair) head, per unit
+  // optional per-row positions of slot-table windows (gapped windows): row j of
+  // a segment sits at row_pos[(q_row0 + j) * row_pos_stride] and sees keys up to
+  // that position; null: rows sit at k_len - q_len + j (bottom-right causal)
+  const int32_t* row_pos;
+  int row_pos_stride;
   // 1 (a test hook): the CTA gives up as a wait that ran out of its bound does
   // (timeout bit, abort flag) right after its first K/V copies are issued.
   // Checked once per CTA, not in the waits: the wait loops stay as lean as
@@ -285,12 +290,10 @@ __device__ __forceinline__ long long slot_segment(const VerifyParams& p, const w
   s.new_row0 = -1;
   s.lens_idx = -1;
   s.n_qg = 0;
-  const bool ok = it.slot >= 0 && it.slot < p.n_slots && it.seq >= 0 && it.seq < p.n_seqs && it.pos0 >= 0 &&
-                  it.q_len >= 0 && (long long)it.pos0 + it.q_len <= p.max_seq && it.q_row0 >= 0 &&
-                  (long long)it.q_row0 + it.q_len <= p.n_rows;
-  if (!ok) return 0;
+  int last = 0;
+  if (check_slot_item(it, p.n_slots, p.n_seqs, p.max_seq, p.n_rows, p.row_pos, p.row_pos_stride, last) != 0) return 0;
   s.k_row0 = ((long long)it.slot * p.n_seqs + it.seq) * (long long)p.max_seq;
-  s.k_len = it.pos0 + it.q_len;
+  s.k_len = last + 1;
   s.q_row0 = it.q_row0;
   s.q_len = it.q_len;
   s.new_row0 = it.q_row0;
@@ -788,6 +791,17 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       const int nvh = S.q_len * p.G;                                   // query vectors per kv head
       const int nvec = (p.pair ? 2 * nvh : nvh) - qg * NQP;  // of this unit / group (may exceed NQP)
 
+      // gapped windows: the position of the row of each of this thread's columns
+      int rp[NL];
+      if (p.row_pos != nullptr) {
+#pragma unroll
+        for (int j = 0; j < NL; ++j) {
+          const int n = col0 + j;
+          const int vn = (p.pair && n >= nvh) ? n - nvh : n;
+          const int row = (p.pair ? vn : qg * NQP + n) / p.G;
+          rp[j] = n < nvec ? p.row_pos[(long long)(S.q_row0 + row) * p.row_pos_stride] : -1;
+        }
+      }
       // running column maxima live in shared memory (mst, log2-scaled), owned
       // by lanes 0..NL-1 of the first warp of each column slice
       if (sq == 0 && lane < NL) mst[col0 + lane] = NEG_INF;
@@ -823,11 +837,19 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         const bool kvalid = key < r_hi;
         const int thr = p.causal ? (key - (S.k_len - S.q_len)) * p.G - qg * NQP : -(1 << 30);
         const int nlim = kvalid ? nvec : 0;
+        if (p.row_pos != nullptr && p.causal) {
 #pragma unroll
-        for (int j = 0; j < NL; ++j) {
-          const int n = col0 + j;
-          const int vn = (p.pair && n >= nvh) ? n - nvh : n;  // vector index within its head
-          s[j] = (n < nlim && vn >= thr) ? s[j] : NEG_INF;    // raw (unscaled) scores
+          for (int j = 0; j < NL; ++j) {
+            const int n = col0 + j;
+            s[j] = (n < nlim && key <= rp[j]) ? s[j] : NEG_INF;  // the row sees keys up to its position
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < NL; ++j) {
+            const int n = col0 + j;
+            const int vn = (p.pair && n >= nvh) ? n - nvh : n;  // vector index within its head
+            s[j] = (n < nlim && vn >= thr) ? s[j] : NEG_INF;    // raw (unscaled) scores
+          }
         }
         // column maxima over the tile's 128 keys
         float* rb = red + (ti & 1u) * (4 * NQP);

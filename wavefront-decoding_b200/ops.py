@@ -15,9 +15,11 @@ dispatcher.
       fa4_attention.attn_varlen (fa4_attention.py:301-317).
   wfd::attn_out(..., Tensor(a!) out) -> ()            the same into `out`
   wfd::wave_attn(q, k_new, v_new, k_cache!, v_cache!, items, max_q,
-                 lens!?=None, slot_offset=0, scale=None, kernel=-1) -> out
+                 lens!?=None, slot_offset=0, scale=None, kernel=-1, row_pos=None) -> out
       write_tokens + gather_pack + attn_varlen of one wavefront tick in one
-      launch pair (batch_kv_cache.py:61-96, ouro_blocks_batch.py:207-231).
+      launch pair (batch_kv_cache.py:61-96, ouro_blocks_batch.py:207-231);
+      row_pos (int32, one per q row, any stride) gives gapped windows their
+      rows' positions (ouro_blocks_batch.py:184-205 pads such runs instead).
   wfd::wave_attn_out(..., Tensor(d!) out) -> ()
   wfd::commit(k_cache!, v_cache!, lens!, items, accept_len?, accept_mask?,
               slot_offset, n_rows) -> (acc_rows, acc_count)
@@ -44,10 +46,10 @@ _SCHEMAS = {
                 "float? scale, Tensor(a!) out) -> ()",
     "wave_attn": "wave_attn(Tensor q, Tensor k_new, Tensor v_new, Tensor(a!) k_cache, Tensor(b!) v_cache, "
                  "Tensor items, int max_q, Tensor(c!)? lens=None, int slot_offset=0, float? scale=None, "
-                 "int kernel=-1) -> Tensor",
+                 "int kernel=-1, Tensor? row_pos=None) -> Tensor",
     "wave_attn_out": "wave_attn_out(Tensor q, Tensor k_new, Tensor v_new, Tensor(a!) k_cache, Tensor(b!) v_cache, "
                      "Tensor items, int max_q, Tensor(c!)? lens, int slot_offset, float? scale, int kernel, "
-                     "Tensor(d!) out) -> ()",
+                     "Tensor? row_pos, Tensor(d!) out) -> ()",
     "commit": "commit(Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor(c!) lens, Tensor items, Tensor? accept_len, "
               "Tensor? accept_mask, int slot_offset, int n_rows) -> (Tensor, Tensor)",
     "commit_out": "commit_out(Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor(c!) lens, Tensor items, "
@@ -149,27 +151,34 @@ def _attn_cuda(q, k, v, cu_q, cu_k, max_q, max_k, causal=False, scale=None):
     return out
 
 
-def _wave_attn_out_cuda(q, k_new, v_new, k_cache, v_cache, items, max_q, lens, slot_offset, scale, kernel, out):
+def _wave_attn_out_cuda(q, k_new, v_new, k_cache, v_cache, items, max_q, lens, slot_offset, scale, kernel, row_pos,
+                        out):
     dev = _check_wave(q, k_new, v_new, k_cache, v_cache, items, lens)
     n_slots, n_seqs, max_seq, Hkv, Dh = k_cache.shape
     if out.shape != q.shape or out.dtype != q.dtype or not out.is_contiguous():
         raise ValueError("out must be a contiguous tensor shaped like q")
+    rp_stride = 1
+    if row_pos is not None:
+        if row_pos.dtype != torch.int32 or row_pos.dim() != 1 or row_pos.numel() < q.shape[0] or \
+                row_pos.device != dev or row_pos.stride(0) < 1:
+            raise ValueError("row_pos must be an int32 device vector with one position per q row")
+        rp_stride = row_pos.stride(0)
     q, k_new, v_new = q.contiguous(), k_new.contiguous(), v_new.contiguous()
     n = items.shape[0]
     ws, wsb = rt.workspace(dev, n, Dh)
-    lib = _abi.load()
-    args = (q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-            out.data_ptr(), rt.ptr(lens), items.data_ptr(), n, int(max_q), int(slot_offset), q.shape[0], n_slots,
-            n_seqs, max_seq, q.shape[1], Hkv, Dh, rt.dtype_code(q.dtype), float(scale or 0.0), ws.data_ptr(), wsb,
-            rt.error_word(dev).data_ptr(), rt.stream_ptr(dev))
-    st = lib.wfd_wave_attn(*args) if kernel < 0 else lib.wfd_wave_attn_kernel(int(kernel), *args)
+    st = _abi.load().wfd_wave_attn_rows(
+        int(kernel), q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        out.data_ptr(), rt.ptr(lens), items.data_ptr(), n, int(max_q), rt.ptr(row_pos), rp_stride, int(slot_offset),
+        q.shape[0], n_slots, n_seqs, max_seq, q.shape[1], Hkv, Dh, rt.dtype_code(q.dtype), float(scale or 0.0),
+        ws.data_ptr(), wsb, rt.error_word(dev).data_ptr(), rt.stream_ptr(dev))
     _abi.check(st, "wfd_wave_attn")
 
 
 def _wave_attn_cuda(q, k_new, v_new, k_cache, v_cache, items, max_q, lens=None, slot_offset=0, scale=None,
-                    kernel=-1):
+                    kernel=-1, row_pos=None):
     out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    _wave_attn_out_cuda(q, k_new, v_new, k_cache, v_cache, items, max_q, lens, slot_offset, scale, kernel, out)
+    _wave_attn_out_cuda(q, k_new, v_new, k_cache, v_cache, items, max_q, lens, slot_offset, scale, kernel, row_pos,
+                        out)
     return out
 
 
@@ -234,12 +243,14 @@ def _attn_out_fake(q, k, v, cu_q, cu_k, max_q, max_k, causal, scale, out):
 
 
 @torch.library.register_fake("wfd::wave_attn")
-def _wave_attn_fake(q, k_new, v_new, k_cache, v_cache, items, max_q, lens=None, slot_offset=0, scale=None, kernel=-1):
+def _wave_attn_fake(q, k_new, v_new, k_cache, v_cache, items, max_q, lens=None, slot_offset=0, scale=None, kernel=-1,
+                    row_pos=None):
     return torch.empty_like(q)
 
 
 @torch.library.register_fake("wfd::wave_attn_out")
-def _wave_attn_out_fake(q, k_new, v_new, k_cache, v_cache, items, max_q, lens, slot_offset, scale, kernel, out):
+def _wave_attn_out_fake(q, k_new, v_new, k_cache, v_cache, items, max_q, lens, slot_offset, scale, kernel, row_pos,
+                        out):
     return None
 
 
