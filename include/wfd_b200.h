@@ -36,8 +36,9 @@ extern "C" {
 #endif
 
 /* Raised whenever a declaration or a struct layout below changes incompatibly
- * (2: wfd_sched_params.depth_slots; 3: wfd_commit_window takes n_rows). */
-#define WFD_ABI_VERSION 3
+ * (2: wfd_sched_params.depth_slots; 3: wfd_commit_window takes n_rows;
+ * 4: wfd_sched_params.gap_windows). */
+#define WFD_ABI_VERSION 4
 
 enum wfd_status {
   WFD_OK = 0,
@@ -343,6 +344,8 @@ typedef struct {
   int32_t scratch_row, scratch_seq;
   int32_t p_slot0, n_prelude, c_slot0, n_coda;
   int32_t depth_slots; /* core depth slots: T_total, or the KV-sharing budget s (depth r -> slot r % s) */
+  int32_t gap_windows; /* 1: all of a sequence's tokens on one depth slot form one R window, gaps included
+                          (attended with per-row positions); 0: only runs of consecutive positions do */
 } wfd_sched_params;
 
 /* sizeof(wfd_sched_params) as compiled into the library: a host that mirrors the

@@ -40,3 +40,14 @@ def test_dtv_verify_sources():
 
 def test_empty():
     assert _windows([], [], []) == (None, [])
+
+
+def test_gap_mode_groups_a_slot_whatever_the_gaps():
+    # s = 2 with gapped windows: positions 4, 6 (slot 0) and 5, 7 (slot 2) are two windows of two rows
+    order, runs = _windows([0, 0, 0, 0], [0, 2, 0, 2], [4, 5, 6, 7], True)
+    assert order == [0, 2, 1, 3]
+    assert runs == [2, 0, 2, 0]
+    # irregular gaps (after a rejection) and a second sequence
+    order, runs = _windows([3, 3, 1, 3], [0, 0, 0, 0], [20, 11, 9, 15], True)
+    assert order == [2, 1, 3, 0]
+    assert runs == [1, 3, 0, 0]

@@ -44,7 +44,7 @@ class wfd_item(ctypes.Structure):
                 ("q_len", ctypes.c_int32), ("q_row0", ctypes.c_int32)]
 
 
-ABI_VERSION = 3  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
+ABI_VERSION = 4  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
 
 
 class wfd_sched_params(ctypes.Structure):
@@ -55,7 +55,7 @@ class wfd_sched_params(ctypes.Structure):
         [(n, ctypes.c_int32) for n in (
             "B", "W", "T_total", "T_draft", "max_new", "emu_len", "n_core", "n_kv_slots", "lens_stride",
             "max_seq", "p_cols", "c_cols", "r_cap", "scratch_row", "scratch_seq", "p_slot0", "n_prelude",
-            "c_slot0", "n_coda", "depth_slots")]
+            "c_slot0", "n_coda", "depth_slots", "gap_windows")]
 
 
 _P = ctypes.c_void_p

@@ -1051,6 +1051,8 @@ static_assert(offsetof(wfd_sched_params, c_out) == offsetof(wfd::SchedParams, c_
 static_assert(offsetof(wfd_sched_params, n_coda) == offsetof(wfd::SchedParams, n_coda), "wfd_sched_params layout");
 static_assert(offsetof(wfd_sched_params, depth_slots) == offsetof(wfd::SchedParams, depth_slots),
               "wfd_sched_params layout");
+static_assert(offsetof(wfd_sched_params, gap_windows) == offsetof(wfd::SchedParams, gap_windows),
+              "wfd_sched_params layout");
 
 extern "C" size_t wfd_sched_params_bytes(void) { return sizeof(wfd_sched_params); }
 

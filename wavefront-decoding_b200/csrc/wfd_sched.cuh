@@ -57,6 +57,7 @@ struct SchedParams {
   int scratch_row, scratch_seq;
   int p_slot0, n_prelude, c_slot0, n_coda;  // first KV slot and count of the prelude / coda layers
   int depth_slots;                           // core depth slots (KV sharing: depth r -> slot r % depth_slots)
+  int gap_windows;                           // 1: a sequence's tokens on one depth slot form one window, gaps included
 };
 
 __device__ __forceinline__ void sched_pad_row(int32_t* row, int cols, const SchedParams& p, int seg_slot0) {
@@ -140,9 +141,11 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
     // consecutive positions on one depth slot (KV sharing) becomes one window:
     // its first row carries the run length in column 5 (the item's q_len), the
     // other rows 0, so the shared slot prefix is read once per run
-    // (ouro_blocks_batch.py:184-205).  Without sharing the live tokens of a
-    // sequence have distinct steps, so every run is one token and the rows keep
-    // token-slot order.
+    // (ouro_blocks_batch.py:184-205).  With gap_windows every token of the
+    // sequence on one depth slot joins one window whatever the gaps between their
+    // positions (the attention reads each row's position from column 1).
+    // Without sharing the live tokens of a sequence have distinct steps, so
+    // every run is one token and the rows keep token-slot order.
     const bool shared = p.depth_slots > 0 && p.depth_slots < p.T_total;
     int ord[kSchedMaxW], dsl[kSchedMaxW], psn[kSchedMaxW];
     int m = 0;
@@ -165,7 +168,7 @@ __global__ void __launch_bounds__(kSchedThreads) sched_pre_tick_kernel(const Sch
     unsigned long long kk = 0;
     for (int i = 0; i < m;) {
       int e = i + 1;
-      while (shared && e < m && dsl[e] == dsl[i] && psn[e] == psn[e - 1] + 1) ++e;
+      while (shared && e < m && dsl[e] == dsl[i] && (p.gap_windows || psn[e] == psn[e - 1] + 1)) ++e;
       for (int k = i; k < e; ++k, ++r) {
         if (r < p.r_cap) {
           int32_t* row = p.r_tab + (long long)r * 6;

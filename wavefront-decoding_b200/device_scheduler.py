@@ -111,6 +111,7 @@ class DeviceWave:
         p.p_slot0, p.n_prelude = cfg.slot_prelude(0), cfg.n_prelude
         p.c_slot0, p.n_coda = cfg.slot_coda(0), cfg.n_coda
         p.depth_slots = cfg.n_depth_slots
+        p.gap_windows = 1 if self.eng.gap_windows else 0
         self._params[key] = p
         return p
 

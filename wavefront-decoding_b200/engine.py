@@ -46,15 +46,18 @@ def _bucket(n: int) -> int:
     raise ValueError(f"union of {n} rows exceeds the largest bucket {_BUCKETS[-1]}")
 
 
-def r_windows(seq_ids: list, slot_bases: list, positions: list):
+def r_windows(seq_ids: list, slot_bases: list, positions: list, gaps: bool = False):
     """Attention windows of an R union (ouro_blocks_batch.py:184-205).
 
     Rows of one sequence on one depth slot (KV sharing, or the sources of a
     draft-then-verify round) are reordered by (sequence, slot, position), and a
-    run of consecutive positions becomes one bottom-right-causal window.
-    Returns (order, runs): order is None when no sequence has two rows on one
-    slot (rows keep their order), else the row permutation; runs[i] is the
-    window's row count on its first row and 0 on the others."""
+    run of consecutive positions becomes one bottom-right-causal window; with
+    `gaps`, all of a sequence's rows on one slot form one window whatever the
+    gaps between their positions (attended with per-row positions, the way the
+    reference pads them into one span).  Returns (order, runs): order is None
+    when no sequence has two rows on one slot (rows keep their order), else the
+    row permutation; runs[i] is the window's row count on its first row and 0 on
+    the others."""
     n = len(seq_ids)
     key = list(zip(seq_ids, slot_bases))
     order = None
@@ -66,7 +69,7 @@ def r_windows(seq_ids: list, slot_bases: list, positions: list):
     i = 0
     while i < n:
         e = i + 1
-        while e < n and key[e] == key[i] and positions[e] == positions[e - 1] + 1:
+        while e < n and key[e] == key[i] and (gaps or positions[e] == positions[e - 1] + 1):
             e += 1
         runs[i] = e - i
         i = e
@@ -134,6 +137,10 @@ class WaveEngine:
         # rows per R attention window: 1 without KV sharing; with sharing a run of
         # one sequence's tokens on one depth slot (at most T_total + 2 tokens live)
         self.r_max_q = 1 if cfg.n_depth_slots == cfg.T_total else cfg.T_total + 2
+        # KV sharing: a sequence's tokens on one depth slot attend as one window,
+        # gaps included, on the tensor-core kernel (per-row positions); the fp32
+        # CUDA-core kernel keeps one window per run of consecutive positions
+        self.gap_windows = cfg.n_depth_slots < cfg.T_total and self.model.dtype == torch.bfloat16
         self.kv_read_bytes = 0
         self.wfd_launches = 0
         self.d2h_bytes = 0
@@ -174,7 +181,7 @@ class WaveEngine:
         runs = None
         if kind == "R":
             order, runs = r_windows([int(x) for x in seq_ids], [cfg.core_slot_base(tk.step) for tk in toks],
-                                    [tk.position for tk in toks])
+                                    [tk.position for tk in toks], gaps=self.gap_windows)
             if order is not None:
                 toks = [toks[i] for i in order]
                 seq_ids = [seq_ids[i] for i in order]
@@ -258,7 +265,7 @@ class WaveEngine:
             for l, blk in enumerate(m.core):
                 q, k, v = m.qkv(blk, x, pos=tab[:, 1])
                 o = wa.wave_attn(q, k, v, self.cache.K, self.cache.V, t.items, self.r_max_q, lens=self.cache.lens,
-                                 slot_offset=cfg.n_prelude + l)
+                                 slot_offset=cfg.n_prelude + l, row_pos=tab[:, 1] if self.gap_windows else None)
                 x = m.finish_block(blk, x, o)
             fused.scatter_rows(x, rows, self.pool_h)
         else:
