@@ -123,8 +123,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4attn", "cfg5", "cfg4tick"], default="cfg2",
-                    help="cfg4tick: per-tick kernel breakdown of config 4 (diagnostic table, no JSON line)")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4attn", "cfg5", "cfg4tick", "prefill"],
+                    default="cfg2",
+                    help="cfg4tick: per-tick kernel breakdown of config 4 (diagnostic table, no JSON line); "
+                         "prefill: the prompt kernel on one config-4 layer")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (cfg2 / cfg3) or in total over all GPUs (cfg4); default: the config's")
     ap.add_argument("--t-draft", type=int, default=2, help="cfg4: draft depth T_draft")
@@ -852,6 +854,55 @@ def run_cfg4(args):
     print(json.dumps(line), flush=True)
 
 
+def run_prefill(args):
+    """--workload prefill: the prompt pass's causal attention of one config-4 layer
+    (B = 64 (--batch), L = 1024, MHA 24 x 64, bf16) on the tcgen05 prompt kernel
+    K7; value = causal TFLOP/s (4 * B * H * Dh * L^2 / 2 per launch), roofline
+    against the measured bf16 tensor peak (burst)."""
+    import torch
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from wavefront_decoding_b200 import attention as wa
+    from wavefront_decoding_b200 import runtime as rt
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, L, H, Dh = args.batch or 64, CFG4["L"], 24, 64
+    g = torch.Generator(device=dev).manual_seed(CFG4["seed"])
+    q = torch.randn((B, L, H, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn((B, L, H, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn((B, L, H, Dh), generator=g, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    for _ in range(max(3, args.warmup)):
+        wa.attn_prefill(q, k, v, causal=True, out=out)
+    torch.cuda.synchronize()
+    rt.read_device_error(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            wa.attn_prefill(q, k, v, causal=True, out=out)
+        ev1.record()
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    rt.read_device_error(dev)
+    flops = 4.0 * B * H * Dh * L * L / 2
+    tf = flops / (ms * 1e-3) / 1e12
+    try:
+        peak, kind = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]), "measured"
+    except Exception:
+        peak, kind = 1590.0, "fallback"
+    print(json.dumps({"metric": "prompt attention TFLOP/s (config-4 layer, causal)", "value": tf, "unit": "TFLOP/s",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                      "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": "prefill_causal_attention", "batch": B, "prompt_len": L, "n_heads": H,
+                                 "head_dim": Dh},
+                      "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                                   "frac": tf / peak, "peak_kind": kind},
+                      "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
+
+
 def run_tick_profile(args):
     """--workload cfg4tick: per-tick kernel breakdown of greedy wavefront decoding
     on the device scheduler (diagnostic; prints a table, no JSON line).  Runs
@@ -946,6 +997,8 @@ def main():
         run_cfg4(args)
     elif args.workload == "cfg4tick":
         run_tick_profile(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     else:
         run_wfd(args)
 
