@@ -187,12 +187,12 @@ EncodeTiledFn encode_tiled() {
 
 // (Dh, Hkv, rows) bf16 key / value buffer (Dh 64 or 128); box = 64 dims x 1 head x
 // 128 rows, 128-byte swizzle (the UMMA SWIZZLE_128B layout); rows past the end read as 0.
-bool make_kv_map(CUtensorMap* m, const void* base, long long rows, int Hkv, int Dh) {
+bool make_kv_map(CUtensorMap* m, const void* base, long long rows, int Hkv, int Dh, int box_rows = kTcTile) {
   EncodeTiledFn fn = encode_tiled();
   if (!fn) return false;
   cuuint64_t dims[3] = {(cuuint64_t)Dh, (cuuint64_t)Hkv, (cuuint64_t)rows};
   cuuint64_t strides[2] = {(cuuint64_t)Dh * 2, (cuuint64_t)Hkv * Dh * 2};
-  cuuint32_t box[3] = {64, 1, (cuuint32_t)kTcTile};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
   cuuint32_t es[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -200,7 +200,8 @@ bool make_kv_map(CUtensorMap* m, const void* base, long long rows, int Hkv, int 
 }
 
 template <int NQP, int DH, int NA>
-int launch_tc(const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& tv, int sms, cudaStream_t st) {
+int launch_tc(const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& tv, const TailMaps& tails, int sms,
+              cudaStream_t st) {
   using C = TcCfg<NQP, DH>;
   static bool attr_set[kMaxDevices] = {};
   int dev = 0;
@@ -211,7 +212,7 @@ int launch_tc(const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& 
       return WFD_ERR_CUDA;
     attr_set[dev] = true;
   }
-  if (launch_pdl(wave_tc_kernel<NQP, DH, NA>, dim3(sms), dim3(tc_threads(NQP)), C::SMEM, st, tk, tv, vp) !=
+  if (launch_pdl(wave_tc_kernel<NQP, DH, NA>, dim3(sms), dim3(tc_threads(NQP)), C::SMEM, st, tk, tv, tails, vp) !=
       cudaSuccess)
     return WFD_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
@@ -225,12 +226,12 @@ int verify_active(int nqp, int G, int max_q) {
 }
 
 template <int DH>
-int launch_tc_dh(int nqp, int na, const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& tv, int sms,
-                 cudaStream_t st) {
-  if (nqp == 32) return launch_tc<32, DH, 32>(vp, tk, tv, sms, st);
-  if (na == 1) return launch_tc<16, DH, 1>(vp, tk, tv, sms, st);
-  if (na == 4) return launch_tc<16, DH, 4>(vp, tk, tv, sms, st);
-  return launch_tc<16, DH, 16>(vp, tk, tv, sms, st);
+int launch_tc_dh(int nqp, int na, const VerifyParams& vp, const CUtensorMap& tk, const CUtensorMap& tv,
+                 const TailMaps& tails, int sms, cudaStream_t st) {
+  if (nqp == 32) return launch_tc<32, DH, 32>(vp, tk, tv, tails, sms, st);
+  if (na == 1) return launch_tc<16, DH, 1>(vp, tk, tv, tails, sms, st);
+  if (na == 4) return launch_tc<16, DH, 4>(vp, tk, tv, tails, sms, st);
+  return launch_tc<16, DH, 16>(vp, tk, tv, tails, sms, st);
 }
 
 // Dh: the cache's head dim (tensor maps); kdh: the kernel's (128 for head pairs).
@@ -238,9 +239,15 @@ int launch_verify(int nqp, int na, const VerifyParams& vp, const void* k, const 
                   int Dh, int kdh, int sms, cudaStream_t st) {
   if (rows <= 0 || rows >= (1ll << 31)) return WFD_ERR_UNSUPPORTED;  // TMA row coordinates are int32
   if ((Dh != 64 && Dh != 128) || (kdh != Dh && !(Dh == 64 && kdh == 128 && vp.pair))) return WFD_ERR_UNSUPPORTED;
+  // full (128-row) boxes, and the tail pieces (64, 32, 16, 8 rows)
   CUtensorMap tk, tv;
+  TailMaps tails;
   if (!make_kv_map(&tk, k, rows, Hkv, Dh) || !make_kv_map(&tv, v, rows, Hkv, Dh)) return WFD_ERR_CUDA;
-  return kdh == 128 ? launch_tc_dh<128>(nqp, na, vp, tk, tv, sms, st) : launch_tc_dh<64>(nqp, na, vp, tk, tv, sms, st);
+  for (int pc = 0; pc < 4; ++pc)
+    if (!make_kv_map(&tails.k[pc], k, rows, Hkv, Dh, 64 >> pc) || !make_kv_map(&tails.v[pc], v, rows, Hkv, Dh, 64 >> pc))
+      return WFD_ERR_CUDA;
+  return kdh == 128 ? launch_tc_dh<128>(nqp, na, vp, tk, tv, tails, sms, st)
+                    : launch_tc_dh<64>(nqp, na, vp, tk, tv, tails, sms, st);
 }
 
 // Common core of every attention entry point: plan, then attend.

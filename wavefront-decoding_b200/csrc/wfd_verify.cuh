@@ -62,6 +62,12 @@ constexpr int kTcTile = 128;        // keys per tile == MMA M
 // threads: TMA warp + MMA warp + 4 softmax warps per 16 query columns
 __host__ __device__ constexpr int tc_threads(int nqp) { return nqp == 32 ? 320 : 192; }
 
+// Tensor maps of the tail pieces of a K / V tile: boxes of 64, 32, 16 and 8 rows.
+struct TailMaps {
+  CUtensorMap k[4];
+  CUtensorMap v[4];
+};
+
 struct VerifyParams {
   const void* q;
   void* out;
@@ -367,7 +373,7 @@ struct UnitIter {
 template <int NQP, int DH, int NA>
 __global__ void __launch_bounds__(tc_threads(NQP), 1)
     wave_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                   const VerifyParams p) {
+                   const __grid_constant__ TailMaps tails, const VerifyParams p) {
   using C = TcCfg<NQP, DH>;
   constexpr int STAGES = C::STAGES;
   constexpr int KB = C::KB;
@@ -429,6 +435,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   if (tid == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_k)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_v)) : "memory");
+
   }
 
   if (tid == 0) {
@@ -618,13 +625,35 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         if (go && lane == 0) {
           unsigned char* dst = kvs + stage * C::KV_STAGE;
           const int row = (int)(row0 + (long long)t * kTcTile);
-          mbar_arrive_expect_tx(&bar_full[stage], (uint32_t)C::KV_STAGE);
+          // A tail tile with at most 96 rows of this range loads only those rows,
+          // rounded up to 8: pieces of 64 / 32 / 16 / 8 rows (1 KB-aligned in the
+          // 128B-swizzled stage, so the layout is that of a full box).  The stage's
+          // other rows keep older data, masked like every key past the range
+          // (scores -inf, V rows zeroed by the softmax).  Longer tails take the
+          // full box: the few rows saved do not pay for the extra copies.
+          const int rows_left = r_hi - r_lo - t * kTcTile;
+          const int nr = rows_left > 96 ? kTcTile : ((rows_left + 7) & ~7);
+          mbar_arrive_expect_tx(&bar_full[stage], (uint32_t)(nr * 128 * 2 * KB));
 #pragma unroll
           for (int bx = 0; bx < KB; ++bx) {
             // box bx: dims 64bx.. of head h, or (pair) head 2h + bx
             const int cx = p.pair ? 0 : 64 * bx, ch = p.pair ? 2 * h + bx : h;
-            tma_load_3d(dst + bx * C::BOX_BYTES, &tm_k, cx, ch, row, &bar_full[stage]);
-            tma_load_3d(dst + (KB + bx) * C::BOX_BYTES, &tm_v, cx, ch, row, &bar_full[stage]);
+            if (nr == kTcTile) {
+              tma_load_3d(dst + bx * C::BOX_BYTES, &tm_k, cx, ch, row, &bar_full[stage]);
+              tma_load_3d(dst + (KB + bx) * C::BOX_BYTES, &tm_v, cx, ch, row, &bar_full[stage]);
+            } else {
+              int off = 0;
+#pragma unroll
+              for (int pc = 0; pc < 4; ++pc) {
+                const int pr = 64 >> pc;  // piece rows
+                if (nr & pr) {
+                  tma_load_3d(dst + bx * C::BOX_BYTES + off * 128, &tails.k[pc], cx, ch, row + off, &bar_full[stage]);
+                  tma_load_3d(dst + (KB + bx) * C::BOX_BYTES + off * 128, &tails.v[pc], cx, ch, row + off,
+                              &bar_full[stage]);
+                  off += pr;
+                }
+              }
+            }
           }
           n_iss = it + 1;
           if (p.fail_waits && n_iss == 1) {  // test hook: give up with this tile's copies in flight
