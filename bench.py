@@ -363,6 +363,71 @@ def cfg3_cpu_sample(K, V, q, kn, vn, items, n_items: int = 4):
     return Kc, Vc, torch.cat(qs), torch.cat(ks), torch.cat(vs), its
 
 
+# bounded CPU sample of config 4: the first B of the 64 sequences (prompt K / V drawn,
+# not computed), decode rate = the tokens of a `long` generation minus those of a
+# `short` one over the difference of their decode times (pipeline fill cancels)
+CFG4_CPU = dict(B=16, short=2, long=6)
+
+
+def cfg4_cpu_baseline(t_draft: int, kv_budget: int, alpha, steps: int = 1, budget_s: float = 150.0):
+    """The reference's decode loop on the host cores: oracle/cpu_path.LoopedBlocksCPU
+    (write_tokens + gather_pack + SDPA varlen loop per layer, bf16 torch CPU)
+    driven by the package's host wavefront scheduler, on CFG4_CPU's sample of the
+    config-4 workload.  One step = one (short, long) pair of generations."""
+    import torch
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from oracle import cpu_path
+    from wavefront_decoding_b200 import scheduler as sch
+    from wavefront_decoding_b200.looped_lm import CONFIG4
+
+    cfg = CONFIG4
+    dims = {k: getattr(cfg, k) for k in ("vocab", "d_model", "n_heads", "n_kv_heads", "head_dim", "d_ff",
+                                         "n_prelude", "n_core", "n_coda", "T_total", "norm_eps", "rope_theta",
+                                         "rope_style")}
+    dims["kv_budget_s"] = kv_budget
+    B, L, short, long_ = CFG4_CPU["B"], CFG4["L"], CFG4_CPU["short"], CFG4_CPU["long"]
+    prompts = torch.randint(0, cfg.vocab, (CFG4["B"], L),
+                            generator=torch.Generator().manual_seed(CFG4["seed"]))[:B].contiguous()
+    W = cpu_path.random_weights(dims, CFG4["model_seed"])
+    blocks = cpu_path.LoopedBlocksCPU(W, dims, B, L + long_ + 2 * cfg.T_total + 8, synthetic_prompt=True,
+                                      seed=CFG4["seed"])
+    policy = sch.SsdPolicy(cfg.T_total, t_draft)
+
+    def generate(n):
+        emus = None
+        if alpha is not None:
+            emus = [sch.EmulatedAcceptance(alpha, seed=CFG4["emu_seed"] * 1_000_003 + b) for b in range(B)]
+        bt = sch.generate_wavefront_batch(blocks, prompts, n, policy, emus)
+        prop = sum(t.n_drafts_proposed for t in bt.per_seq)
+        acc = sum(t.n_drafts_accepted for t in bt.per_seq)
+        return bt.n_tokens, bt.walltime_s - bt.prefill_s, prop, acc
+
+    generate(short)                                   # warm-up
+    d_tok = d_s = prop = acc = 0
+    n = 0
+    t_start = time.perf_counter()
+    while n < max(1, steps):
+        a = generate(short)
+        b = generate(long_)
+        d_tok += b[0] - a[0]
+        d_s += b[1] - a[1]
+        prop += b[2]
+        acc += b[3]
+        n += 1
+        if time.perf_counter() - t_start > budget_s:
+            break
+    rate = d_tok / d_s
+    return {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{B} of the {CFG4['B']} config-4 sequences, prompt {L} (prompt K/V drawn at random, the "
+                      f"prompt pass is outside the decode region), wavefront T_draft {t_draft}: decode tokens of "
+                      f"a {long_}-token generation minus a {short}-token one over the decode-time difference, "
+                      f"{n} pair(s); per layer write_tokens + gather_pack + SDPA varlen loop, bf16 torch CPU",
+            "acceptance_rate": acc / prop if prop else None, "steps": n,
+            "ms_per_token_step": 1e3 * d_s / max(1, d_tok) * B, "host_cpu_count": os.cpu_count()}
+
+
 def host_threads() -> int:
     """Every core this process may run on, whatever OMP_NUM_THREADS says (torchrun
     sets it to 1 per rank): the CPU baseline gets the whole host."""
@@ -384,9 +449,17 @@ def run_reference(args):
         return
     host_threads()
     if args.workload == "cfg4":
-        print(json.dumps({"impl": "reference", "unavailable": "cfg4 (end-to-end 381M-parameter model, 64 x 1024 "
-                          "prompts, 256 tokens) is not timed on the host cores; the reference arm covers the "
-                          "attention configs 2 and 3"}), flush=True)
+        base = cfg4_cpu_baseline(args.t_draft, args.kv_budget, args.alpha, steps=max(1, args.steps))
+        line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": base["steps"], "warmup": 1,
+                "ms_per_step": base["ms_per_token_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, uniform random "
+                "prompt ids)", "config": cfg4_config(args, world),
+                "acceptance_rate": base["acceptance_rate"],
+                "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     if args.workload == "cfg2":
         c, q, K, V, kn, vn, items = cfg2_cpu_inputs(CFG2["seed"], args.batch)
@@ -784,11 +857,29 @@ def cfg4_e2e_record(dev, world: int, rank: int) -> dict:
             "tokens_per_s_per_gpu": r["tot_tokens"] / (r["dec_max"] * 1e-3) / world,
             "ms_decode": r["dec_max"], "ms_with_prefill": r["all_max"],
             "acceptance_rate": (r["tot_acc"] / r["tot_prop"]) if r["tot_prop"] else None,
-            "config": {"model": "looped LM 770M (config 4), random init, bf16", "global_batch": CFG4["B"],
+            "config": {"model": f"looped LM config 4 ({r['cfg'].n_params() / 1e6:.0f}M params), random init, "
+                                "bf16", "global_batch": CFG4["B"],
                        "batch_per_gpu": r["Bl"], "prompt_len": CFG4["L"], "new_tokens": CFG4_E2E_NEW,
                        "T_draft": 2, "scheduler": "device", "parallelism": f"sequences sharded, {world} rank(s)"},
             "timing": "one timed generation after one warm-up, CUDA events, max over ranks; value = decode "
                       "region, e2e = with prompt upload and prefill"}
+
+
+def cfg4_config(args, world: int) -> dict:
+    from wavefront_decoding_b200.looped_lm import CONFIG4 as cfg
+    Bg = args.batch or CFG4["B"]
+    return {"workload": "cfg4_looped_lm_e2e_greedy_decode",
+            "model": f"looped LM {cfg.n_params() / 1e6:.0f}M params: vocab {cfg.vocab}, d {cfg.d_model}, "
+                     f"{cfg.n_heads}x{cfg.head_dim} heads (kv {cfg.n_kv_heads}), SwiGLU {cfg.d_ff}, "
+                     f"prelude {cfg.n_prelude} / core {cfg.n_core} x R={cfg.T_total} / coda {cfg.n_coda}",
+            "global_batch": Bg, "batch_per_gpu": Bg // world if Bg % world == 0 else f"{Bg // world}-{-(-Bg // world)}",
+            "prompt_len": CFG4["L"], "new_tokens": args.new_tokens or CFG4["new"],
+            "T_draft": args.t_draft, "scheduler": args.scheduler, "batch_invariant": args.batch_invariant,
+            "draft_length": args.draft_length if args.scheduler == "dtv" else None,
+            "kv_budget_s": args.kv_budget,
+            "acceptance": "greedy gold == draft" if args.alpha is None else f"emulated Bernoulli({args.alpha})",
+            "parallelism": f"sequences sharded, {world} rank(s), no collective on the hot path",
+            "timing": "decode region per generation, CUDA events, max over ranks; KV working set > L2, no flush"}
 
 
 def run_cfg4(args):
@@ -824,19 +915,7 @@ def run_cfg4(args):
         "warmup": max(1, args.warmup), "ms_per_step": r["dec_max"] / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, "
         "uniform random prompt ids)",
-        "config": {"workload": "cfg4_looped_lm_e2e_greedy_decode",
-                   "model": f"looped LM {cfg.n_params() / 1e6:.0f}M params: vocab {cfg.vocab}, d {cfg.d_model}, "
-                            f"{cfg.n_heads}x{cfg.head_dim} heads (kv {cfg.n_kv_heads}), SwiGLU {cfg.d_ff}, "
-                            f"prelude {cfg.n_prelude} / core {cfg.n_core} x R={cfg.T_total} / coda {cfg.n_coda}",
-                   "global_batch": Bg, "batch_per_gpu": Bl if Bg % world == 0 else f"{Bg // world}-{-(-Bg // world)}",
-                   "prompt_len": CFG4["L"], "new_tokens": new,
-                   "T_draft": args.t_draft, "scheduler": args.scheduler, "batch_invariant": args.batch_invariant,
-                   "draft_length": args.draft_length if args.scheduler == "dtv" else None,
-                   "kv_budget_s": args.kv_budget,
-                   "acceptance": "greedy gold == draft" if args.alpha is None else f"emulated Bernoulli({args.alpha})",
-                   "parallelism": f"sequences sharded, {world} rank(s), no collective on the hot path",
-                   "timing": "decode region per generation, CUDA events, max over ranks; "
-                             "KV working set > L2, no flush"},
+        "config": cfg4_config(args, world),
         "tokens_per_s_per_gpu": value / world,
         "acceptance_rate": (r["tot_acc"] / r["tot_prop"]) if r["tot_prop"] else None,
         "ticks_per_generation": r["ticks"] / args.steps,
@@ -851,6 +930,10 @@ def run_cfg4(args):
         "clocks": r["clocks"],
         "cpu_baseline": None,
     }
+    if world == 1 and not args.no_cpu_baseline:
+        host_threads()
+        base = cfg4_cpu_baseline(args.t_draft, args.kv_budget, args.alpha)
+        line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps(line), flush=True)
 
 
