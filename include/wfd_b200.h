@@ -37,8 +37,8 @@ extern "C" {
 
 /* Raised whenever a declaration or a struct layout below changes incompatibly
  * (2: wfd_sched_params.depth_slots; 3: wfd_commit_window takes n_rows;
- * 4: wfd_sched_params.gap_windows). */
-#define WFD_ABI_VERSION 4
+ * 4: wfd_sched_params.gap_windows; 5: wfd_linear). */
+#define WFD_ABI_VERSION 5
 
 enum wfd_status {
   WFD_OK = 0,
@@ -300,6 +300,47 @@ int wfd_rope_split(const void* qkv, const float* cos_tab, const float* sin_tab, 
 /* SwiGLU gate: out (n, dff) = silu(g) * u where gu (n, 2 dff) = [g | u] per row
  * (dff % 8 == 0). */
 int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, int32_t dtype, void* stream);
+
+/* Linear layer of a few rows on the tensor cores with the block's element-wise
+ * work fused in (bf16; fp32 accumulation).  y = s_r * x_r . W for W (K, F)
+ * row-major, where s_r = rsqrt(mean(x_r^2) + eps) when row_norm is set (an
+ * RMSNorm whose weight the caller has multiplied into W's rows) and 1 otherwise;
+ * then, by mode:
+ *   WFD_LINEAR_PLAIN     out (n_rows, F) = y
+ *   WFD_LINEAR_RESIDUAL  out (n_rows, F) += y, in place
+ *   WFD_LINEAR_SWIGLU    W's columns interleave gate and up projections per 64
+ *                        (columns 128j.. = gate features 64j..64j+63, then the up
+ *                        features 64j..): out (n_rows, F / 2) = silu(g) * u, with g
+ *                        and u rounded to bf16 first (F % 128 == 0)
+ *   WFD_LINEAR_ROPE      F = (H + 2 Hkv) Dh (F % 128 == 0, Dh 64 or 128): y rounded to
+ *                        bf16, then split and rotated as wfd_rope_split does
+ * The reference runs these as framework modules around its attention backend
+ * (RMSNorm, q/k/v/o projections, RoPE, SwiGLU MLP; ouro_blocks_batch.py:100-121),
+ * so this has no C counterpart in it.  Rows are processed independently of each
+ * other: a row's result does not depend on n_rows.  x, w, out, q, k, v 16-byte
+ * aligned; K % 8 == 0, ldx % 8 == 0, ldx >= K. */
+enum wfd_linear_mode { WFD_LINEAR_PLAIN = 0, WFD_LINEAR_RESIDUAL = 1, WFD_LINEAR_SWIGLU = 2, WFD_LINEAR_ROPE = 3 };
+
+typedef struct wfd_linear_params {
+  const void* x;            /* (n_rows, K) bf16 rows, row stride ldx elements          */
+  const void* w;            /* (K, F) bf16, row-major                                    */
+  void* out;                /* plain / residual: row stride ldo; swiglu: (n_rows, F / 2) */
+  void* q;                  /* rope: q (n_rows, H, Dh), k / v (n_rows, Hkv, Dh)         */
+  void* k;
+  void* v;
+  const float* cos_tab;     /* rope: (max_pos, Dh / 2) fp32                              */
+  const float* sin_tab;
+  const int32_t* pos;       /* rope: row r at pos[r * pos_stride]; NULL: r % pos_period  */
+  int32_t* err;             /* device error word (wfd_read_error)                        */
+  int32_t n_rows, K, F, ldx, ldo;
+  int32_t mode, row_norm;
+  float eps;
+  int32_t H, Hkv, Dh, rope_style, pos_stride, pos_period, max_pos;
+} wfd_linear_params;
+
+int wfd_linear(const wfd_linear_params* p, void* stream);
+/* sizeof(wfd_linear_params) as compiled into the library. */
+size_t wfd_linear_params_bytes(void);
 
 /* Row gather: out[i] = a[idx[i * idx_stride]] (+ b[same row] when b != NULL),
  * rows of d elements (d % 8 == 0), n_src rows in a / b.  An index outside

@@ -42,7 +42,7 @@ def test_python_binding_covers_header(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.wfd_abi_version() == 4
+    assert lib.wfd_abi_version() == 5
     assert lib.wfd_status_string(0) == b"ok"
     assert b"workspace" in lib.wfd_status_string(3)
 
@@ -52,6 +52,7 @@ def test_item_struct_layout(lib):
     assert ctypes.sizeof(_abi.wfd_item) == 20
     # the ctypes mirror of the scheduler parameters matches the compiled struct
     assert ctypes.sizeof(_abi.wfd_sched_params) == lib.wfd_sched_params_bytes()
+    assert ctypes.sizeof(_abi.wfd_linear_params) == lib.wfd_linear_params_bytes()
 
 
 def test_product_does_not_import_oracle():

@@ -28,7 +28,10 @@ EXPORTED = (
     "wfd_items_from_table", "wfd_argmax_rows",
     "wfd_sched_pre_tick", "wfd_sched_route", "wfd_sched_settle", "wfd_sched_params_bytes",
     "wfd_set_batch_invariant", "wfd_get_batch_invariant", "wfd_test_fail_waits",
+    "wfd_linear", "wfd_linear_params_bytes",
 )
+
+WFD_LINEAR_PLAIN, WFD_LINEAR_RESIDUAL, WFD_LINEAR_SWIGLU, WFD_LINEAR_ROPE = 0, 1, 2, 3
 
 
 class WfdError(RuntimeError):
@@ -44,7 +47,7 @@ class wfd_item(ctypes.Structure):
                 ("q_len", ctypes.c_int32), ("q_row0", ctypes.c_int32)]
 
 
-ABI_VERSION = 4  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
+ABI_VERSION = 5  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
 
 
 class wfd_sched_params(ctypes.Structure):
@@ -56,6 +59,15 @@ class wfd_sched_params(ctypes.Structure):
             "B", "W", "T_total", "T_draft", "max_new", "emu_len", "n_core", "n_kv_slots", "lens_stride",
             "max_seq", "p_cols", "c_cols", "r_cap", "scratch_row", "scratch_seq", "p_slot0", "n_prelude",
             "c_slot0", "n_coda", "depth_slots", "gap_windows")]
+
+
+class wfd_linear_params(ctypes.Structure):
+    """include/wfd_b200.h: wfd_linear_params (field order and types must match)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "x", "w", "out", "q", "k", "v", "cos_tab", "sin_tab", "pos", "err")] + \
+        [(n, ctypes.c_int32) for n in ("n_rows", "K", "F", "ldx", "ldo", "mode", "row_norm")] + \
+        [("eps", ctypes.c_float)] + \
+        [(n, ctypes.c_int32) for n in ("H", "Hkv", "Dh", "rope_style", "pos_stride", "pos_period", "max_pos")]
 
 
 _P = ctypes.c_void_p
@@ -113,6 +125,9 @@ _SIGS = {
     "wfd_set_batch_invariant": ([_I], _I),
     "wfd_get_batch_invariant": ([], _I),
     "wfd_test_fail_waits": ([_I], _I),
+    # const wfd_linear_params*, stream
+    "wfd_linear": ([_P, _P], _I),
+    "wfd_linear_params_bytes": ([], _S),
     # const wfd_sched_params*, stream
     "wfd_sched_pre_tick": ([_P, _P], _I),
     "wfd_sched_route": ([_P, _P], _I),

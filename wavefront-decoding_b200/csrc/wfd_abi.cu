@@ -15,6 +15,7 @@
 #include "wfd_cache.cuh"
 #include "wfd_common.cuh"
 #include "wfd_decode.cuh"
+#include "wfd_linear.cuh"
 #include "wfd_model.cuh"
 #include "wfd_sched.cuh"
 #include "wfd_plan.cuh"
@@ -969,6 +970,154 @@ extern "C" int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, i
   } else
     return WFD_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+// ---- K8: skinny linear layers (wfd_linear) ----
+namespace {
+
+// (K, F) bf16 weights: box = 64 features x 128 k rows, 128-byte swizzle (the
+// MN-major A operand); features or k rows past the end read as 0.
+bool make_w_map(CUtensorMap* m, const void* base, int K, int F) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)F, (cuuint64_t)K};
+  cuuint64_t strides[1] = {(cuuint64_t)F * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)kLinTile};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// (n_rows, K) bf16 rows of stride ldx: box = 64 k x np rows, 128-byte swizzle (the
+// K-major B operand); rows past n_rows read as 0.
+bool make_x_map(CUtensorMap* m, const void* base, int n_rows, int K, int ldx, int np) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)n_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)np};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// k ranges per feature tile (= the cluster size): the largest of 1, 2, 4, 8 with
+// at least one 128-row k stage per CTA and at most 7/4 CTAs per SM, so the
+// clusters of a launch are resident at once when two CTAs fit an SM (up to 32
+// rows per block; whole clusters must fit a GPC).  Depends on F, K and the SM
+// count only, never on the row count: the merge order of a row stays the same.
+constexpr int kLinMaxSplit = 8;
+int linear_split(int n_tiles, int n_k, int sms) {
+  int s = 1;
+  while (2 * s <= kLinMaxSplit && 2 * s <= n_k && (long long)n_tiles * 2 * s * 4 <= 7ll * sms) s *= 2;
+  return s;
+}
+
+template <int NP>
+int launch_linear(const LinearParams& lp, const CUtensorMap& tw, const CUtensorMap& tx, dim3 grid, int split,
+                  cudaStream_t st) {
+  using C = LinCfg<NP>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(linear_tc_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
+      return WFD_ERR_CUDA;
+    attr_set[dev] = true;
+  }
+  // programmatic stream serialization + one cluster per feature tile (its k ranges)
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kLinThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)split;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (cudaLaunchKernelEx(&cfg, linear_tc_kernel<NP>, tw, tx, lp) != cudaSuccess) return WFD_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" size_t wfd_linear_params_bytes(void) { return sizeof(wfd_linear_params); }
+
+extern "C" int wfd_linear(const wfd_linear_params* a, void* stream) {
+  if (!a) return WFD_ERR_INVALID_ARG;
+  const int n = a->n_rows, K = a->K, F = a->F;
+  if (n < 0 || K <= 0 || F <= 0 || K % 8 != 0 || F % 8 != 0 || a->ldx < K || a->ldx % 8 != 0)
+    return WFD_ERR_INVALID_ARG;
+  if (a->mode < WFD_LINEAR_PLAIN || a->mode > WFD_LINEAR_ROPE) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!a->x || !a->w || !a->err) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(a->x) || !aligned16(a->w)) return WFD_ERR_ALIGNMENT;
+  if (a->mode == WFD_LINEAR_ROPE) {
+    if (a->Dh != 64 && a->Dh != 128) return WFD_ERR_UNSUPPORTED;
+    if (a->H <= 0 || a->Hkv <= 0 || (long long)(a->H + 2 * a->Hkv) * a->Dh != F || F % kLinTile != 0)
+      return WFD_ERR_INVALID_ARG;
+    if (a->rope_style != 0 && a->rope_style != 1) return WFD_ERR_INVALID_ARG;
+    if (!a->q || !a->k || !a->v || !a->cos_tab || !a->sin_tab || a->max_pos <= 0) return WFD_ERR_INVALID_ARG;
+    if (a->pos ? a->pos_stride < 1 : a->pos_period < 1) return WFD_ERR_INVALID_ARG;
+  } else {
+    if (!a->out) return WFD_ERR_INVALID_ARG;
+    const int width = a->mode == WFD_LINEAR_SWIGLU ? F / 2 : F;
+    if (a->mode == WFD_LINEAR_SWIGLU && F % kLinTile != 0) return WFD_ERR_INVALID_ARG;
+    if (a->ldo < width) return WFD_ERR_INVALID_ARG;
+  }
+  const int sms = current_sms();
+  if (sms <= 0) return WFD_ERR_CUDA;
+  const int np = n <= 16 ? 16 : (n <= 32 ? 32 : 64);
+  const int rb = (n + np - 1) / np;
+  const int n_tiles = (F + kLinTile - 1) / kLinTile;
+  const int n_k = (K + kLinTile - 1) / kLinTile;
+  const int split = linear_split(n_tiles, n_k, sms);
+  if ((long long)n_tiles * split >= (1ll << 31) || rb > 65535) return WFD_ERR_UNSUPPORTED;
+
+  LinearParams lp;
+  memset(&lp, 0, sizeof(lp));
+  lp.n_rows = n;
+  lp.K = K;
+  lp.F = F;
+  lp.n_k = n_k;
+  lp.n_tiles = n_tiles;
+  lp.split = split;
+  lp.mode = a->mode;
+  lp.row_norm = a->row_norm ? 1 : 0;
+  lp.eps = a->eps;
+  lp.out = static_cast<__nv_bfloat16*>(a->out);
+  lp.ldo = a->ldo;
+  lp.q = static_cast<__nv_bfloat16*>(a->q);
+  lp.k = static_cast<__nv_bfloat16*>(a->k);
+  lp.v = static_cast<__nv_bfloat16*>(a->v);
+  lp.H = a->H;
+  lp.Hkv = a->Hkv;
+  lp.Dh = a->Dh;
+  lp.style = a->rope_style;
+  lp.cosb = a->cos_tab;
+  lp.sinb = a->sin_tab;
+  lp.pos = a->pos;
+  lp.pos_stride = a->pos_stride;
+  lp.pos_period = a->pos_period;
+  lp.max_pos = a->max_pos;
+  lp.err = a->err;
+
+  CUtensorMap tw, tx;
+  if (!make_w_map(&tw, a->w, K, F) || !make_x_map(&tx, a->x, n, K, a->ldx, np)) return WFD_ERR_CUDA;
+  const dim3 grid((unsigned)(n_tiles * split), (unsigned)rb);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (np == 16) return launch_linear<16>(lp, tw, tx, grid, split, st);
+  if (np == 32) return launch_linear<32>(lp, tw, tx, grid, split, st);
+  return launch_linear<64>(lp, tw, tx, grid, split, st);
 }
 
 extern "C" int wfd_gather_rows(const void* a, const void* b, const int32_t* idx, int32_t idx_stride, void* out,

@@ -124,3 +124,97 @@ def argmax_rows(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     _abi.check(st, "wfd_argmax_rows")
     return out
 
+
+
+# ---------------------------------------------------------------------------
+# skinny linear layers on the tensor cores (wfd_linear): a few rows times a
+# weight matrix, with the block's RMSNorm / residual / SwiGLU / RoPE fused in
+# ---------------------------------------------------------------------------
+def fold_norm(w: torch.Tensor, norm: torch.Tensor) -> torch.Tensor:
+    """W' = diag(norm) W (rows of W scaled by the RMSNorm weight), for a linear
+    call with the row norm on: s_r x_r . W' == (x_r * s_r * norm) . W."""
+    return (norm.float()[:, None] * w.float()).to(w.dtype).contiguous()
+
+
+def interleave_gate_up(wgu: torch.Tensor) -> torch.Tensor:
+    """(K, 2 dff) = [gate | up] -> columns interleaved per 64 (gate 64j.., then up
+    64j..), the layout the SwiGLU mode of wfd_linear reads (dff % 64 == 0)."""
+    K, two_dff = wgu.shape
+    dff = two_dff // 2
+    assert dff % 64 == 0
+    return wgu.view(K, 2, dff // 64, 64).permute(0, 2, 1, 3).reshape(K, two_dff).contiguous()
+
+
+def _linear(x: torch.Tensor, w: torch.Tensor, mode: int, *, out=None, norm_eps=None, q=None, k=None, v=None,
+            rope=None) -> None:
+    import ctypes
+    dev = rt.require_cuda(x, w)
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise TypeError("wfd_linear takes bf16 rows and weights")
+    if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[0] or x.stride(1) != 1 or not w.is_contiguous():
+        raise ValueError(f"wfd_linear: x {tuple(x.shape)} (row-major rows) against W {tuple(w.shape)} (contiguous)")
+    n, K = x.shape
+    p = _abi.wfd_linear_params()
+    p.x, p.w, p.ldx = x.data_ptr(), w.data_ptr(), x.stride(0)
+    p.n_rows, p.K, p.F = n, K, w.shape[1]
+    p.mode = mode
+    p.row_norm = 0 if norm_eps is None else 1
+    p.eps = 0.0 if norm_eps is None else float(norm_eps)
+    if out is not None:
+        if out.dtype != torch.bfloat16 or out.dim() != 2 or out.stride(1) != 1 or out.shape[0] != n:
+            raise ValueError("wfd_linear: out must be bf16 (n_rows, width) rows")
+        p.out, p.ldo = out.data_ptr(), out.stride(0)
+    if rope is not None:
+        cos, sin, H, Hkv, Dh, pos, pos_period, interleaved = rope
+        p.q, p.k, p.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+        p.cos_tab, p.sin_tab, p.max_pos = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+        p.H, p.Hkv, p.Dh, p.rope_style = H, Hkv, Dh, 1 if interleaved else 0
+        if pos is not None:
+            assert pos.dtype == torch.int32 and pos.dim() == 1 and pos.shape[0] >= n
+            p.pos, p.pos_stride = pos.data_ptr(), pos.stride(0)
+        else:
+            assert pos_period > 0
+            p.pos_period = pos_period
+    p.err = rt.error_word(dev).data_ptr()
+    _abi.check(_abi.load().wfd_linear(ctypes.byref(p), rt.stream_ptr(dev)), "wfd_linear")
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+           norm_eps: float | None = None) -> torch.Tensor:
+    """out (n, F) = x (n, K) @ w (K, F); with norm_eps each row is first scaled by
+    rsqrt(mean(x^2) + eps) (an RMSNorm whose weight is folded into w: fold_norm)."""
+    if out is None:
+        out = torch.empty((x.shape[0], w.shape[1]), dtype=x.dtype, device=x.device)
+    _linear(x, w, _abi.WFD_LINEAR_PLAIN, out=out, norm_eps=norm_eps)
+    return out
+
+
+def linear_residual(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out (n, F) += x (n, K) @ w (K, F), in place."""
+    _linear(x, w, _abi.WFD_LINEAR_RESIDUAL, out=out)
+    return out
+
+
+def linear_swiglu(x: torch.Tensor, w_il: torch.Tensor, norm_eps: float | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(g) * u (n, dff) of g | u = x @ W for W given in the interleaved layout
+    of interleave_gate_up (optionally row-normed: fold_norm before interleaving)."""
+    if out is None:
+        out = torch.empty((x.shape[0], w_il.shape[1] // 2), dtype=x.dtype, device=x.device)
+    _linear(x, w_il, _abi.WFD_LINEAR_SWIGLU, out=out, norm_eps=norm_eps)
+    return out
+
+
+def linear_rope(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads: int,
+                n_kv_heads: int, head_dim: int, *, pos: torch.Tensor | None = None, pos_period: int = 0,
+                interleaved: bool = False, norm_eps: float | None = None):
+    """q (n, H, Dh), k, v (n, Hkv, Dh) of the fused QKV projection x @ w with RoPE
+    at each row's position (as rope_split on the bf16 projection)."""
+    n = x.shape[0]
+    assert cos.dtype == torch.float32 and sin.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous()
+    q = torch.empty((n, n_heads, head_dim), dtype=x.dtype, device=x.device)
+    k = torch.empty((n, n_kv_heads, head_dim), dtype=x.dtype, device=x.device)
+    v = torch.empty((n, n_kv_heads, head_dim), dtype=x.dtype, device=x.device)
+    _linear(x, w, _abi.WFD_LINEAR_ROPE, norm_eps=norm_eps, q=q, k=k, v=v,
+            rope=(cos, sin, n_heads, n_kv_heads, head_dim, pos, pos_period, interleaved))
+    return q, k, v
