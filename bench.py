@@ -63,6 +63,7 @@ UNIT = "GB/s"
 FALLBACK_HBM_GBS = 6650.0
 
 CFG2 = dict(B=8, R=8, H=16, Hkv=4, Dh=128, S=4096, seed=1)
+GRAPH_STEPS = 50  # attention workloads: consecutive steps captured per CUDA graph
 CFG3 = dict(B=32, R=8, H=32, Hkv=8, Dh=128, L0=8192, W=8, seed=2, accept_seed=3)
 CFG4 = dict(B=64, L=1024, new=256, seed=4, model_seed=0, emu_seed=5)
 # the attention op of one config-4 R tick: 64 sequences x 8 loop depths, MHA 24 x 64,
@@ -522,7 +523,7 @@ def workload_config(name, c, world, rows=None):
              "acceptance": f"Bernoulli({c['alpha']}) seed {c['seed']}, accepted prefix per sequence",
              "l2": "KV working set 137 GB > L2, no flush"}
     d["parallelism"] = f"sequences sharded, {world} rank(s)"
-    d["timing"] = "CUDA graph replay"
+    d["timing"] = f"CUDA graphs of up to {GRAPH_STEPS} consecutive steps"
     if rows is not None:
         d["rows_per_step_per_gpu"] = rows
     return d
@@ -587,15 +588,25 @@ def run_wfd(args):
         step()
     torch.cuda.synchronize()
     rt.read_device_error(dev)
-    g = torch.cuda.CUDAGraph()
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(g, stream=s):
-            step()
-    torch.cuda.current_stream().wait_stream(s)
-    for _ in range(args.warmup):
-        g.replay()
+    # the K timed steps run as replays of graphs of up to GRAPH_STEPS consecutive
+    # steps (one replay per step would add a graph launch gap to every step)
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(n):
+                    step()
+        torch.cuda.current_stream().wait_stream(s)
+        return g
+
+    per = max(1, min(GRAPH_STEPS, args.steps))
+    g_full = capture(per)
+    g_rest = capture(args.steps % per) if args.steps % per else None
+    plan = [g_full] * (args.steps // per) + ([g_rest] if g_rest is not None else [])
+    for _ in range(max(1, -(-args.warmup // per))):
+        g_full.replay()
     torch.cuda.synchronize()
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -604,7 +615,7 @@ def run_wfd(args):
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         ev0.record()
-        for _ in range(args.steps):
+        for g in plan:
             g.replay()
         ev1.record()
         torch.cuda.synchronize()

@@ -126,7 +126,10 @@ struct TcCfg {
   // independent TMEM accumulators (k-steps j with j % CH == c go to chain c,
   // summed by the softmax warps): consecutive MMAs into one accumulator wait
   // for each other, so CH chains keep CH MMAs in flight.
-  static constexpr int CH = WFD_MMA_CHAINS;
+  // With 32 columns the softmax warps bound the tile period and a second chain
+  // doubles their TMEM reads (config 3: 1829 vs 1912 us a step with one chain);
+  // with 16 columns the chains let the MMA warp keep two MMAs in flight.
+  static constexpr int CH = NQP == 32 ? 1 : WFD_MMA_CHAINS;
   static constexpr int S_COL = 0;                          // S^T buffer sb, chain c: (sb * CH + c) * NQP
   static constexpr int O_COL = 2 * CH * NQP;               // O^T chain c: O_COL + c * NQP
   static constexpr int TMEM_USED = 3 * CH * NQP;
@@ -410,6 +413,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   __shared__ __align__(8) uint64_t bar_qfree[2];   // unit's S MMAs done with its Q^T (MMA commit)
   __shared__ __align__(8) uint64_t bar_drain;      // every MMA of the CTA complete (final MMA commit)
   __shared__ uint32_t s_tmem;
+  __shared__ int s_rp[NQP];  // gapped windows: each query column's row position (softmax warps)
   __shared__ volatile int s_abort;
   __shared__ int s_flag;
 
@@ -820,16 +824,17 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       const int nvh = S.q_len * p.G;                                   // query vectors per kv head
       const int nvec = (p.pair ? 2 * nvh : nvh) - qg * NQP;  // of this unit / group (may exceed NQP)
 
-      // gapped windows: the position of the row of each of this thread's columns
-      int rp[NL];
+      // gapped windows: the position of each column's row, in shared memory (not
+      // registers: the 32-column variant is at its register limit); the barrier at
+      // the end of the previous unit keeps it from being rewritten early
       if (p.row_pos != nullptr) {
-#pragma unroll
-        for (int j = 0; j < NL; ++j) {
-          const int n = col0 + j;
+        if (sq == 0 && lane < NL) {
+          const int n = col0 + lane;
           const int vn = (p.pair && n >= nvh) ? n - nvh : n;
           const int row = (p.pair ? vn : qg * NQP + n) / p.G;
-          rp[j] = n < nvec ? p.row_pos[(long long)(S.q_row0 + row) * p.row_pos_stride] : -1;
+          s_rp[n] = n < nvec ? p.row_pos[(long long)(S.q_row0 + row) * p.row_pos_stride] : -1;
         }
+        softmax_bar<SMT>();
       }
       // running column maxima live in shared memory (mst, log2-scaled), owned
       // by lanes 0..NL-1 of the first warp of each column slice
@@ -870,7 +875,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
 #pragma unroll
           for (int j = 0; j < NL; ++j) {
             const int n = col0 + j;
-            s[j] = (n < nlim && key <= rp[j]) ? s[j] : NEG_INF;  // the row sees keys up to its position
+            s[j] = (n < nlim && key <= s_rp[n]) ? s[j] : NEG_INF;  // the row sees keys up to its position
           }
         } else {
 #pragma unroll
