@@ -124,7 +124,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["wfd", "reference"], default="wfd")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4attn", "cfg5", "cfg4tick", "prefill"],
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4attn", "cfg5", "cfg4tick", "prefill",
+                                           "linear"],
                     default="cfg2",
                     help="cfg4tick: per-tick kernel breakdown of config 4 (diagnostic table, no JSON line); "
                          "prefill: the prompt kernel on one config-4 layer")
@@ -997,6 +998,98 @@ def run_prefill(args):
                       "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
 
 
+def run_linear(args):
+    """--workload linear: the four linear layers of config-4 blocks on the fused
+    skinny-linear kernel K8 (wfd_linear: RMSNorm + QKV + RoPE, o_proj + residual,
+    RMSNorm + gate/up + SwiGLU, down + residual), --batch rows (default 8), eight
+    layers with their own weights per step (453 MB, larger than L2); value = weight
+    bytes streamed per second (HBM roofline).  The same chain on RMSNorm + cuBLAS +
+    the element-wise kernels is timed beside it (`unfused`)."""
+    import torch
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from wavefront_decoding_b200 import fused
+    from wavefront_decoding_b200 import runtime as rt
+    from wavefront_decoding_b200.looped_lm import CONFIG4 as cfg
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, d, dff, H, Dh, layers = args.batch or 8, cfg.d_model, cfg.d_ff, cfg.n_heads, cfg.head_dim, 8
+    g = torch.Generator(device=dev).manual_seed(CFG4["model_seed"])
+
+    def w(*shape):
+        return (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+    ones = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    W = [dict(qkv=w(d, 3 * H * Dh), o=w(H * Dh, d), gu=w(d, 2 * dff), dn=w(dff, d)) for _ in range(layers)]
+    for blk in W:
+        blk["qkv_f"] = fused.fold_norm(blk["qkv"], ones)
+        blk["gu_f"] = fused.interleave_gate_up(fused.fold_norm(blk["gu"], ones))
+    S = 4096
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, Dh, 2, dtype=torch.float64) / Dh))
+    ang = torch.outer(torch.arange(S, dtype=torch.float64), inv)
+    cos, sin = ang.cos().float().to(dev), ang.sin().float().to(dev)
+    x = torch.randn((n, d), generator=g, device=dev).to(torch.bfloat16)
+    attn = torch.randn((n, H * Dh), generator=g, device=dev).to(torch.bfloat16)
+    pos = torch.randint(0, S, (n,), generator=g, device=dev, dtype=torch.int32)
+    rt.error_word(dev)
+
+    def fused_step():
+        for blk in W:
+            fused.linear_rope(x, blk["qkv_f"], cos, sin, H, H, Dh, pos=pos, norm_eps=cfg.norm_eps)
+            fused.linear_residual(attn, blk["o"], x)
+            a = fused.linear_swiglu(x, blk["gu_f"], norm_eps=cfg.norm_eps)
+            fused.linear_residual(a, blk["dn"], x)
+
+    def unfused_step():
+        for blk in W:
+            h = fused.rmsnorm(x, ones, cfg.norm_eps)
+            fused.rope_split(h @ blk["qkv"], cos, sin, H, H, Dh, pos=pos)
+            x.addmm_(attn, blk["o"])
+            a = fused.silu_mul(fused.rmsnorm(x, ones, cfg.norm_eps) @ blk["gu"])
+            x.addmm_(a, blk["dn"])
+
+    def timed(step):
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(gr, stream=st):
+                step()
+        torch.cuda.current_stream().wait_stream(st)
+        gr.replay()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clk:
+            ev0.record()
+            for _ in range(args.steps):
+                gr.replay()
+            ev1.record()
+            torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) / args.steps, clk.summary()
+
+    ms, clocks = timed(fused_step)
+    ms_unfused, _ = timed(unfused_step)
+    rt.read_device_error(dev)
+    wbytes = sum(t.numel() * 2 for blk in W for t in (blk["qkv"], blk["o"], blk["gu"], blk["dn"]))
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    print(json.dumps({"metric": "fused linear layers: weight bytes streamed (config-4 blocks)", "value": gbs,
+                      "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                      "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": "linear_fused_cfg4_blocks", "rows": n, "layers": layers,
+                                 "launches_per_layer": 4, "weights_mb": wbytes / 1e6},
+                      "unfused": {"ms_per_step": ms_unfused, "launches_per_layer": 8,
+                                  "what": "RMSNorm + cuBLAS GEMM + RoPE split / SwiGLU kernels"},
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                                   "peak_kind": peak_kind},
+                      "gpu_launches": 4 * layers * args.steps, "clocks": clocks}), flush=True)
+
+
 def run_tick_profile(args):
     """--workload cfg4tick: per-tick kernel breakdown of greedy wavefront decoding
     on the device scheduler (diagnostic; prints a table, no JSON line).  Runs
@@ -1093,6 +1186,8 @@ def main():
         run_tick_profile(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "linear":
+        run_linear(args)
     else:
         run_wfd(args)
 
