@@ -60,3 +60,33 @@ def test_product_does_not_import_oracle():
     for p in pkg.rglob("*.py"):
         src = p.read_text()
         assert "oracle" not in re.findall(r"^\s*(?:from|import)\s+(\w+)", src, flags=re.M), p
+
+
+def test_linear_rejects_bad_arguments_on_the_host(lib):
+    """wfd_linear's argument checks run before any device work: bad shapes, modes and
+    missing pointers come back as WFD_ERR_INVALID_ARG (no GPU needed), and an empty
+    call is a no-op."""
+    from wavefront_decoding_b200 import _abi
+
+    def call(**kw):
+        p = _abi.wfd_linear_params()
+        p.x, p.w, p.out, p.err = 16, 32, 48, 64   # never dereferenced: the checks below fail first
+        p.n_rows, p.K, p.F, p.ldx, p.ldo = 4, 256, 256, 256, 256
+        p.mode = _abi.WFD_LINEAR_PLAIN
+        for k, v in kw.items():
+            setattr(p, k, v)
+        return lib.wfd_linear(ctypes.byref(p), None)
+
+    INVALID = 1
+    assert lib.wfd_linear(None, None) == INVALID
+    assert call(n_rows=-1) == INVALID
+    assert call(K=100) == INVALID                 # K % 8
+    assert call(F=0) == INVALID
+    assert call(ldx=128) == INVALID               # ldx < K
+    assert call(mode=7) == INVALID
+    assert call(n_rows=0) == 0                    # nothing to do
+    assert call(x=None) == INVALID
+    assert call(mode=_abi.WFD_LINEAR_ROPE, Dh=64, H=0, Hkv=1) == INVALID
+    assert call(mode=_abi.WFD_LINEAR_ROPE, Dh=64, H=1, Hkv=1, F=256, q=16, k=16, v=16,
+                cos_tab=16, sin_tab=16, max_pos=8, pos_period=0) == INVALID   # neither pos nor a period
+    assert call(mode=_abi.WFD_LINEAR_SWIGLU, F=192, ldo=96) == INVALID          # F % 128
