@@ -35,8 +35,9 @@
 // griddep_wait(), so the weights stream while the previous kernel finishes;
 // X (the MMAs' B operand, also the row norms' input) and every output are
 // touched only after it.
-// Every mbarrier wait is bounded; the two cluster barriers are reached by every
-// thread of every CTA whatever happens.  No multicast.
+// Every mbarrier wait is bounded; the cluster barrier is reached by every thread
+// of every CTA whatever happens (a thread-block cluster's CTAs are resident
+// together, so a peer's shared memory exists from the start).  No multicast.
 #pragma once
 
 #include <cuda.h>
