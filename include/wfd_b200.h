@@ -37,8 +37,9 @@ extern "C" {
 
 /* Raised whenever a declaration or a struct layout below changes incompatibly
  * (2: wfd_sched_params.depth_slots; 3: wfd_commit_window takes n_rows;
- * 4: wfd_sched_params.gap_windows; 5: wfd_linear). */
-#define WFD_ABI_VERSION 5
+ * 4: wfd_sched_params.gap_windows; 5: wfd_linear; 6: wfd_rope_split_norm,
+ * wfd_silu_mul_norm). */
+#define WFD_ABI_VERSION 6
 
 enum wfd_status {
   WFD_OK = 0,
@@ -300,6 +301,20 @@ int wfd_rope_split(const void* qkv, const float* cos_tab, const float* sin_tab, 
 /* SwiGLU gate: out (n, dff) = silu(g) * u where gu (n, 2 dff) = [g | u] per row
  * (dff % 8 == 0). */
 int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, int32_t dtype, void* stream);
+
+/* RMSNorm folded into the next linear layer.  With W' = diag(norm weight) W the
+ * projection of the normalised row is s_r * (x_r . W'), s_r = rsqrt(mean(x_r^2) +
+ * eps); the GEMM takes x itself and these variants apply s_r to its output:
+ * wfd_rope_split_norm is wfd_rope_split of s_r * qkv_r (v included);
+ * wfd_silu_mul_norm is out = silu(s_r g) * (s_r u).  x: (n, d) with row stride ldx
+ * elements, the rows the GEMM read (d % 8 == 0, ldx % 8 == 0, 16-byte aligned).  Each
+ * row is processed independently of the others. */
+int wfd_rope_split_norm(const void* qkv, const void* x, int32_t ldx, int32_t d, float eps, const float* cos_tab,
+                        const float* sin_tab, const int32_t* pos, int32_t pos_stride, int32_t pos_period,
+                        int32_t max_pos, void* q, void* k, void* v, int32_t n, int32_t n_heads, int32_t n_kv_heads,
+                        int32_t head_dim, int32_t style, int32_t dtype, int32_t* d_err, void* stream);
+int wfd_silu_mul_norm(const void* gu, const void* x, int32_t ldx, int32_t d, float eps, void* out, int32_t n,
+                      int32_t dff, int32_t dtype, void* stream);
 
 /* Linear layer of a few rows on the tensor cores with the block's element-wise
  * work fused in (bf16; fp32 accumulation).  y = s_r * x_r . W for W (K, F)

@@ -42,7 +42,7 @@ def test_python_binding_covers_header(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.wfd_abi_version() == 5
+    assert lib.wfd_abi_version() == 6
     assert lib.wfd_status_string(0) == b"ok"
     assert b"workspace" in lib.wfd_status_string(3)
 

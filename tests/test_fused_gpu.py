@@ -142,3 +142,74 @@ def test_items_from_table_and_argmax(cuda_dev):
                 out = torch.empty(5, dtype=torch.int32, device=cuda_dev)
                 fused.argmax_rows(x, out)
                 assert torch.equal(out.long(), x.float().argmax(dim=-1)), (dt, V, x.data_ptr() % 16)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n", [1, 7, 64, 300])
+@pytest.mark.parametrize("interleaved", [False, True])
+def test_rope_split_with_folded_norm(cuda_dev, dt, n, interleaved):
+    """wfd_rope_split_norm: rope_split of s_r * qkv_r, s_r = rsqrt(mean(x_r^2) + eps)
+    from the pre-norm rows x (a strided view), against fp32 torch."""
+    from wavefront_decoding_b200 import fused
+    g = gi.gen(33)
+    H, Hkv, Dh, d, S = 8, 4, 64, 512, 300
+    qkv = torch.randn((n, (H + 2 * Hkv) * Dh), generator=g).to(dt).to(cuda_dev)
+    xbig = (torch.randn((n, d + 64), generator=g) * 3).to(dt).to(cuda_dev)
+    x = xbig[:, :d]                                   # row stride d + 64
+    inv = 1.0 / (10000.0 ** (torch.arange(0, Dh, 2, dtype=torch.float64) / Dh))
+    ang = torch.outer(torch.arange(S, dtype=torch.float64), inv)
+    cos, sin = ang.cos().float().to(cuda_dev), ang.sin().float().to(cuda_dev)
+    pos = torch.randint(0, S, (n,), generator=g, dtype=torch.int32).to(cuda_dev)
+    q, k, v = fused.rope_split(qkv, cos, sin, H, Hkv, Dh, pos=pos, interleaved=interleaved, norm_x=x,
+                               norm_eps=1e-6)
+    xf = x.float()
+    sc = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)
+    y = qkv.float() * sc
+    pl = pos.long()
+    tol = _tol(dt) * 4
+    ref_q = _rope_ref(y[:, :H * Dh].view(n, H, Dh), pl, cos, sin, interleaved)
+    ref_k = _rope_ref(y[:, H * Dh:(H + Hkv) * Dh].view(n, Hkv, Dh), pl, cos, sin, interleaved)
+    ref_v = y[:, (H + Hkv) * Dh:].view(n, Hkv, Dh)
+    for got, ref in ((q, ref_q), (k, ref_k), (v, ref_v)):
+        assert (got.float() - ref).abs().max().item() <= tol * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n", [1, 9, 300])
+def test_silu_mul_with_folded_norm(cuda_dev, dt, n):
+    from wavefront_decoding_b200 import fused
+    g = gi.gen(34)
+    dff, d = 1536, 512
+    gu = torch.randn((n, 2 * dff), generator=g).to(dt).to(cuda_dev)
+    x = (torch.randn((n, d), generator=g) * 2).to(dt).to(cuda_dev)
+    out = fused.silu_mul(gu, norm_x=x, norm_eps=1e-6)
+    sc = torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+    gg, uu = gu.float()[:, :dff] * sc, gu.float()[:, dff:] * sc
+    ref = torch.nn.functional.silu(gg) * uu
+    assert (out.float() - ref).abs().max().item() <= _tol(dt) * 4 * max(1.0, ref.abs().max().item())
+
+
+def test_folded_norm_model_matches_explicit_norm(cuda_dev):
+    """The bf16 looped LM with folded norms against the same model with explicit
+    RMSNorm launches: q / k / v and the block output agree within bf16 rounding."""
+    from wavefront_decoding_b200.looped_lm import LoopedLM, LoopedLMConfig
+    cfg = LoopedLMConfig(vocab=512, d_model=256, n_heads=4, n_kv_heads=2, head_dim=64, d_ff=512, n_prelude=1,
+                         n_core=2, n_coda=1, T_total=4)
+    m = LoopedLM(cfg, seed=3, dtype=torch.bfloat16, device="cuda")
+    assert m.fold_norms
+    m.rope_tables(64)
+    blk = m.core[0]
+    blk.norm1 = (torch.rand(cfg.d_model, generator=gi.gen(35)) + 0.5).to(torch.bfloat16).to(cuda_dev)
+    blk.norm2 = (torch.rand(cfg.d_model, generator=gi.gen(36)) + 0.5).to(torch.bfloat16).to(cuda_dev)
+    m._fold()
+    x = torch.randn((10, cfg.d_model), generator=gi.gen(37)).to(torch.bfloat16).to(cuda_dev)
+    pos = torch.arange(10, dtype=torch.int32, device=cuda_dev) * 3
+    folded = m.qkv(blk, x, pos=pos)
+    attn = torch.randn((10, cfg.n_heads, cfg.head_dim), generator=gi.gen(38)).to(torch.bfloat16).to(cuda_dev)
+    out_f = m.finish_block(blk, x.clone(), attn)
+    m.fold_norms = False
+    explicit = m.qkv(blk, x, pos=pos)
+    out_e = m.finish_block(blk, x.clone(), attn)
+    for a, b in zip(folded, explicit):
+        assert (a.float() - b.float()).abs().max().item() <= 3e-2 * max(1.0, b.float().abs().max().item())
+    assert (out_f.float() - out_e.float()).abs().max().item() <= 3e-2 * max(1.0, out_e.float().abs().max().item())

@@ -28,7 +28,7 @@ EXPORTED = (
     "wfd_items_from_table", "wfd_argmax_rows",
     "wfd_sched_pre_tick", "wfd_sched_route", "wfd_sched_settle", "wfd_sched_params_bytes",
     "wfd_set_batch_invariant", "wfd_get_batch_invariant", "wfd_test_fail_waits",
-    "wfd_linear", "wfd_linear_params_bytes",
+    "wfd_linear", "wfd_linear_params_bytes", "wfd_rope_split_norm", "wfd_silu_mul_norm",
 )
 
 WFD_LINEAR_PLAIN, WFD_LINEAR_RESIDUAL, WFD_LINEAR_SWIGLU, WFD_LINEAR_ROPE = 0, 1, 2, 3
@@ -47,7 +47,7 @@ class wfd_item(ctypes.Structure):
                 ("q_len", ctypes.c_int32), ("q_row0", ctypes.c_int32)]
 
 
-ABI_VERSION = 5  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
+ABI_VERSION = 6  # include/wfd_b200.h: WFD_ABI_VERSION (declarations and struct layouts below)
 
 
 class wfd_sched_params(ctypes.Structure):
@@ -114,6 +114,11 @@ _SIGS = {
     "wfd_rope_split": ([_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P], _I),
     # gu out n dff dtype stream
     "wfd_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
+    # qkv x ldx d eps cos sin pos pos_stride pos_period max_pos q k v n H Hkv Dh style dtype err stream
+    "wfd_rope_split_norm": ([_P, _P, _I, _I, _F, _P, _P, _P, _I, _I, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P],
+                            _I),
+    # gu x ldx d eps out n dff dtype stream
+    "wfd_silu_mul_norm": ([_P, _P, _I, _I, _F, _P, _I, _I, _I, _P], _I),
     # a b idx stride out n d n_src dtype err stream
     "wfd_gather_rows": ([_P, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P], _I),
     # src idx stride dst zero n d n_dst dtype err stream

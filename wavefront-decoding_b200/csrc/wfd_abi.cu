@@ -952,6 +952,77 @@ extern "C" int wfd_rope_split(const void* qkv, const float* cos_tab, const float
   return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
 }
 
+namespace {
+// (rows, chunks per row) of a row-scaled kernel: about two CTAs per SM, at least
+// one element group per thread of a chunk
+dim3 norm_grid(int n, long long per_row_groups) {
+  const int sms = current_sms() > 0 ? current_sms() : 148;
+  long long gy = (2ll * sms + n - 1) / n;
+  const long long cap = (per_row_groups + kNormThreads - 1) / kNormThreads;
+  if (gy > cap) gy = cap;
+  if (gy < 1) gy = 1;
+  if (gy > 65535) gy = 65535;
+  return dim3((unsigned)n, (unsigned)gy);
+}
+bool norm_args_ok(const void* x, int32_t ldx, int32_t d, float eps) {
+  return x && d > 0 && d % 8 == 0 && ldx >= d && ldx % 8 == 0 && eps >= 0.f && aligned16(x);
+}
+}  // namespace
+
+extern "C" int wfd_rope_split_norm(const void* qkv, const void* x, int32_t ldx, int32_t d, float eps,
+                                   const float* cos_tab, const float* sin_tab, const int32_t* pos, int32_t pos_stride,
+                                   int32_t pos_period, int32_t max_pos, void* q, void* k, void* v, int32_t n,
+                                   int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t style, int32_t dtype,
+                                   int32_t* d_err, void* stream) {
+  if (n < 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 2 != 0 || max_pos <= 0)
+    return WFD_ERR_INVALID_ARG;
+  if (style != 0 && style != 1) return WFD_ERR_INVALID_ARG;
+  if (!pos && pos_period <= 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!qkv || !cos_tab || !sin_tab || !q || !k || !v || !d_err) return WFD_ERR_INVALID_ARG;
+  if (!norm_args_ok(x, ldx, d, eps)) return x && !aligned16(x) ? WFD_ERR_ALIGNMENT : WFD_ERR_INVALID_ARG;
+  const dim3 grid = norm_grid(n, (long long)(n_heads + 2 * n_kv_heads) * (head_dim / 2));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == WFD_DTYPE_BF16) {
+    if (launch_pdl(rope_split_norm_kernel<__nv_bfloat16>, grid, dim3(kNormThreads), 0, st,
+                   static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(x), ldx, d, eps, cos_tab,
+                   sin_tab, pos, pos_stride, pos_period, static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k),
+                   static_cast<__nv_bfloat16*>(v), n_heads, n_kv_heads, head_dim, style, max_pos, d_err) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else if (dtype == WFD_DTYPE_F32) {
+    if (launch_pdl(rope_split_norm_kernel<float>, grid, dim3(kNormThreads), 0, st, static_cast<const float*>(qkv),
+                   static_cast<const float*>(x), ldx, d, eps, cos_tab, sin_tab, pos, pos_stride, pos_period,
+                   static_cast<float*>(q), static_cast<float*>(k), static_cast<float*>(v), n_heads, n_kv_heads,
+                   head_dim, style, max_pos, d_err) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else
+    return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
+extern "C" int wfd_silu_mul_norm(const void* gu, const void* x, int32_t ldx, int32_t d, float eps, void* out,
+                                 int32_t n, int32_t dff, int32_t dtype, void* stream) {
+  if (n < 0 || dff <= 0 || dff % 8 != 0) return WFD_ERR_INVALID_ARG;
+  if (n == 0) return WFD_OK;
+  if (!gu || !out) return WFD_ERR_INVALID_ARG;
+  if (!aligned16(gu) || !aligned16(out)) return WFD_ERR_ALIGNMENT;
+  if (!norm_args_ok(x, ldx, d, eps)) return x && !aligned16(x) ? WFD_ERR_ALIGNMENT : WFD_ERR_INVALID_ARG;
+  const dim3 grid = norm_grid(n, dff / 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == WFD_DTYPE_BF16) {
+    if (launch_pdl(silu_mul_norm_kernel<__nv_bfloat16>, grid, dim3(kNormThreads), 0, st,
+                   static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(x), ldx, d, eps,
+                   static_cast<__nv_bfloat16*>(out), dff) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else if (dtype == WFD_DTYPE_F32) {
+    if (launch_pdl(silu_mul_norm_kernel<float>, grid, dim3(kNormThreads), 0, st, static_cast<const float*>(gu),
+                   static_cast<const float*>(x), ldx, d, eps, static_cast<float*>(out), dff) != cudaSuccess)
+      return WFD_ERR_CUDA;
+  } else
+    return WFD_ERR_UNSUPPORTED;
+  return cudaGetLastError() == cudaSuccess ? WFD_OK : WFD_ERR_CUDA;
+}
+
 extern "C" int wfd_silu_mul(const void* gu, void* out, int32_t n, int32_t dff, int32_t dtype, void* stream) {
   if (n < 0 || dff <= 0 || dff % 8 != 0) return WFD_ERR_INVALID_ARG;
   if (n == 0) return WFD_OK;

@@ -153,6 +153,106 @@ __global__ void __launch_bounds__(kModelThreads) silu_mul_kernel(const T* __rest
   }
 }
 
+// ---------------------------------------------------------------------------
+// RMSNorm folded into the next linear layer: with W' = diag(norm weight) W, the
+// layer's output for row r is s_r * (x_r . W') with s_r = rsqrt(mean(x_r^2) + eps),
+// so the GEMM takes x itself and the scale rides on the kernel after it.  These
+// variants of the RoPE split and the SwiGLU gate compute s_r from x (one CTA per
+// row and chunk of the row; every CTA of a row sums x_r^2 in the same order) and
+// apply it to the GEMM output before their own arithmetic.  Each row is
+// processed independently of the others.
+// ---------------------------------------------------------------------------
+constexpr int kNormThreads = 256;
+
+// s_r for row `row` of x (d elements, d % 8 == 0), for every thread of the CTA
+template <typename T>
+__device__ __forceinline__ float row_scale(const T* __restrict__ x, long long ldx, int row, int d, float eps) {
+  __shared__ float s_part[kNormThreads / 32];
+  const T* xr = x + (long long)row * ldx;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 8; c < d; c += kNormThreads * 8) {
+    float v[8];
+    Vec8<T>::load(xr + c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += s_part[w];
+  return rsqrtf(tot / (float)d + eps);
+}
+
+// rope_split_kernel with the row scale: CTA (row, chunk) handles element pairs
+// [chunk * per, (chunk + 1) * per) of the row; v is s_r * its GEMM output.
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
+    rope_split_norm_kernel(const T* __restrict__ qkv, const T* __restrict__ x, int ldx, int d, float eps,
+                           const float* __restrict__ cosb, const float* __restrict__ sinb,
+                           const int32_t* __restrict__ pos, int pos_stride, int pos_period, T* __restrict__ q,
+                           T* __restrict__ k, T* __restrict__ v, int H, int Hkv, int Dh, int style, int max_pos,
+                           int* err) {
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
+  const int r = blockIdx.x;
+  const float sc = row_scale(x, ldx, r, d, eps);
+  const int half = Dh >> 1;
+  const int heads = H + 2 * Hkv;
+  const int per_row = heads * half;
+  const int per = (per_row + gridDim.y - 1) / gridDim.y;
+  const int e0 = blockIdx.y * per, e1 = min(per_row, e0 + per);
+  int ps = pos ? pos[(long long)r * pos_stride] : (r % pos_period);
+  if (ps < 0 || ps >= max_pos) {
+    if (threadIdx.x == 0 && blockIdx.y == 0) set_error(err, kErrBadPos);
+    ps = 0;
+  }
+  const T* src_row = qkv + (long long)r * heads * Dh;
+  for (int e = e0 + threadIdx.x; e < e1; e += kNormThreads) {
+    const int hh = e / half, i = e - hh * half;
+    const T* src = src_row + (long long)hh * Dh;
+    const int i0 = style ? 2 * i : i, i1 = style ? 2 * i + 1 : i + half;
+    const float a = to_f(src[i0]) * sc, b = to_f(src[i1]) * sc;
+    if (hh >= H + Hkv) {
+      T* dst = v + ((long long)r * Hkv + (hh - H - Hkv)) * Dh;
+      dst[i0] = from_f<T>(a);
+      dst[i1] = from_f<T>(b);
+      continue;
+    }
+    const float c = cosb[(long long)ps * half + i], s = sinb[(long long)ps * half + i];
+    T* dst = hh < H ? q + ((long long)r * H + hh) * Dh : k + ((long long)r * Hkv + (hh - H)) * Dh;
+    dst[i0] = from_f<T>(a * c - b * s);
+    dst[i1] = from_f<T>(b * c + a * s);
+  }
+}
+
+// silu_mul_kernel with the row scale: out = silu(s_r g) * (s_r u), CTA (row, chunk)
+// handles 8-element vectors [chunk * per, (chunk + 1) * per) of the row.
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
+    silu_mul_norm_kernel(const T* __restrict__ gu, const T* __restrict__ x, int ldx, int d, float eps,
+                         T* __restrict__ out, int dff) {
+  griddep_wait();  // launched with programmatic stream serialization (no early trigger)
+  const int r = blockIdx.x;
+  const float sc = row_scale(x, ldx, r, d, eps);
+  const int vpr = dff / 8;
+  const int per = (vpr + gridDim.y - 1) / gridDim.y;
+  const int v0 = blockIdx.y * per, v1 = min(vpr, v0 + per);
+  for (int vi = v0 + threadIdx.x; vi < v1; vi += kNormThreads) {
+    const int c = vi * 8;
+    float g[8], u[8];
+    Vec8<T>::load(gu + (long long)r * 2 * dff + c, g);
+    Vec8<T>::load(gu + (long long)r * 2 * dff + dff + c, u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float gs = g[i] * sc;
+      g[i] = gs / (1.f + expf(-gs)) * (u[i] * sc);
+    }
+    Vec8<T>::store(out + (long long)r * dff + c, g);
+  }
+}
+
 }  // namespace wfd
 
 namespace wfd {

@@ -132,7 +132,11 @@ class WaveEngine:
         # plan (with the window append), attention (tcgen05 or CUDA-core), SwiGLU
         # gate.  Per body: P gather + item table + scatter, R gather + item table +
         # scatter, C gather + item table + final RMSNorm + greedy argmax.
-        self._launches = {"P": 3 + 6 * cfg.n_prelude, "R": 3 + 6 * cfg.n_core, "C": 4 + 6 * cfg.n_coda}
+        # With the norms folded into the next layer (bf16) the two RMSNorm launches of
+        # a layer and the final RMSNorm of the C body are gone.
+        per_layer = 4 if model.fold_norms else 6
+        self._launches = {"P": 3 + per_layer * cfg.n_prelude, "R": 3 + per_layer * cfg.n_core,
+                          "C": (3 if model.fold_norms else 4) + per_layer * cfg.n_coda}
         self._layers = {"P": cfg.n_prelude, "R": cfg.n_core, "C": cfg.n_coda}
         # rows per R attention window: 1 without KV sharing; with sharing a run of
         # one sequence's tokens on one depth slot (at most T_total + 2 tokens live)

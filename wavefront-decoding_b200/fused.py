@@ -30,12 +30,22 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
     return out
 
 
+def _norm_rows(norm_x: torch.Tensor, n: int):
+    """(pointer, row stride, width) of the pre-norm rows x of a folded RMSNorm."""
+    if norm_x.dim() != 2 or norm_x.shape[0] != n or norm_x.stride(1) != 1:
+        raise ValueError(f"norm_x must be ({n}, d) rows with unit column stride, got {tuple(norm_x.shape)}")
+    return norm_x.data_ptr(), norm_x.stride(0), norm_x.shape[1]
+
+
 def rope_split(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads: int, n_kv_heads: int, head_dim: int,
-               *, pos: torch.Tensor | None = None, pos_period: int = 0, interleaved: bool = False):
+               *, pos: torch.Tensor | None = None, pos_period: int = 0, interleaved: bool = False,
+               norm_x: torch.Tensor | None = None, norm_eps: float = 0.0):
     """qkv (n, (H + 2 Hkv) Dh) -> q (n, H, Dh), k (n, Hkv, Dh) rotated, v (n, Hkv, Dh).
 
     pos: int32 positions, one per row (a strided column view is fine), or None
-    with pos_period = L for rows that are L consecutive positions per sequence."""
+    with pos_period = L for rows that are L consecutive positions per sequence.
+    norm_x: the rows x the QKV GEMM read when an RMSNorm is folded into its weight
+    (fold_norm): every row of qkv is first scaled by rsqrt(mean(x^2) + norm_eps)."""
     dev = rt.require_cuda(qkv, cos, sin)
     n = qkv.shape[0]
     if not qkv.is_contiguous():
@@ -51,6 +61,16 @@ def rope_split(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads:
     else:
         assert pos_period > 0
         pptr, pstride = None, 0
+    if norm_x is not None:
+        assert norm_x.dtype == qkv.dtype
+        xp, ldx, d = _norm_rows(norm_x, n)
+        st = _abi.load().wfd_rope_split_norm(qkv.data_ptr(), xp, ldx, d, float(norm_eps), cos.data_ptr(),
+                                             sin.data_ptr(), pptr, pstride, pos_period, cos.shape[0], q.data_ptr(),
+                                             k.data_ptr(), v.data_ptr(), n, n_heads, n_kv_heads, head_dim,
+                                             1 if interleaved else 0, rt.dtype_code(qkv.dtype),
+                                             rt.error_word(dev).data_ptr(), rt.stream_ptr(dev))
+        _abi.check(st, "wfd_rope_split_norm")
+        return q, k, v
     st = _abi.load().wfd_rope_split(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), pptr, pstride, pos_period,
                                     cos.shape[0], q.data_ptr(), k.data_ptr(), v.data_ptr(), n, n_heads, n_kv_heads,
                                     head_dim, 1 if interleaved else 0, rt.dtype_code(qkv.dtype),
@@ -59,14 +79,23 @@ def rope_split(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads:
     return q, k, v
 
 
-def silu_mul(gu: torch.Tensor) -> torch.Tensor:
-    """gu (..., 2 dff) = [g | u] -> silu(g) * u (..., dff)."""
+def silu_mul(gu: torch.Tensor, *, norm_x: torch.Tensor | None = None, norm_eps: float = 0.0) -> torch.Tensor:
+    """gu (..., 2 dff) = [g | u] -> silu(g) * u (..., dff).  norm_x: the rows the
+    gate/up GEMM read when an RMSNorm is folded into its weight (fold_norm): g and
+    u are first scaled by rsqrt(mean(x^2) + norm_eps) of their row."""
     dev = rt.require_cuda(gu)
     if not gu.is_contiguous():
         gu = gu.contiguous()
     dff = gu.shape[-1] // 2
     out = torch.empty((*gu.shape[:-1], dff), dtype=gu.dtype, device=dev)
     n = gu.numel() // (2 * dff) if dff else 0
+    if norm_x is not None:
+        assert norm_x.dtype == gu.dtype
+        xp, ldx, d = _norm_rows(norm_x, n)
+        st = _abi.load().wfd_silu_mul_norm(gu.data_ptr(), xp, ldx, d, float(norm_eps), out.data_ptr(), n, dff,
+                                           rt.dtype_code(gu.dtype), rt.stream_ptr(dev))
+        _abi.check(st, "wfd_silu_mul_norm")
+        return out
     st = _abi.load().wfd_silu_mul(gu.data_ptr(), out.data_ptr(), n, dff, rt.dtype_code(gu.dtype), rt.stream_ptr(dev))
     _abi.check(st, "wfd_silu_mul")
     return out

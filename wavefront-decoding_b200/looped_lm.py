@@ -118,6 +118,20 @@ class LoopedLM:
         self.lm_head = (torch.randn((d, cfg.vocab), generator=g) * (1.0 / math.sqrt(d))).to(dtype=dtype,
                                                                                            device=self.device)
         self._rope_cache = None
+        # bf16: every RMSNorm is folded into the linear layer after it (its weight
+        # multiplied into that layer's rows, its row scale applied by the kernel that
+        # follows the GEMM), one launch fewer per norm; fp32 keeps the explicit norm,
+        # the reference's own arithmetic
+        self.fold_norms = dtype == torch.bfloat16
+        self._fold()
+
+    def _fold(self) -> None:
+        if not self.fold_norms:
+            return
+        for blk in self.prelude + self.core + self.coda:
+            blk.wqkv_n = fused.fold_norm(blk.wqkv, blk.norm1)
+            blk.wgu_n = fused.fold_norm(blk.wgu, blk.norm2)
+        self.lm_head_n = fused.fold_norm(self.lm_head, self.final_norm)
 
     def load_weights(self, W: dict) -> "LoopedLM":
         """Replace every weight from a dict of tensors: embed (V, d), final_norm (d),
@@ -136,6 +150,7 @@ class LoopedLM:
             for blk, wb in zip(blocks, W[name]):
                 for k in ("norm1", "wqkv", "wo", "norm2", "wgu", "wd"):
                     setattr(blk, k, put(wb[k], getattr(blk, k)))
+        self._fold()
         return self
 
     # ------------------------------------------------------------------
@@ -159,11 +174,16 @@ class LoopedLM:
         Returns contiguous q (.., H, Dh), k / v (.., Hkv, Dh)."""
         cfg = self.cfg
         lead = x.shape[:-1]
-        h = self.rmsnorm(x, blk.norm1).reshape(-1, cfg.d_model)
-        qkv = h @ blk.wqkv
         cos, sin = self._rope_cache
-        q, k, v = fused.rope_split(qkv, cos, sin, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, pos=pos,
-                                   pos_period=pos_period, interleaved=cfg.rope_style == "interleaved")
+        if self.fold_norms:
+            x2 = x.reshape(-1, cfg.d_model)
+            q, k, v = fused.rope_split(x2 @ blk.wqkv_n, cos, sin, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, pos=pos,
+                                       pos_period=pos_period, interleaved=cfg.rope_style == "interleaved",
+                                       norm_x=x2, norm_eps=cfg.norm_eps)
+        else:
+            h = self.rmsnorm(x, blk.norm1).reshape(-1, cfg.d_model)
+            q, k, v = fused.rope_split(h @ blk.wqkv, cos, sin, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, pos=pos,
+                                       pos_period=pos_period, interleaved=cfg.rope_style == "interleaved")
         return (q.view(*lead, cfg.n_heads, cfg.head_dim), k.view(*lead, cfg.n_kv_heads, cfg.head_dim),
                 v.view(*lead, cfg.n_kv_heads, cfg.head_dim))
 
@@ -175,14 +195,21 @@ class LoopedLM:
         shp = x.shape
         x2 = x.view(-1, cfg.d_model)
         x2.addmm_(attn.reshape(-1, cfg.n_heads * cfg.head_dim), blk.wo)
-        a = fused.silu_mul(self.rmsnorm(x2, blk.norm2) @ blk.wgu)
+        if self.fold_norms:
+            a = fused.silu_mul(x2 @ blk.wgu_n, norm_x=x2, norm_eps=cfg.norm_eps)
+        else:
+            a = fused.silu_mul(self.rmsnorm(x2, blk.norm2) @ blk.wgu)
         return x2.addmm_(a, blk.wd).view(shp)
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         return (self.rmsnorm(x.contiguous(), self.final_norm) @ self.lm_head).float()
 
     def greedy_ids(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        """out (int32) = argmax of each row's logits (first maximum), without an fp32 copy."""
+        """out (int32) = argmax of each row's logits (first maximum), without an fp32 copy.
+        With folded norms the final RMSNorm's weight sits in lm_head_n and its row
+        scale, positive, leaves the argmax unchanged: it is not computed."""
+        if self.fold_norms:
+            return fused.argmax_rows(x.contiguous() @ self.lm_head_n, out)
         return fused.argmax_rows(self.rmsnorm(x.contiguous(), self.final_norm) @ self.lm_head, out)
 
     # ------------------------------------------------------------------
