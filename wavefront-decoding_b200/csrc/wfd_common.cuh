@@ -205,6 +205,13 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
   return r;
 }
 
+__device__ __forceinline__ int ld_relaxed_gpu(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 __device__ __forceinline__ float ld_cg_f32(const float* p) {
   float r;
   asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(r) : "l"(p));

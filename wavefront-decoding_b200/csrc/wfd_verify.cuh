@@ -836,6 +836,15 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         }
         softmax_bar<SMT>();
       }
+      // the CTAs whose shares hold keys of this unit; if the others have all
+      // published their partials by the time this CTA gets to the unit (the usual
+      // case for a CTA's last unit: the next CTA began with the rest of it), this
+      // CTA merges without publishing its own.  Read now, used after the tiles.
+      const int c_first = (int)(ustart / share);
+      const int c_last = (int)((ustart + S.k_len - 1) / share);
+      const int n_contrib = p.invariant ? 1 : c_last - c_first + 1;
+      int arrived = 0;
+      if (n_contrib > 1 && stid == 0) arrived = ld_relaxed_gpu(p.ws_cnt + c_first);
       // running column maxima live in shared memory (mst, log2-scaled), owned
       // by lanes 0..NL-1 of the first warp of each column slice
       if (sq == 0 && lane < NL) mst[col0 + lane] = NEG_INF;
@@ -1045,9 +1054,6 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
       softmax_bar<SMT>();
       auto lsum = [&](int n) { return lb[n] + lb[NQP + n] + lb[2 * NQP + n] + lb[3 * NQP + n]; };
 
-      const int c_first = (int)(ustart / share);
-      const int c_last = (int)((ustart + S.k_len - 1) / share);
-      const int n_contrib = p.invariant ? 1 : c_last - c_first + 1;
       const int dim = my_row;  // O^T TMEM lane == head dim (lanes >= DH hold nothing)
       const bool dim_ok = dim < DH;
       // output element of query column n held by this thread's O^T row, or -1
@@ -1074,24 +1080,33 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
           }
         }
       } else {
-        const int slot = (ustart < a) ? 2 * (int)blockIdx.x : 2 * (int)blockIdx.x + 1;
-        float* pb = p.ws_part + (size_t)slot * C::PART_FLOATS;
-        // every thread holds the same m[]; thread n publishes column n's (m, l);
-        // O^T only for the unit's query columns (the merge reads no others)
-        if (stid < NA) {
-          pb[stid] = mst[stid];
-          pb[NQP + stid] = lsum(stid);
-        }
-#pragma unroll
-        for (int j = 0; j < NL; ++j)
-          if (col0 + j < nvec && dim_ok) pb[2 * NQP + (col0 + j) * DH + dim] = oacc[j];
-        __threadfence();
-        softmax_bar<SMT>();
+        // 2: every other contributor had published when this CTA began the unit
+        // (relaxed read, made an acquire by the fence), so this CTA merges now
         if (stid == 0) {
-          const int prev = atomicAdd(p.ws_cnt + c_first, 1);
-          s_flag = (prev == n_contrib - 1) ? 1 : 0;
+          s_flag = (arrived == n_contrib - 1) ? 2 : 0;
+          if (s_flag == 2) fence_acq_rel_gpu();
         }
         softmax_bar<SMT>();
+        if (s_flag != 2) {
+          const int slot = (ustart < a) ? 2 * (int)blockIdx.x : 2 * (int)blockIdx.x + 1;
+          float* pb = p.ws_part + (size_t)slot * C::PART_FLOATS;
+          // every thread holds the same m[]; thread n publishes column n's (m, l);
+          // O^T only for the unit's query columns (the merge reads no others)
+          if (stid < NA) {
+            pb[stid] = mst[stid];
+            pb[NQP + stid] = lsum(stid);
+          }
+#pragma unroll
+          for (int j = 0; j < NL; ++j)
+            if (col0 + j < nvec && dim_ok) pb[2 * NQP + (col0 + j) * DH + dim] = oacc[j];
+          __threadfence();
+          softmax_bar<SMT>();
+          if (stid == 0) {
+            const int prev = atomicAdd(p.ws_cnt + c_first, 1);
+            s_flag = (prev == n_contrib - 1) ? 1 : 0;
+          }
+          softmax_bar<SMT>();
+        }
         if (s_flag && dim_ok) {
           __threadfence();
           // Online merge, this thread's columns in chunks of MCH, contributors in
