@@ -248,7 +248,9 @@ def decode_device_inputs(dev, c: dict, seed: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """Clocks / throttle reasons sampled during the timed region: the nvidia-smi
+    clocks line (every 20 ms) and, in-process, NVML every ~1 ms (a timed region of
+    a few ms would otherwise hold one sample or none)."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -257,14 +259,49 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
 
+    def _poll(self):
+        import pynvml
+        try:
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:
+            self._ready.set()
+            return
+        self._ready.set()
+        self._go.wait()  # NVML is up; samples only from the start of the timed region
+        try:
+            while not self._stop.is_set():
+                try:
+                    self.nvml_rows.append(dict(sm=float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                               max=mx, power=pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                               bits=int(get_reasons(h))))
+                except Exception:
+                    break
+                self._stop.wait(0.001)
+        finally:
+            try:
+                pynvml.nvmlShutdown()
+            except Exception:
+                pass
+
     def __enter__(self):
+        import threading
         self.first = []
+        self.nvml_rows = []
+        self._stop, self._ready, self._go = threading.Event(), threading.Event(), threading.Event()
+        self._thread = threading.Thread(target=self._poll, daemon=True)
+        self._thread.start()
+        self._ready.wait(timeout=10.0)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "20", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            self._go.set()
             return self
         # the timed region starts once sampling is live (nvidia-smi takes a
         # moment to print its first line)
@@ -272,9 +309,13 @@ class ClockSampler:
         r, _, _ = select.select([self.proc.stdout], [], [], 10.0)
         if r:
             self.first = [self.proc.stdout.readline()]
+        self._go.set()  # NVML samples from here on: the timed region starts next
         return self
 
     def __exit__(self, *exc):
+        self._stop.set()
+        self._go.set()
+        self._thread.join(timeout=5)
         self.lines = []
         if self.proc is not None:
             self.proc.terminate()
@@ -296,17 +337,25 @@ class ClockSampler:
                                  pcap=f[8]))
             except ValueError:
                 continue
-        if not rows:
-            return None
         reasons = set()
         for r in rows:
             for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
                               ("pcap", "sw_power_cap")):
                 if r[key].lower().startswith("active"):
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(r["sm"] for r in rows), "sm_max_mhz": max(r["max"] for r in rows),
-                "reasons": sorted(reasons), "samples": len(rows),
-                "power_w_max": max(r["power"] for r in rows)}
+        # NVML reason bits: sw power cap 0x4, hw slowdown 0x8, sw thermal 0x20, hw thermal 0x40
+        nv = getattr(self, "nvml_rows", [])
+        for r in nv:
+            for bit, name in ((0x4, "sw_power_cap"), (0x8, "hw_slowdown"), (0x20, "sw_thermal_slowdown"),
+                              (0x40, "hw_thermal_slowdown")):
+                if r["bits"] & bit:
+                    reasons.add(name)
+        allr = rows + nv
+        if not allr:
+            return None
+        return {"sm_mhz": statistics.median(r["sm"] for r in allr), "sm_max_mhz": max(r["max"] for r in allr),
+                "reasons": sorted(reasons), "samples": len(allr), "samples_nvidia_smi": len(rows),
+                "samples_nvml": len(nv), "power_w_max": max(r["power"] for r in allr)}
 
 
 def cpu_baseline(q, K, V, kn, vn, items, budget_s: float, warmup: int = 1, steps: int | None = None,
