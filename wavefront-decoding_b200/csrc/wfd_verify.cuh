@@ -54,10 +54,10 @@
 namespace wfd {
 
 constexpr int kVerifyMaxRows = 32;  // query vectors per unit (larger windows -> query groups)
-constexpr int kSelfPlanMax = 256;
+constexpr int kSelfPlanMax = 256;  // item tables up to this size are planned by the attention CTAs themselves
 #ifndef WFD_MMA_CHAINS
 #define WFD_MMA_CHAINS 2
-#endif   // item tables up to this size are planned by the attention CTAs themselves
+#endif
 constexpr int kTcTile = 128;        // keys per tile == MMA M
 // threads: TMA warp + MMA warp + 4 softmax warps per 16 query columns
 __host__ __device__ constexpr int tc_threads(int nqp) { return nqp == 32 ? 320 : 192; }
@@ -121,18 +121,20 @@ struct TcCfg {
   static constexpr int P_ATOM = 8 * P_ROWB;                // 8 key rows
   static constexpr int RED_FLOATS = 2 * 4 * NQP;           // double-buffered per-warp column values
   static constexpr int SMEM =
-      STAGES * KV_STAGE + GUARD + 2 * Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + (2 * NQP + 4) * 4 + 1024;
-  // Each accumulation (S^T of a tile, O^T of a tile) is split over CH
+      STAGES * KV_STAGE + GUARD + 2 * Q_BYTES + P_BYTES + 2 * RED_FLOATS * 4 + (3 * NQP + 4) * 4 + 1024;
+  // Each accumulation (S^T of a tile: CHS, O^T of a tile: CHO) is split over
   // independent TMEM accumulators (k-steps j with j % CH == c go to chain c,
   // summed by the softmax warps): consecutive MMAs into one accumulator wait
   // for each other, so CH chains keep CH MMAs in flight.
-  // With 32 columns the softmax warps bound the tile period and a second chain
-  // doubles their TMEM reads (config 3: 1829 vs 1912 us a step with one chain);
-  // with 16 columns the chains let the MMA warp keep two MMAs in flight.
-  static constexpr int CH = NQP == 32 ? 1 : WFD_MMA_CHAINS;
-  static constexpr int S_COL = 0;                          // S^T buffer sb, chain c: (sb * CH + c) * NQP
-  static constexpr int O_COL = 2 * CH * NQP;               // O^T chain c: O_COL + c * NQP
-  static constexpr int TMEM_USED = 3 * CH * NQP;
+  // With 32 columns the softmax warps bound the tile period: a second S chain
+  // doubles their TMEM reads (config 3: 1829 vs 1912 us a step with one chain)
+  // and a second O chain measured 1.6 % slower; with 16 columns the chains let
+  // the MMA warp keep two MMAs in flight.
+  static constexpr int CHS = NQP == 32 ? 1 : WFD_MMA_CHAINS;
+  static constexpr int CHO = NQP == 32 ? 1 : WFD_MMA_CHAINS;
+  static constexpr int S_COL = 0;                          // S^T buffer sb, chain c: (sb * CHS + c) * NQP
+  static constexpr int O_COL = 2 * CHS * NQP;              // O^T chain c: O_COL + c * NQP
+  static constexpr int TMEM_USED = (2 * CHS + CHO) * NQP;
   static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128 : 256;
   static constexpr int PART_FLOATS = NQP * (DH + 2);
   static_assert(NQP == 16 || NQP == 32, "N of the swap-AB MMA");
@@ -236,9 +238,16 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float (&v)[32]) {
 // their control flow (same loop trips, same named barriers) but issue no more
 // TMA or MMA work, so nothing in the CTA can block without a bound.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
-  bool ok = false;
-  if (!*abort_flag) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  // The first probe (non-blocking, so an aborted role never suspends on it) and
+  // the abort flag's load are independent: a wait whose phase has completed
+  // costs one shared-memory round trip, not two.  These waits sit on the tile
+  // loops' critical paths (config 3: 1622 -> 1577 us a step).
+  bool ok = mbar_test_wait(bar, parity);
+  const bool aborted = *abort_flag;
+  if (aborted) {
+    ok = false;
+  } else if (!ok) {
+    for (uint32_t i = 1; i < kSpinLimit; ++i) {
       if (mbar_try_wait(bar, parity)) {
         ok = true;
         break;
@@ -282,11 +291,22 @@ __device__ __forceinline__ float warp_col_reduce(float (&w)[N], int lane) {
   return r;
 }
 
+// Maximum of v over the 32 lanes of the warp, in every lane (the f32 form of
+// redux.sync is sm_100a).  NaN inputs are ignored, as by fmaxf.
+__device__ __forceinline__ float warp_max_f32(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
 template <int N>
 __device__ __forceinline__ int reduced_col(int lane) {
   constexpr int LOGN = N == 1 ? 0 : N == 2 ? 1 : N == 4 ? 2 : N == 8 ? 3 : N == 16 ? 4 : 5;
-  if (LOGN == 0) return 0;
-  return (int)(__brev((unsigned)(lane & (N - 1))) >> (32 - LOGN));
+  if constexpr (LOGN == 0) {
+    return 0;
+  } else {
+    return (int)(__brev((unsigned)(lane & (N - 1))) >> (32 - LOGN));
+  }
 }
 
 // Segment i of a slot-mode item table exactly as the plan kernel builds it
@@ -400,7 +420,8 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
   float* lred = red + C::RED_FLOATS;                       // [2][4][NQP] column sums
   float* mst = lred + C::RED_FLOATS;                       // [NQP] running column max (log2-scaled)
   float* ast = mst + NQP;                                  // [NQP] this tile's rescale factors
-  int* rflag = reinterpret_cast<int*>(ast + NQP);          // [H2] any factor != 1 this tile
+  float* msf = ast + NQP;                                  // [NQP] mst with -inf as 0 (exp2 of masked scores)
+  int* rflag = reinterpret_cast<int*>(msf + NQP);          // [H2] any factor != 1 this tile
 
   __shared__ __align__(8) uint64_t bar_full[STAGES];
   __shared__ __align__(8) uint64_t bar_empty[STAGES];
@@ -758,8 +779,8 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
               // K step j: dims 16j..16j+15 = box j/4, byte 32*(j%4) inside the 128B row
               const uint32_t koff = (uint32_t)((j >> 2) * C::BOX_BYTES + (j & 3) * 32);
               const uint32_t qoff = (uint32_t)((j >> 2) * (NQP * 128) + (j & 3) * 32);
-              umma_f16(tmem + (uint32_t)((sb * C::CH + j % C::CH) * NQP), umma_desc(k_addr + koff, 16, 1024, 2),
-                       umma_desc(qa + qoff, 16, 1024, 2), IDESC_S, j >= C::CH ? 1u : 0u);
+              umma_f16(tmem + (uint32_t)((sb * C::CHS + j % C::CHS) * NQP), umma_desc(k_addr + koff, 16, 1024, 2),
+                       umma_desc(qa + qoff, 16, 1024, 2), IDESC_S, j >= C::CHS ? 1u : 0u);
             }
             umma_commit(&bar_sfull[sb]);
             if (t == n_t - 1) umma_commit(&bar_qfree[qb]);  // the unit's Q^T buffer may be rewritten
@@ -777,9 +798,9 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               // K step j: keys 16j..16j+15 = two 8-row groups of both V boxes / of P^T
-              umma_f16(tmem + (uint32_t)(C::O_COL + (j % C::CH) * NQP), umma_desc(v_addr + j * 2048, C::BOX_BYTES, 1024, 2),
+              umma_f16(tmem + (uint32_t)(C::O_COL + (j % C::CHO) * NQP), umma_desc(v_addr + j * 2048, C::BOX_BYTES, 1024, 2),
                        umma_desc(p_addr + j * 2 * C::P_ATOM, 16, C::P_ATOM, C::P_LAYOUT), IDESC_PV,
-                       j >= C::CH ? 1u : 0u);
+                       j >= C::CHO ? 1u : 0u);
             }
             umma_commit(&bar_ofull);
             umma_commit(&bar_empty[stage]);
@@ -861,10 +882,10 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         tc_wait(&bar_sfull[sb], (ti >> 1) & 1u, &s_abort, p.err);
         tc_fence_after();
         float s[LW];
-        tmem_ld<LW>(tq + (uint32_t)(sb * C::CH * NQP + col0), s);
-        if constexpr (C::CH == 2) {
+        tmem_ld<LW>(tq + (uint32_t)(sb * C::CHS * NQP + col0), s);
+        if constexpr (C::CHS == 2) {
           float s1[LW];
-          tmem_ld<LW>(tq + (uint32_t)((sb * C::CH + 1) * NQP + col0), s1);
+          tmem_ld<LW>(tq + (uint32_t)((sb * C::CHS + 1) * NQP + col0), s1);
           tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < LW; ++j) s[j] += s1[j];
@@ -880,7 +901,15 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         const bool kvalid = key < r_hi;
         const int thr = p.causal ? (key - (S.k_len - S.q_len)) * p.G - qg * NQP : -(1 << 30);
         const int nlim = kvalid ? nvec : 0;
-        if (p.row_pos != nullptr && p.causal) {
+        // a tile whose keys all lie in the unit and below the causal frontier of
+        // the window's first row, for real query columns only, masks nothing
+        // (warp-uniform)
+        const int tile_last = r_lo + t * kTcTile + kTcTile - 1;
+        const bool interior = tile_last < r_hi && col0 + NL <= nvec && p.row_pos == nullptr &&
+                              (!p.causal || tile_last <= S.k_len - S.q_len);
+        if (interior) {
+          // every score stands
+        } else if (p.row_pos != nullptr && p.causal) {
 #pragma unroll
           for (int j = 0; j < NL; ++j) {
             const int n = col0 + j;
@@ -894,14 +923,23 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
             s[j] = (n < nlim && vn >= thr) ? s[j] : NEG_INF;    // raw (unscaled) scores
           }
         }
-        // column maxima over the tile's 128 keys
+        // column maxima over the tile's 128 keys: this warp's 32 by redux, the
+        // quadrants' by the column owner below
         float* rb = red + (ti & 1u) * (4 * NQP);
         {
-          float w[NL];
+          float r[NL];
 #pragma unroll
-          for (int j = 0; j < NL; ++j) w[j] = s[j];
-          const float r = warp_col_reduce<NL, true>(w, lane);
-          if (lane < NL) rb[sq * NQP + col0 + reduced_col<NL>(lane)] = r;
+          for (int j = 0; j < NL; ++j) r[j] = warp_max_f32(s[j]);
+          if (lane == 0) {
+            float* rw = rb + sq * NQP + col0;
+            if constexpr (NL % 4 == 0) {
+#pragma unroll
+              for (int j = 0; j < NL; j += 4) *reinterpret_cast<float4*>(rw + j) = make_float4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < NL; ++j) rw[j] = r[j];
+            }
+          }
         }
         softmax_bar<SMT>();
         // column owner: new running max (moved only when the tile exceeds it by
@@ -913,15 +951,19 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
             const int cl = col0 + lane;
             const float tmax = fmaxf(fmaxf(rb[cl], rb[NQP + cl]), fmaxf(rb[2 * NQP + cl], rb[3 * NQP + cl]));
             const float mo = mst[cl];
+            float mn = mo;
             if (tmax != NEG_INF) {
               const float ts = tmax * c2;
               if (mo == NEG_INF) {
-                mst[cl] = ts;
+                mn = ts;
               } else if (ts > mo + 8.f) {
                 alpha = fast_exp2(mo - ts);
-                mst[cl] = ts;
+                mn = ts;
               }
             }
+            if (mn != mo) mst[cl] = mn;
+            // a column with no visible key yet has only -inf scores: exp2(-inf - 0) = 0
+            msf[cl] = mn == NEG_INF ? 0.f : mn;
             ast[cl] = alpha;
           }
           const bool any = __any_sync(0xffffffffu, alpha != 1.f);
@@ -945,7 +987,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
           tc_fence_after();
           float o[LW];
           tmem_ld<LW>(tq + (uint32_t)(C::O_COL + col0), o);
-          if constexpr (C::CH == 2) {
+          if constexpr (C::CHO == 2) {
             float o1[LW];
             tmem_ld<LW>(tq + (uint32_t)(C::O_COL + NQP + col0), o1);
             tc_wait_ld();
@@ -986,13 +1028,13 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         for (int c = 0; c < PCHL; ++c) {
           float mv[8];
           if constexpr (NL >= 8) {
-            const float4 m0 = reinterpret_cast<const float4*>(mst + col0)[2 * c];
-            const float4 m1 = reinterpret_cast<const float4*>(mst + col0)[2 * c + 1];
+            const float4 m0 = reinterpret_cast<const float4*>(msf + col0)[2 * c];
+            const float4 m1 = reinterpret_cast<const float4*>(msf + col0)[2 * c + 1];
             mv[0] = m0.x; mv[1] = m0.y; mv[2] = m0.z; mv[3] = m0.w;
             mv[4] = m1.x; mv[5] = m1.y; mv[6] = m1.z; mv[7] = m1.w;
           } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) mv[e] = e < NL ? mst[col0 + e] : 0.f;
+            for (int e = 0; e < 8; ++e) mv[e] = e < NL ? msf[col0 + e] : 0.f;
           }
           uint32_t w4[4];
 #pragma unroll
@@ -1002,7 +1044,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
             for (int e = 0; e < 2; ++e) {
               const int j = c * 8 + 2 * i + e;
               if (j < NL) {
-                pr2[e] = (s[j] == NEG_INF) ? 0.f : fast_exp2(fmaf(s[j], c2, -mv[2 * i + e]));
+                pr2[e] = fast_exp2(fmaf(s[j], c2, -mv[2 * i + e]));  // masked: exp2(-inf) = 0
                 lp[j] += pr2[e];
               } else {
                 pr2[e] = 0.f;
@@ -1024,7 +1066,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         tc_fence_after();
         float o[LW];
         tmem_ld<LW>(tq + (uint32_t)(C::O_COL + col0), o);
-        if constexpr (C::CH == 2) {
+        if constexpr (C::CHO == 2) {
           float o1[LW];
           tmem_ld<LW>(tq + (uint32_t)(C::O_COL + NQP + col0), o1);
           tc_wait_ld();
