@@ -84,7 +84,7 @@ CFG5S1 = dict(CFG5, B=128, R=1, kv_budget=1)
 # 2, scaled by the units processed (x4 to batch 32, x4 to batch 64, x32 to batch 64).
 NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
                      ("cfg2", "tc"): 538_103_040 + 3_908_608,
-                     ("cfg3", "tc"): (2_189_589_504 + 9_263_104) * 4,
+                     ("cfg3", "tc"): (2_158_536_192 + 9_401_600) * 4,
                      ("cfg4attn", "tc"): (866_308_864 + 4_023_040) * 4,
                      ("cfg5", "tc"): (4_314_130_176 + 6_834_176) * 32}
 
