@@ -83,7 +83,7 @@ CFG5S1 = dict(CFG5, B=128, R=1, kv_budget=1)
 # workload.  cfg3 was captured at batch 8, cfg4attn at batch 16 and cfg5 at batch
 # 2, scaled by the units processed (x4 to batch 32, x4 to batch 64, x32 to batch 64).
 NCU_TRAFFIC_BYTES = {("cfg2", "cuda_core"): 537_539_072 + 5_969_920,
-                     ("cfg2", "tc"): 538_103_040 + 3_908_608,
+                     ("cfg2", "tc"): 538_102_272 + 4_250_368,
                      ("cfg3", "tc"): (2_158_536_192 + 9_401_600) * 4,
                      ("cfg4attn", "tc"): (866_308_864 + 4_023_040) * 4,
                      ("cfg5", "tc"): (4_314_130_176 + 6_834_176) * 32}
