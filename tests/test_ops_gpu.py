@@ -13,6 +13,7 @@ import torch
 import golden_inputs as gi
 from oracle import attention as oattn
 from oracle.kv_cache import SlotCacheOracle
+from wavefront_decoding_b200 import ops as _ops  # noqa: F401  (registers torch.ops.wfd.*)
 
 pytestmark = pytest.mark.gpu
 
@@ -104,6 +105,52 @@ def test_wave_attn_op_vs_oracle_and_graph_capture(cuda_dev):
         assert _maxdiff(out, ref) < TOL_BF16
         assert np.array_equal(Kd.float().cpu().numpy(), o.K)
     assert np.array_equal(lens.cpu().numpy(), np.asarray(o.seqlen))
+    assert rt.read_device_error(cuda_dev) == 0
+    del graph
+
+
+def test_workspace_growth_keeps_captured_graph_valid(cuda_dev):
+    """A graph captured against the device workspace replays exactly after a later
+    call grows the workspace and the allocator has handed out memory of the old
+    buffer's size, filled with 0xFF: the replaced buffer stays allocated."""
+    from wavefront_decoding_b200 import runtime as rt
+    items, K, V, q, kn, vn = _wave_inputs(cuda_dev, seed=5)
+    Kd, Vd = K.to(cuda_dev).contiguous(), V.to(cuda_dev).contiguous()
+    qd, knd, vnd = q.to(cuda_dev), kn.to(cuda_dev), vn.to(cuda_dev)
+    it = torch.tensor(items, dtype=torch.int32, device=cuda_dev)
+    lens = torch.zeros(K.shape[:2], dtype=torch.int32, device=cuda_dev)
+    out = torch.empty_like(qd)
+    rt.reserve_workspace(cuda_dev, 64, 128)
+    rt.error_word(cuda_dev)
+
+    def body():
+        torch.ops.wfd.wave_attn_out(qd, knd, vnd, Kd, Vd, it, 7, lens, 0, None, -1, None, out)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        body()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    graph.replay()
+    torch.cuda.synchronize()
+    first = out.clone()
+    idx = cuda_dev.index if cuda_dev.index is not None else torch.cuda.current_device()
+    old_buf, old_items, _ = rt._ws[idx]
+    rt.reserve_workspace(cuda_dev, old_items * 4, 128)
+    assert rt._ws[idx][0].data_ptr() != old_buf.data_ptr()
+    n_old = old_buf.numel()
+    del old_buf
+    junk = [torch.full((n_old,), 0xFF, dtype=torch.uint8, device=cuda_dev) for _ in range(4)]
+    torch.cuda.synchronize()
+    for _ in range(3):
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, first)
+    assert all(int(j.min()) == 0xFF for j in junk)  # the replay wrote nothing outside its buffers
     assert rt.read_device_error(cuda_dev) == 0
     del graph
 

@@ -4,7 +4,9 @@ stream handles and tensor checks.
 PyTorch supplies device memory and the current CUDA stream; every compute step
 is a libwfd_b200 launch.  The workspace (segment table, prefix, arrival
 counters, split-K partials) is allocated once per device, zero-filled once, and
-grown only outside CUDA-graph capture (the kernels leave it zeroed again).
+grown only outside CUDA-graph capture (the kernels leave it zeroed again).  A grown
+workspace keeps the previous buffer allocated: graphs captured against it still
+point at it, and the allocator must not hand it to anything else.
 """
 from __future__ import annotations
 
@@ -16,6 +18,7 @@ from . import _abi
 
 _state_lock = threading.Lock()
 _ws: dict[int, tuple[torch.Tensor, int, int]] = {}   # device -> (buffer, max_items, head_dim)
+_ws_retired: dict[int, list[torch.Tensor]] = {}       # device -> buffers replaced by a larger one
 _err: dict[int, torch.Tensor] = {}
 
 
@@ -74,6 +77,8 @@ def workspace(device: torch.device, max_items: int, head_dim: int) -> tuple[torc
                 raise _abi.WfdError("wfd_workspace_bytes", -1, "could not size workspace")
             buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
             _abi.check(lib.wfd_workspace_init(buf.data_ptr(), nbytes, stream_ptr(device)), "wfd_workspace_init")
+        if cur is not None:
+            _ws_retired.setdefault(idx, []).append(cur[0])
         _ws[idx] = (buf, n_items, dh)
         return buf, nbytes
 
