@@ -1056,7 +1056,9 @@ def run_linear(args):
     RMSNorm + gate/up + SwiGLU, down + residual), --batch rows (default 8), eight
     layers with their own weights per step (453 MB, larger than L2); value = weight
     bytes streamed per second (HBM roofline).  The same chain on RMSNorm + cuBLAS +
-    the element-wise kernels is timed beside it (`unfused`)."""
+    the element-wise kernels is timed beside it (`unfused`), and the chain the bf16
+    engine runs, cuBLAS with the RMSNorm folded into the weights and its row scale
+    applied by the RoPE split / SwiGLU kernels (`folded`)."""
     import torch
 
     import __graft_entry__
@@ -1077,7 +1079,8 @@ def run_linear(args):
     W = [dict(qkv=w(d, 3 * H * Dh), o=w(H * Dh, d), gu=w(d, 2 * dff), dn=w(dff, d)) for _ in range(layers)]
     for blk in W:
         blk["qkv_f"] = fused.fold_norm(blk["qkv"], ones)
-        blk["gu_f"] = fused.interleave_gate_up(fused.fold_norm(blk["gu"], ones))
+        blk["gu_n"] = fused.fold_norm(blk["gu"], ones)
+        blk["gu_f"] = fused.interleave_gate_up(blk["gu_n"])
     S = 4096
     inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, Dh, 2, dtype=torch.float64) / Dh))
     ang = torch.outer(torch.arange(S, dtype=torch.float64), inv)
@@ -1100,6 +1103,13 @@ def run_linear(args):
             fused.rope_split(h @ blk["qkv"], cos, sin, H, H, Dh, pos=pos)
             x.addmm_(attn, blk["o"])
             a = fused.silu_mul(fused.rmsnorm(x, ones, cfg.norm_eps) @ blk["gu"])
+            x.addmm_(a, blk["dn"])
+
+    def folded_step():
+        for blk in W:
+            fused.rope_split(x @ blk["qkv_f"], cos, sin, H, H, Dh, pos=pos, norm_x=x, norm_eps=cfg.norm_eps)
+            x.addmm_(attn, blk["o"])
+            a = fused.silu_mul(x @ blk["gu_n"], norm_x=x, norm_eps=cfg.norm_eps)
             x.addmm_(a, blk["dn"])
 
     def timed(step):
@@ -1126,6 +1136,7 @@ def run_linear(args):
 
     ms, clocks = timed(fused_step)
     ms_unfused, _ = timed(unfused_step)
+    ms_folded, _ = timed(folded_step)
     rt.read_device_error(dev)
     wbytes = sum(t.numel() * 2 for blk in W for t in (blk["qkv"], blk["o"], blk["gu"], blk["dn"]))
     gbs = wbytes / (ms * 1e-3) / 1e9
@@ -1137,6 +1148,9 @@ def run_linear(args):
                                  "launches_per_layer": 4, "weights_mb": wbytes / 1e6},
                       "unfused": {"ms_per_step": ms_unfused, "launches_per_layer": 8,
                                   "what": "RMSNorm + cuBLAS GEMM + RoPE split / SwiGLU kernels"},
+                      "folded": {"ms_per_step": ms_folded, "launches_per_layer": 6,
+                                 "what": "cuBLAS GEMM on norm-folded weights + RoPE split / SwiGLU with the row scale "
+                                         "(the bf16 engine's chain)"},
                       "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                                    "peak_kind": peak_kind},
                       "gpu_launches": 4 * layers * args.steps, "clocks": clocks}), flush=True)
