@@ -262,11 +262,12 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
   return __all_sync(0xffffffffu, ok);
 }
 
-// Column reduction (max or sum) of the N values each of the 32 lanes holds:
-// butterfly reduce-scatter; lane l ends with column bitrev(l mod N) reduced
-// over all 32 lanes.  Destroys w.
-template <int N, bool IS_MAX>
-__device__ __forceinline__ float warp_col_reduce(float (&w)[N], int lane) {
+// Column sums of the N values each of the 32 lanes holds: butterfly
+// reduce-scatter; lane l ends with column bitrev(l mod N) summed over all 32
+// lanes, in an order fixed by the lane pattern.  Destroys w.  (Column maxima
+// take one redux.sync per column instead: warp_max_f32.)
+template <int N>
+__device__ __forceinline__ float warp_col_sum(float (&w)[N], int lane) {
 #pragma unroll
   for (int l = 0; (N >> l) > 1; ++l) {
     const int H = (N >> l) >> 1;
@@ -277,7 +278,7 @@ __device__ __forceinline__ float warp_col_reduce(float (&w)[N], int lane) {
         const float send = up ? w[i] : w[i + H];
         const float keep = up ? w[i + H] : w[i];
         const float got = __shfl_xor_sync(0xffffffffu, send, 1 << l);
-        w[i] = IS_MAX ? fmaxf(keep, got) : keep + got;
+        w[i] = keep + got;
       }
     }
   }
@@ -286,7 +287,7 @@ __device__ __forceinline__ float warp_col_reduce(float (&w)[N], int lane) {
 #pragma unroll
   for (int l = LOGN; l < 5; ++l) {
     const float got = __shfl_xor_sync(0xffffffffu, r, 1 << l);
-    r = IS_MAX ? fmaxf(r, got) : r + got;
+    r = r + got;
   }
   return r;
 }
@@ -1090,7 +1091,7 @@ __global__ void __launch_bounds__(tc_threads(NQP), 1)
         float w[NL];
 #pragma unroll
         for (int j = 0; j < NL; ++j) w[j] = lp[j];
-        const float r = warp_col_reduce<NL, false>(w, lane);
+        const float r = warp_col_sum<NL>(w, lane);
         if (lane < NL) lb[sq * NQP + col0 + reduced_col<NL>(lane)] = r;
       }
       softmax_bar<SMT>();
